@@ -1,0 +1,692 @@
+// gemv.cu -- batch-1 quantized GEMV, the decode projection (engine.zig:547-819 qkv/o/ffn/head).
+//
+// Design (HBM-bound; one pass over the quantized bytes, nothing else):
+//   * A warp owns 16 rows.  Each lane streams 128-bit, L1-bypassing loads of
+//     its rows' quant bytes from the planes layout and dequantises them in
+//     registers to fp16 -- for Q8_0/Q4_0/Q4_1/Q5_x/F16/BF16 exactly the
+//     reference's fp16 weight RN16(dequant_f32) (load_gguf.zig:371); for the
+//     K-quants as RN16 of the exact scaled quant, with Q4_K's minimum term
+//     subtracted in fp32 after the MMA (see TQ4K).
+//   * The fp16 weights are the A operand of mma.sync m16n8k16 (fp32
+//     accumulate).  B holds the activation split as x = hi + lo (two fp16
+//     columns, ~22 bits), so the tensor core does the dot products and the
+//     CUDA cores only unpack bits: 1-2 ALU ops per weight.
+//   * Within each group of 4 columns a lane feeds the pairs (0,2) and (1,3),
+//     which is what PRMT/LOP3 produce from packed bytes without shuffles; the
+//     activation is stored in the same permuted order ("xq", common.cuh).
+//   * 4 warps per CTA split the CTA's K range; split-K across CTAs (ksplit)
+//     reduces deterministically through a workspace: the last CTA of a tile
+//     (atomic ticket) sums the partials in a fixed order and resets the ticket.
+#include "common.cuh"
+
+namespace cuq {
+
+namespace {
+
+struct W {
+    const uint8_t *q, *q2, *s, *s2;  // plane pointers (see common.cuh)
+    uint32_t rows, cols;
+};
+
+W wview(const Planes &p) {
+    W w;
+    w.q = p.base + p.off_q;
+    w.q2 = p.off_q2 == SIZE_MAX ? nullptr : p.base + p.off_q2;
+    w.s = p.off_s == SIZE_MAX ? nullptr : p.base + p.off_s;
+    w.s2 = p.off_s2 == SIZE_MAX ? nullptr : p.base + p.off_s2;
+    w.rows = p.rows;
+    w.cols = p.cols;
+    return w;
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// half2 with 0x6400 exponent over the low bits of both 16-bit lanes: 1024 + field.
+__device__ __forceinline__ uint32_t magic(uint32_t v, uint32_t mask) { return (v & mask) | 0x64006400u; }
+
+// ------------------------------------------------------------- per type ---
+// Each type provides SPAN (columns per lane-row per iteration x 4 lanes),
+// KSTEPS (MMA k-steps per iteration), load() of one iteration's bytes for rows
+// r0 and r0+8, frag() giving the A registers of k-step s, and koff() giving
+// the first column of the 4-column group the lane feeds at k-step s.
+
+struct TQ8_0 {
+    static constexpr int SPAN = 64, KSTEPS = 4;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 q[2]; __half2 d[2]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        uint32_t k = it * SPAN + tig * 16;
+        if (k < w.cols) {
+            R.q[0] = ldg_stream(w.q + (size_t)r0 * w.cols + k);
+            R.q[1] = ldg_stream(w.q + (size_t)(r0 + 8) * w.cols + k);
+            const __half *d = reinterpret_cast<const __half *>(w.s) + (size_t)(k >> 5) * w.rows;
+            R.d[0] = __half2half2(d[r0]);
+            R.d[1] = __half2half2(d[r0 + 8]);
+        } else {
+            R.q[0] = R.q[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // q = 0
+            R.d[0] = R.d[1] = __float2half2_rn(0.f);
+        }
+    }
+    __device__ static uint32_t word(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+        const __half2 off = __float2half2_rn(1152.f);
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t u = word(R.q[rr], s) ^ 0x80808080u;  // int8 q -> q + 128 (unsigned byte)
+            __half2 p02 = u2h(__byte_perm(u, 0x64646464u, 0x4240u));  // 1152 + q for bytes 0, 2
+            __half2 p13 = u2h(__byte_perm(u, 0x64646464u, 0x4341u));
+            a[rr] = h2u(__hmul2(__hsub2(p02, off), R.d[rr]));        // RN16(q * d)
+            a[rr + 2] = h2u(__hmul2(__hsub2(p13, off), R.d[rr]));
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 16 + s * 4; }
+};
+
+// Legacy 32-blocks with 4-bit nibbles: one block per lane per iteration.
+template <int T>
+struct TQ4L {
+    static constexpr int SPAN = 128, KSTEPS = 8;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 q[2]; __half2 d[2], m[2]; uint32_t qh[2]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        uint32_t k = it * SPAN + tig * 32;
+        if (k < w.cols) {
+            uint32_t b = k >> 5;
+            R.q[0] = ldg_stream(w.q + (size_t)r0 * (w.cols / 2) + b * 16);
+            R.q[1] = ldg_stream(w.q + (size_t)(r0 + 8) * (w.cols / 2) + b * 16);
+            if (T == CUQ_Q4_0 || T == CUQ_Q5_0) {
+                const __half *d = reinterpret_cast<const __half *>(w.s) + (size_t)b * w.rows;
+                R.d[0] = __half2half2(d[r0]);
+                R.d[1] = __half2half2(d[r0 + 8]);
+                R.m[0] = R.m[1] = __float2half2_rn(0.f);
+            } else {
+                const __half2 *dm = reinterpret_cast<const __half2 *>(w.s) + (size_t)b * w.rows;
+                __half2 x0 = dm[r0], x1 = dm[r0 + 8];
+                R.d[0] = __low2half2(x0);
+                R.m[0] = __high2half2(x0);
+                R.d[1] = __low2half2(x1);
+                R.m[1] = __high2half2(x1);
+            }
+            if (T == CUQ_Q5_0 || T == CUQ_Q5_1) {
+                const uint32_t *qh = reinterpret_cast<const uint32_t *>(w.q2) + (size_t)b * w.rows;
+                R.qh[0] = qh[r0];
+                R.qh[1] = qh[r0 + 8];
+            } else {
+                R.qh[0] = R.qh[1] = 0;
+            }
+        } else {
+            R.q[0] = R.q[1] = make_uint4(0, 0, 0, 0);
+            R.d[0] = R.d[1] = R.m[0] = R.m[1] = __float2half2_rn(0.f);
+            R.qh[0] = R.qh[1] = 0;
+        }
+    }
+    // k-step s: word i = s >> 1 of the block, low nibbles (s even) or high (s odd).
+    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+        const int i = s >> 1;
+        const bool hi = s & 1;
+        constexpr bool five = (T == CUQ_Q5_0 || T == CUQ_Q5_1);
+        constexpr bool has_min = (T == CUQ_Q4_1 || T == CUQ_Q5_1);
+        // offset removed before scaling: 1024 + (8 | 16 for the signed types)
+        const float offv = 1024.f + (T == CUQ_Q4_0 ? 8.f : T == CUQ_Q5_0 ? 16.f : 0.f);
+        const __half2 off = __float2half2_rn(offv);
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t u = TQ8_0::word(R.q[rr], i);
+            uint32_t v02 = hi ? (u >> 4) : u, v13 = hi ? (u >> 12) : (u >> 8);
+            uint32_t p02 = magic(v02, 0x000F000Fu), p13 = magic(v13, 0x000F000Fu);
+            if (five) {
+                // 5th bits: weight j (< 16) uses qh bit j, weight 16+j uses bit 16+j.
+                uint32_t t = R.qh[rr] >> (4 * i);
+                if (!hi) {
+                    p02 |= ((t << 4) & 0x10u) | ((t << 18) & 0x100000u);
+                    p13 |= ((t << 3) & 0x10u) | ((t << 17) & 0x100000u);
+                } else {
+                    p02 |= ((t >> 12) & 0x10u) | ((t << 2) & 0x100000u);
+                    p13 |= ((t >> 13) & 0x10u) | ((t << 1) & 0x100000u);
+                }
+            }
+            __half2 x02 = __hsub2(u2h(p02), off), x13 = __hsub2(u2h(p13), off);
+            if (has_min) {
+                a[rr] = h2u(__hfma2(x02, R.d[rr], R.m[rr]));          // RN16(q*d + m)
+                a[rr + 2] = h2u(__hfma2(x13, R.d[rr], R.m[rr]));
+            } else {
+                a[rr] = h2u(__hmul2(x02, R.d[rr]));                    // RN16((q - 8|16) * d)
+                a[rr + 2] = h2u(__hmul2(x13, R.d[rr]));
+            }
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 32 + (s & 1) * 16 + (s >> 1) * 4; }
+};
+
+__device__ __forceinline__ void scale_min_k4(int j, const uint8_t *q, int &d, int &m) {
+    if (j < 4) {
+        d = q[j] & 63;
+        m = q[j + 4] & 63;
+    } else {
+        d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+    }
+}
+
+// Q4_K: one 256-superblock per iteration; lane tig owns the 32-byte group tig
+// (sub-blocks 2tig in the low nibbles and 2tig+1 in the high nibbles).
+// The reference weight is d1*q - m1 with d1 = d*sc, m1 = dmin*m, both exact in
+// fp32 (gguf.zig:975-992).  fma(1024+q, sc, -1024*sc) = q*sc is an integer
+// <= 945, exact in fp16; then one fma(q*sc, d, -m1h) with m1h = RN16(m1) rounds
+// d1*q - m1h once, at the weight's own magnitude (as the reference's fp16 weight
+// is rounded).  The small remainder (m1 - m1h) * sum(x) over the sub-block is
+// subtracted after the MMA in fp32, so no scale error is shared by a sub-block.
+struct TQ4K {
+    static constexpr int SPAN = 256, KSTEPS = 16;
+    static constexpr bool HAS_CORR = true;
+    struct Raw { uint4 q[2][2]; __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t r = r0 + rr * 8;
+            const uint8_t *qp = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + tig * 32;
+            R.q[rr][0] = ldg_stream(qp);
+            R.q[rr][1] = ldg_stream(qp + 16);
+            uint4 meta = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
+            const uint8_t *mb = reinterpret_cast<const uint8_t *>(&meta);
+            R.d[rr] = __half2half2(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
+            float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
+#pragma unroll
+            for (int part = 0; part < 2; part++) {
+                int sc, mm;
+                scale_min_k4(2 * tig + part, mb + 4, sc, mm);
+                R.sc[rr][part] = __float2half2_rn((float)sc);
+                R.csc[rr][part] = __float2half2_rn(-1024.f * (float)sc);  // exact: |1024*63| < 65504
+                float m1 = dmin * (float)mm;                                // exact in fp32
+                __half m1h = __float2half_rn(m1);
+                R.nm1[rr][part] = __half2half2(__hneg(m1h));
+                R.m1[rr][part] = m1 - __half2float(m1h);                    // remainder, exact
+            }
+        }
+    }
+    // k-step s: word i = s & 7 of the group, part = s >> 3 (low nibbles, then high).
+    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+        const int i = s & 7, part = s >> 3;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t u = TQ8_0::word(R.q[rr][i >> 2], i & 3);
+            uint32_t v02 = part ? (u >> 4) : u, v13 = part ? (u >> 12) : (u >> 8);
+            __half2 q02 = __hfma2(u2h(magic(v02, 0x000F000Fu)), R.sc[rr][part], R.csc[rr][part]);  // q*sc
+            __half2 q13 = __hfma2(u2h(magic(v13, 0x000F000Fu)), R.sc[rr][part], R.csc[rr][part]);
+            a[rr] = h2u(__hfma2(q02, R.d[rr], R.nm1[rr][part]));  // RN16(d1*q - m1h)
+            a[rr + 2] = h2u(__hfma2(q13, R.d[rr], R.nm1[rr][part]));
+        }
+    }
+    // sum over this lane's two sub-blocks of (m1 - m1h) * sum(x), for rows r0 and r0+8
+    __device__ static void correct(const Raw &R, const float *xsum, int it, int tig, float &c0, float &c1) {
+        float4 X = *reinterpret_cast<const float4 *>(xsum + 16 * it + 4 * tig);
+        float xl = X.x + X.y, xh = X.z + X.w;
+        c0 += R.m1[0][0] * xl + R.m1[0][1] * xh;
+        c1 += R.m1[1][0] * xl + R.m1[1][1] * xh;
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 64 + (s >> 3) * 32 + (s & 7) * 4; }
+};
+
+// Q6_K: one superblock per iteration; lane tig owns half h = tig/2 and the
+// 16 l-values starting at 16*(tig&1): ql bytes [64h+lh, +16) and [64h+32+lh, +16),
+// qh bytes [32h+lh, +16); it produces 64 weights per row.
+// The sub-block scale d*sc is exact in fp32 (11 x 8 bits); it is carried as
+// an fp16 pair s_hi + s_lo so each weight RN16((q-32) * d * sc) is rounded
+// once, like the reference's fp16 weight (gguf.zig:1036-1059, load_gguf.zig:371).
+struct TQ6K {
+    static constexpr int SPAN = 256, KSTEPS = 16;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 a[2], b[2], h[2]; __half2 s[2][4], sl[2][4]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        const int hh = tig >> 1, lh = (tig & 1) * 16;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t r = r0 + rr * 8;
+            const uint8_t *ql = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + hh * 64 + lh;
+            R.a[rr] = ldg_stream(ql);
+            R.b[rr] = ldg_stream(ql + 32);
+            R.h[rr] = ldg_stream(w.q2 + (size_t)r * (w.cols / 4) + (size_t)it * 64 + hh * 32 + lh);
+            uint4 scv = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
+            const int8_t *sc = reinterpret_cast<const int8_t *>(&scv);
+            float d = __half2float(reinterpret_cast<const __half *>(w.s2)[(size_t)it * w.rows + r]);
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                float scale = d * (float)sc[hh * 8 + 2 * t + (tig & 1)];  // exact
+                __half hi = __float2half_rn(scale);
+                R.s[rr][t] = __half2half2(hi);
+                R.sl[rr][t] = __float2half2_rn(scale - __half2float(hi));
+            }
+        }
+    }
+    // k-step s: t = s >> 2 (which quarter), word i = s & 3.
+    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+        const int t = s >> 2, i = s & 3;
+        const __half2 off = __float2half2_rn(1056.f);  // 1024 + 32
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t A = TQ8_0::word(R.a[rr], i), B = TQ8_0::word(R.b[rr], i), Q = TQ8_0::word(R.h[rr], i);
+            uint32_t p02, p13;
+            switch (t) {
+            case 0:
+                p02 = (A & 0x000F000Fu) | ((Q << 4) & 0x00300030u);
+                p13 = ((A >> 8) & 0x000F000Fu) | ((Q >> 4) & 0x00300030u);
+                break;
+            case 1:
+                p02 = (B & 0x000F000Fu) | ((Q << 2) & 0x00300030u);
+                p13 = ((B >> 8) & 0x000F000Fu) | ((Q >> 6) & 0x00300030u);
+                break;
+            case 2:
+                p02 = ((A >> 4) & 0x000F000Fu) | (Q & 0x00300030u);
+                p13 = ((A >> 12) & 0x000F000Fu) | ((Q >> 8) & 0x00300030u);
+                break;
+            default:
+                p02 = ((B >> 4) & 0x000F000Fu) | ((Q >> 2) & 0x00300030u);
+                p13 = ((B >> 12) & 0x000F000Fu) | ((Q >> 10) & 0x00300030u);
+                break;
+            }
+            __half2 x02 = __hsub2(u2h(p02 | 0x64006400u), off), x13 = __hsub2(u2h(p13 | 0x64006400u), off);
+            a[rr] = h2u(__hfma2(x02, R.s[rr][t], __hmul2(x02, R.sl[rr][t])));  // ~RN16((q-32) * scale)
+            a[rr + 2] = h2u(__hfma2(x13, R.s[rr][t], __hmul2(x13, R.sl[rr][t])));
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) {
+        return it * SPAN + (tig >> 1) * 128 + (s >> 2) * 32 + (tig & 1) * 16 + (s & 3) * 4;
+    }
+};
+
+// F16 / BF16: 16 weights per lane-row per iteration.
+template <int T>
+struct T16 {
+    static constexpr int SPAN = 64, KSTEPS = 4;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 q[2][2]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        uint32_t k = it * SPAN + tig * 16;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            if (k < w.cols) {
+                const uint8_t *p = w.q + ((size_t)(r0 + rr * 8) * w.cols + k) * 2;
+                R.q[rr][0] = ldg_stream(p);
+                R.q[rr][1] = ldg_stream(p + 16);
+            } else {
+                R.q[rr][0] = R.q[rr][1] = make_uint4(0, 0, 0, 0);
+            }
+        }
+    }
+    __device__ static uint32_t cvt(uint32_t lo16src, uint32_t hi16src) {
+        // two bf16 (low halves of the sources) -> fp16x2, RN (Gguf.readF16 of a bf16 tensor)
+        float a = __uint_as_float(lo16src << 16), b = __uint_as_float(hi16src << 16);
+        return h2u(__floats2half2_rn(a, b));
+    }
+    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const uint4 &v = R.q[rr][s >> 1];
+            uint32_t w0 = (s & 1) ? v.z : v.x, w1 = (s & 1) ? v.w : v.y;  // (e0,e1), (e2,e3)
+            if (T == CUQ_F16) {
+                a[rr] = __byte_perm(w0, w1, 0x5410u);      // (e0, e2)
+                a[rr + 2] = __byte_perm(w0, w1, 0x7632u);  // (e1, e3)
+            } else {
+                a[rr] = cvt(w0, w1);
+                a[rr + 2] = cvt(w0 >> 16, w1 >> 16);
+            }
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 16 + s * 4; }
+};
+
+// ------------------------------------------------------------------ kernel -
+
+struct KArgs {
+    W w, w2;
+    const __half *xq;
+    const float *xsum;  // per-16-column sums of x (xq_sums)
+    uint32_t kpad;
+    float *y;
+    const float *bias;
+    __half *xq_out;
+    uint32_t kpad_out;
+    unsigned long long *argmax64;
+    float *ws;
+    unsigned int *counters;
+    int ksplit;
+};
+
+__device__ __forceinline__ unsigned long long pack_argmax(float v, uint32_t idx) {
+    uint32_t u = __float_as_uint(v);
+    uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+__device__ __forceinline__ uint32_t xq_pos(uint32_t i) { return (i & ~3u) | ((i & 1u) << 1) | ((i >> 1) & 1u); }
+
+template <class TT, int EPI>
+__global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
+    constexpr bool DUAL = (EPI == EPI_SILU_XQ);
+    __shared__ float red[4][DUAL ? 32 : 16];
+    __shared__ int is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const uint32_t tile = blockIdx.x, row0 = tile * 16;
+    const uint32_t r0 = row0 + g;
+    const int ni = (int)((p.w.cols + TT::SPAN - 1) / TT::SPAN);
+    const int per = (ni + p.ksplit - 1) / p.ksplit;
+    const int it0 = blockIdx.y * per, it1 = min(ni, it0 + per);
+
+    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);
+    const bool bl = g < 2;
+
+    float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+    float k0 = 0.f, k1 = 0.f, k20 = 0.f, k21 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
+    for (int it = it0 + warp; it < it1; it += 4) {
+        typename TT::Raw R, R2;
+        TT::load(R, p.w, r0, it, tig);
+        if (DUAL) TT::load(R2, p.w2, r0, it, tig);
+#pragma unroll
+        for (int s = 0; s < TT::KSTEPS; s++) {
+            uint2 b = make_uint2(0u, 0u);
+            if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
+            uint32_t a[4];
+            TT::frag(R, s, a);
+            mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
+            if (DUAL) {
+                TT::frag(R2, s, a);
+                mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
+            }
+        }
+        if (TT::HAS_CORR) {
+            TT::correct(R, p.xsum, it, tig, k0, k1);
+            if (DUAL) TT::correct(R2, p.xsum, it, tig, k20, k21);
+        }
+    }
+    if (TT::HAS_CORR) {  // the four lanes of a row hold different sub-blocks: sum them
+#pragma unroll
+        for (int sh = 1; sh <= 2; sh <<= 1) {
+            k0 += __shfl_xor_sync(0xffffffffu, k0, sh);
+            k1 += __shfl_xor_sync(0xffffffffu, k1, sh);
+            k20 += __shfl_xor_sync(0xffffffffu, k20, sh);
+            k21 += __shfl_xor_sync(0xffffffffu, k21, sh);
+        }
+    }
+    if (tig == 0) {
+        red[warp][g] = (c[0] + c[1]) - k0;
+        red[warp][g + 8] = (c[2] + c[3]) - k1;
+        if (DUAL) {
+            red[warp][16 + g] = (c2[0] + c2[1]) - k20;
+            red[warp][16 + g + 8] = (c2[2] + c2[3]) - k21;
+        }
+    }
+    __syncthreads();
+    constexpr int NV = DUAL ? 32 : 16;
+    const int t = threadIdx.x;
+    float v = 0.f;
+    if (t < NV) v = ((red[0][t] + red[1][t]) + red[2][t]) + red[3][t];
+    const uint32_t rows = p.w.rows;
+    if (p.ksplit > 1) {
+        // split-K: publish the partial, the last CTA of this tile reduces in order.
+        if (t < NV) {
+            uint32_t row = row0 + (t & 15);
+            p.ws[((size_t)blockIdx.y * (DUAL ? 2 : 1) + (t >> 4)) * rows + row] = v;
+        }
+        __threadfence();
+        __syncthreads();
+        if (t == 0) {
+            unsigned int prev = atomicAdd(&p.counters[tile], 1u);
+            is_last = (prev == (unsigned)p.ksplit - 1u);
+        }
+        __syncthreads();
+        if (!is_last) return;
+        __threadfence();
+        if (t < NV) {
+            uint32_t row = row0 + (t & 15);
+            float acc = 0.f;
+            for (int ky = 0; ky < p.ksplit; ky++)
+                acc += __ldcg(&p.ws[((size_t)ky * (DUAL ? 2 : 1) + (t >> 4)) * rows + row]);
+            v = acc;
+        }
+        if (t == 0) p.counters[tile] = 0u;
+    }
+    if (EPI == EPI_SILU_XQ) {
+        __shared__ float gu[32];
+        if (t < 32) gu[t] = v;
+        __syncthreads();
+        __shared__ float act16[16];
+        if (t < 16) {
+            uint32_t row = row0 + t;
+            float gt = gu[t], ut = gu[16 + t];
+            // cpu.siluMul (cpu.zig:65-70): g * (1 / (1 + exp(-g))) * u
+            float sg = 1.0f / (1.0f + expf(-gt));
+            float act = (gt * sg) * ut;
+            if (p.y) p.y[row] = act;
+            __half hi = __float2half_rn(act);
+            __half lo = __float2half_rn(act - __half2float(hi));
+            uint32_t pos = xq_pos(row);
+            p.xq_out[pos] = hi;
+            p.xq_out[p.kpad_out + pos] = lo;
+            act16[t] = act;
+        }
+        __syncthreads();
+        if (t == 0) {  // this tile's 16 rows are exactly one xq sum group
+            float acc = 0.f;
+            for (int j = 0; j < 16; j++) acc += act16[j];
+            xq_sums(p.xq_out, p.kpad_out)[tile] = acc;
+        }
+        return;
+    }
+    if (t < 16) {
+        uint32_t row = row0 + t;
+        if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
+            if (p.bias) v = v + p.bias[row];
+            p.y[row] = v;
+        } else if (EPI == EPI_ADD) {
+            if (p.bias) v = v + p.bias[row];
+            p.y[row] = p.y[row] + v;
+        }
+    }
+    if (EPI == EPI_ARGMAX) {
+        // first index of the maximum within the tile (cpu.zig:477-483), then a
+        // packed 64-bit max across tiles: larger value wins, then smaller index.
+        if (t < 32) {
+            unsigned long long key = t < 16 ? pack_argmax(v, row0 + t) : 0ull;
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                key = other > key ? other : key;
+            }
+            if (t == 0) atomicMax(p.argmax64, key);
+        }
+    }
+}
+
+template <class TT>
+int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
+    KArgs k;
+    k.w = wview(*a.w);
+    if (a.w2) k.w2 = wview(*a.w2);
+    k.xq = a.xq;
+    k.kpad = xq_pad(a.w->cols);
+    k.xsum = xq_sums(a.xq, k.kpad);
+    k.y = a.y;
+    k.bias = a.bias;
+    k.xq_out = a.xq_out;
+    k.kpad_out = xq_pad(a.w->rows);
+    k.argmax64 = a.argmax64;
+    k.ws = a.ws;
+    k.counters = a.counters;
+    k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
+    dim3 grid(a.w->rows / 16, k.ksplit);
+    switch (epi) {
+    case EPI_STORE: gemv_kernel<TT, EPI_STORE><<<grid, 128, 0, s>>>(k); break;
+    case EPI_ADD: gemv_kernel<TT, EPI_ADD><<<grid, 128, 0, s>>>(k); break;
+    case EPI_SILU_XQ: gemv_kernel<TT, EPI_SILU_XQ><<<grid, 128, 0, s>>>(k); break;
+    case EPI_ARGMAX: gemv_kernel<TT, EPI_ARGMAX><<<grid, 128, 0, s>>>(k); break;
+    default: set_error("bad epilogue %d", epi); return CUQ_EINVAL;
+    }
+    CUQ_CUDA_TRY(cudaGetLastError());
+    return CUQ_OK;
+}
+
+// -------------------------------------------------------------- xq makers --
+
+__global__ void to_xq_kernel(const float *__restrict__ x, uint32_t n, uint32_t x_stride, __half *__restrict__ xq,
+                             uint32_t kpad, size_t vec_stride) {
+    const uint32_t v = blockIdx.y;
+    const float *xv = x + (size_t)v * x_stride;
+    __half *o = xq + (size_t)v * vec_stride;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < kpad; i += gridDim.x * blockDim.x) {
+        float f = i < n ? xv[i] : 0.f;
+        __half hi = __float2half_rn(f);
+        __half lo = __float2half_rn(f - __half2float(hi));
+        uint32_t pos = xq_pos(i);
+        o[pos] = hi;
+        o[kpad + pos] = lo;
+    }
+    float *sums = xq_sums(o, kpad);
+    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < kpad / 16; u += gridDim.x * blockDim.x) {
+        float acc = 0.f;
+        for (uint32_t j = 16 * u; j < 16 * u + 16; j++) acc += j < n ? xv[j] : 0.f;
+        sums[u] = acc;
+    }
+}
+
+// One CTA per row: cpu.rmsnorm (cpu.zig:11-18), then the xq split.
+__global__ void rmsnorm_xq_kernel(const float *__restrict__ x, const float *__restrict__ w, uint32_t n, float eps,
+                                  __half *__restrict__ xq, uint32_t kpad, size_t vec_stride, float *h_out) {
+    const float *xr = x + (size_t)blockIdx.x * n;
+    __half *o = xq + (size_t)blockIdx.x * vec_stride;
+    __shared__ float part[32];
+    float acc = 0.f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = xr[i];
+        acc += v * v;
+    }
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float s = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+        if (threadIdx.x == 0) part[0] = s;
+    }
+    __syncthreads();
+    const float mean = part[0] / (float)n;
+    const float inv = 1.0f / sqrtf(mean + eps);
+    for (uint32_t i = threadIdx.x; i < kpad; i += blockDim.x) {
+        float f = 0.f;
+        if (i < n) {
+            f = (xr[i] * inv) * w[i];
+            if (h_out) h_out[(size_t)blockIdx.x * n + i] = f;
+        }
+        __half hi = __float2half_rn(f);
+        __half lo = __float2half_rn(f - __half2float(hi));
+        uint32_t pos = xq_pos(i);
+        o[pos] = hi;
+        o[kpad + pos] = lo;
+    }
+    float *sums = xq_sums(o, kpad);
+    for (uint32_t u = threadIdx.x; u < kpad / 16; u += blockDim.x) {
+        float acc = 0.f;
+        for (uint32_t j = 16 * u; j < 16 * u + 16 && j < n; j++) acc += (xr[j] * inv) * w[j];
+        sums[u] = acc;
+    }
+}
+
+}  // namespace
+
+int launch_to_xq(const float *x, uint32_t n, uint32_t n_vec, uint32_t x_stride, __half *xq, cudaStream_t s) {
+    uint32_t kpad = xq_pad(n);
+    dim3 grid((kpad + 255) / 256, n_vec);
+    to_xq_kernel<<<grid, 256, 0, s>>>(x, n, x_stride, xq, kpad, xq_halves(n));
+    CUQ_CUDA_TRY(cudaGetLastError());
+    return CUQ_OK;
+}
+
+int launch_rmsnorm_xq(const float *x, const float *w, uint32_t n, uint32_t n_rows, float eps, __half *xq,
+                      float *h_out, cudaStream_t s) {
+    rmsnorm_xq_kernel<<<n_rows, 256, 0, s>>>(x, w, n, eps, xq, xq_pad(n), xq_halves(n), h_out);
+    CUQ_CUDA_TRY(cudaGetLastError());
+    return CUQ_OK;
+}
+
+int gemv_pick_ksplit(const Planes &w, int sm_count) {
+    int span;
+    switch (w.type) {
+    case CUQ_Q8_0: case CUQ_F16: case CUQ_BF16: span = 64; break;
+    case CUQ_Q4_K: case CUQ_Q6_K: span = 256; break;
+    default: span = 128; break;
+    }
+    int ni = (int)((w.cols + span - 1) / span);
+    int tiles = (int)(w.rows / 16);
+    int want = (sm_count * 8 + tiles - 1) / tiles;  // ~8 CTAs of 4 warps per SM
+    int maxk = ni / 8;                              // keep >= 2 iterations per warp
+    if (want > maxk) want = maxk;
+    if (want > 16) want = 16;
+    if (want < 1) want = 1;
+    return want;
+}
+
+int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
+    const Planes &w = *a.w;
+    if (!gemv_supported(w.type)) {
+        set_error("UnsupportedType: no GEMV for ggml type %d", w.type);
+        return CUQ_EUNSUPPORTED;
+    }
+    if (w.rows % 16 || w.rows == 0) {
+        set_error("gemv: rows (%u) must be a positive multiple of 16", w.rows);
+        return CUQ_EINVAL;
+    }
+    if ((w.type == CUQ_F16 || w.type == CUQ_BF16) && w.cols % 16) {
+        set_error("gemv: 16-bit weights need cols %% 16 == 0 (cols %u)", w.cols);
+        return CUQ_EINVAL;
+    }
+    if (epi == EPI_SILU_XQ && (!a.w2 || a.w2->type != w.type || a.w2->rows != w.rows || a.w2->cols != w.cols)) {
+        set_error("gemv: gate/up must share type and shape");
+        return CUQ_EINVAL;
+    }
+    if (a.ksplit > 1 && (!a.ws || !a.counters)) {
+        set_error("gemv: split-K needs a workspace");
+        return CUQ_EINVAL;
+    }
+    switch (w.type) {
+    case CUQ_Q8_0: return launch_t<TQ8_0>(a, epi, s);
+    case CUQ_Q4_0: return launch_t<TQ4L<CUQ_Q4_0>>(a, epi, s);
+    case CUQ_Q4_1: return launch_t<TQ4L<CUQ_Q4_1>>(a, epi, s);
+    case CUQ_Q5_0: return launch_t<TQ4L<CUQ_Q5_0>>(a, epi, s);
+    case CUQ_Q5_1: return launch_t<TQ4L<CUQ_Q5_1>>(a, epi, s);
+    case CUQ_Q4_K: return launch_t<TQ4K>(a, epi, s);
+    case CUQ_Q6_K: return launch_t<TQ6K>(a, epi, s);
+    case CUQ_F16: return launch_t<T16<CUQ_F16>>(a, epi, s);
+    case CUQ_BF16: return launch_t<T16<CUQ_BF16>>(a, epi, s);
+    }
+    return CUQ_EUNSUPPORTED;
+}
+
+}  // namespace cuq

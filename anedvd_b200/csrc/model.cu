@@ -1,0 +1,685 @@
+// model.cu -- the engine: Engine.init / forward / prefill / reset (src/engine.zig)
+// and Session.generate's greedy loop (src/generate.zig:166-250), device-resident.
+//
+// A decode step is one fixed launch sequence (captured once in a CUDA graph):
+//   embed row -> per layer [rmsnorm->xq, qkv GEMV(+bias), RoPE + fp16 KV write,
+//   split attention + combine->xq, o GEMV (+= residual), rmsnorm->xq,
+//   gate|up GEMV with SiLU*mul epilogue->xq, down GEMV (+= residual)] ->
+//   final rmsnorm->xq, lm_head GEMV with fused argmax -> finish kernel.
+// The step reads its token and position from device memory and the finish
+// kernel writes the next ones, so consecutive steps (a prompt fed token by
+// token, then greedy decoding) replay the graph with no host round-trip.
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "model.h"
+#include "ops.cuh"
+
+using namespace cuq;
+
+namespace cuq {
+int sm_count_current();
+}
+
+namespace {
+
+enum { R_Q = 0, R_K, R_V, R_O, R_GATE, R_UP, R_DOWN };
+
+uint32_t q_dim(const cuq_config &c) { return c.heads * c.head_dim; }
+uint32_t kv_dim(const cuq_config &c) { return c.kv_heads * c.head_dim; }
+
+void free_pending(PendingTensor &t) {
+    if (t.raw) cudaFree(t.raw);
+    t = PendingTensor();
+}
+
+void free_planes(Planes &p) {
+    if (p.base) cudaFree(p.base);
+    p.base = nullptr;
+}
+
+// Repack one or more same-typed pending tensors (concatenated by rows) into planes.
+int build_proj(Proj &out, std::vector<PendingTensor *> parts, cudaStream_t s) {
+    int type = parts[0]->type;
+    uint32_t cols = parts[0]->cols, rows = 0;
+    size_t nbytes = 0;
+    for (auto *t : parts) {
+        rows += t->rows;
+        nbytes += t->nbytes;
+    }
+    out.p = Planes();
+    out.p.type = type;
+    out.p.rows = rows;
+    out.p.cols = cols;
+    if (!plan_planes(out.p)) {
+        set_error("UnsupportedType: ggml type %d has no GEMV here", type);
+        return CUQ_EUNSUPPORTED;
+    }
+    CUQ_CUDA_TRY(cudaMalloc(&out.p.base, out.p.nbytes));
+    uint8_t *cat = parts[0]->raw;
+    bool own = false;
+    if (parts.size() > 1) {
+        CUQ_CUDA_TRY(cudaMalloc(&cat, nbytes));
+        own = true;
+        size_t off = 0;
+        for (auto *t : parts) {
+            CUQ_CUDA_TRY(cudaMemcpyAsync(cat + off, t->raw, t->nbytes, cudaMemcpyDeviceToDevice, s));
+            off += t->nbytes;
+        }
+    }
+    int rc = launch_repack(cat, out.p, s);
+    cudaStreamSynchronize(s);
+    if (own) cudaFree(cat);
+    return rc;
+}
+
+__global__ void finish_step_kernel(StepState *st, const uint32_t *forced, uint32_t *out_tokens) {
+    unsigned long long a = st->argmax64;
+    uint32_t idx = 0xFFFFFFFFu - (uint32_t)(a & 0xFFFFFFFFull);
+    st->argmax64 = 0ull;
+    int s = st->step;
+    out_tokens[s] = idx;
+    st->step = s + 1;
+    st->pos = st->pos + 1;
+    st->token = (s + 1 < st->n_forced) ? (int)forced[s + 1] : (int)idx;
+}
+
+}  // namespace
+
+static int enqueue_step(cuq_model *m) {
+    const cuq_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    const int *pos_ptr = &m->state->pos;
+    const uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    int rc;
+    uint64_t nk = 0;  // kernel launches in the step (each launcher below enqueues one, attention two)
+#define TRY(x)                       \
+    do {                             \
+        rc = (x);                    \
+        if (rc != CUQ_OK) return rc; \
+        nk++;                        \
+    } while (0)
+    TRY(launch_embed_row(m->embed.p, &m->state->token, m->x, s));
+    for (uint32_t l = 0; l < c.layers; l++) {
+        Layer &L = m->layers[l];
+        // attention half (main.zig:434-485 / engine.zig:569-620)
+        TRY(launch_rmsnorm_xq(m->x, L.attn_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, s));
+        for (auto &seg : L.qkv) {
+            GemvArgs a;
+            a.w = &seg.p;
+            a.xq = m->xq_h;
+            a.y = m->qkv + seg.row_off;
+            a.bias = L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr;
+            a.ws = m->ws;
+            a.counters = m->counters;
+            a.ksplit = gemv_pick_ksplit(seg.p, m->sm_count);
+            TRY(launch_gemv(a, EPI_STORE, s));
+        }
+        TRY(launch_rope_cache(m->qkv, qd + 2 * kvd, m->q_rot, L.k_cache, L.v_cache, m->opt.max_seq, m->rope_cs,
+                              pos_ptr, 0, 1, c.heads, c.kv_heads, c.head_dim, c.rope_adjacent, s));
+        TRY(launch_attention_decode(m->q_rot, L.k_cache, L.v_cache, m->opt.max_seq, pos_ptr, 0, c.heads, c.kv_heads,
+                                    c.head_dim, m->attn_part, m->attn_nsplit, nullptr, m->xq_attn, s));
+        {
+            GemvArgs a;
+            a.w = &L.o.p;
+            a.xq = m->xq_attn;
+            a.y = m->x;
+            a.bias = L.o_bias;
+            a.ws = m->ws;
+            a.counters = m->counters;
+            a.ksplit = gemv_pick_ksplit(L.o.p, m->sm_count);
+            TRY(launch_gemv(a, EPI_ADD, s));
+        }
+        // feed-forward half (engine.zig:622-700, split path with cpu.gateMul)
+        TRY(launch_rmsnorm_xq(m->x, L.ffn_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, s));
+        if (L.gate_up_dual) {
+            GemvArgs a;
+            a.w = &L.gate.p;
+            a.w2 = &L.up.p;
+            a.xq = m->xq_h;
+            a.y = nullptr;
+            a.xq_out = m->xq_act;
+            a.ws = m->ws;
+            a.counters = m->counters;
+            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count);
+            TRY(launch_gemv(a, EPI_SILU_XQ, s));
+        } else {
+            GemvArgs a;
+            a.xq = m->xq_h;
+            a.ws = m->ws;
+            a.counters = m->counters;
+            a.w = &L.gate.p;
+            a.y = m->gate_buf;
+            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count);
+            TRY(launch_gemv(a, EPI_STORE, s));
+            a.w = &L.up.p;
+            a.y = m->up_buf;
+            a.ksplit = gemv_pick_ksplit(L.up.p, m->sm_count);
+            TRY(launch_gemv(a, EPI_STORE, s));
+            TRY(launch_silu_mul(m->act, m->gate_buf, m->up_buf, c.inter, s));
+            TRY(launch_to_xq(m->act, c.inter, 1, c.inter, m->xq_act, s));
+        }
+        {
+            GemvArgs a;
+            a.w = &L.down.p;
+            a.xq = m->xq_act;
+            a.y = m->x;
+            a.ws = m->ws;
+            a.counters = m->counters;
+            a.ksplit = gemv_pick_ksplit(L.down.p, m->sm_count);
+            TRY(launch_gemv(a, EPI_ADD, s));
+        }
+    }
+    // final norm + lm_head (main.zig:532-534, engine.zig:865-900) with the argmax fused
+    TRY(launch_rmsnorm_xq(m->x, m->final_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, s));
+    {
+        const Proj &head = c.tie_embeddings ? m->embed : m->output;
+        GemvArgs a;
+        a.w = &head.p;
+        a.xq = m->xq_h;
+        a.y = m->logits;
+        a.argmax64 = &m->state->argmax64;
+        a.ws = m->ws;
+        a.counters = m->counters;
+        a.ksplit = gemv_pick_ksplit(head.p, m->sm_count);
+        TRY(launch_gemv(a, EPI_ARGMAX, s));
+    }
+    finish_step_kernel<<<1, 1, 0, s>>>(m->state, m->forced, m->out_tokens);
+    CUQ_CUDA_TRY(cudaGetLastError());
+    nk += 1 + c.layers;  // finish kernel + the combine launch inside each attention
+    m->stats.kernels_per_step = nk;
+#undef TRY
+    return CUQ_OK;
+}
+
+static int run_steps(cuq_model *m, uint32_t n) {
+    for (uint32_t i = 0; i < n; i++) {
+        if (m->graph_exec) {
+            CUQ_CUDA_TRY(cudaGraphLaunch(m->graph_exec, m->stream));
+            m->stats.graph_replays++;
+        } else {
+            int rc = enqueue_step(m);
+            if (rc) return rc;
+        }
+    }
+    return CUQ_OK;
+}
+
+extern "C" {
+
+cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
+    if (!cfg) {
+        set_error("cuq_model_create: null config");
+        return nullptr;
+    }
+    const cuq_config &c = *cfg;
+    if (!c.hidden || !c.layers || !c.heads || !c.kv_heads || !c.head_dim || !c.inter || !c.vocab ||
+        c.heads % c.kv_heads || (c.head_dim != 64 && c.head_dim != 128) || c.hidden % 16 || c.inter % 16 ||
+        c.vocab % 16) {
+        set_error("cuq_model_create: unsupported geometry (hidden %u heads %u/%u head_dim %u inter %u vocab %u)",
+                  c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab);
+        return nullptr;
+    }
+    cuq_model *m = new cuq_model();
+    m->cfg = c;
+    cuq_options o{};
+    if (opts) o = *opts;
+    if (!o.max_seq) o.max_seq = 2048;
+    if (!o.max_chunk) o.max_chunk = 512;
+    if (!o.tp_size) o.tp_size = 1;
+    m->opt = o;
+    m->sm_count = sm_count_current();
+    m->layers.resize(c.layers);
+    const uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    bool ok = false;
+    do {
+        if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) break;
+        size_t kv_bytes = (size_t)c.kv_heads * o.max_seq * c.head_dim * sizeof(__half);
+        bool bad = false;
+        for (auto &L : m->layers) {
+            if (cudaMalloc(&L.k_cache, kv_bytes) != cudaSuccess || cudaMalloc(&L.v_cache, kv_bytes) != cudaSuccess ||
+                cudaMemset(L.k_cache, 0, kv_bytes) != cudaSuccess || cudaMemset(L.v_cache, 0, kv_bytes) != cudaSuccess) {
+                bad = true;
+                break;
+            }
+        }
+        if (bad) break;
+        m->stats.kv_bytes = 2 * kv_bytes * c.layers;
+        m->attn_nsplit = attn_pick_nsplit(c.kv_heads, o.max_seq, m->sm_count);
+        if (cudaMalloc(&m->x, sizeof(float) * c.hidden) != cudaSuccess) break;
+        if (cudaMalloc(&m->qkv, sizeof(float) * (qd + 2 * kvd)) != cudaSuccess) break;
+        if (cudaMalloc(&m->q_rot, sizeof(float) * qd) != cudaSuccess) break;
+        if (cudaMalloc(&m->logits, sizeof(float) * c.vocab) != cudaSuccess) break;
+        if (cudaMalloc(&m->act, sizeof(float) * c.inter) != cudaSuccess) break;
+        if (cudaMalloc(&m->gate_buf, sizeof(float) * c.inter) != cudaSuccess) break;
+        if (cudaMalloc(&m->up_buf, sizeof(float) * c.inter) != cudaSuccess) break;
+        if (cudaMalloc(&m->attn_part, sizeof(float) * (size_t)m->attn_nsplit * c.heads * (c.head_dim + 2)) !=
+            cudaSuccess)
+            break;
+        size_t xh = xq_halves(c.hidden), xa = xq_halves(qd), xi = xq_halves(c.inter);
+        if (cudaMalloc(&m->xq_h, sizeof(__half) * xh) != cudaSuccess) break;
+        if (cudaMalloc(&m->xq_attn, sizeof(__half) * xa) != cudaSuccess) break;
+        if (cudaMalloc(&m->xq_act, sizeof(__half) * xi) != cudaSuccess) break;
+        cudaMemset(m->xq_h, 0, sizeof(__half) * xh);
+        cudaMemset(m->xq_attn, 0, sizeof(__half) * xa);
+        cudaMemset(m->xq_act, 0, sizeof(__half) * xi);
+        // RoPE table, reference formula (cpu.zig:26-31)
+        std::vector<float> cs((size_t)o.max_seq * c.head_dim);
+        build_rope_table(cs.data(), o.max_seq, c.head_dim, c.rope_theta);
+        if (cudaMalloc(&m->rope_cs, sizeof(float) * cs.size()) != cudaSuccess) break;
+        if (cudaMemcpy(m->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice) != cudaSuccess) break;
+        if (cudaMalloc(&m->state, sizeof(StepState)) != cudaSuccess) break;
+        cudaMemset(m->state, 0, sizeof(StepState));
+        if (cudaMallocHost(&m->state_host, sizeof(StepState)) != cudaSuccess) break;
+        if (cudaMalloc(&m->forced, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
+        if (cudaMalloc(&m->out_tokens, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
+        if (cudaMallocHost(&m->out_host, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
+        if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess) break;
+        ok = true;
+    } while (0);
+    if (!ok) {
+        set_error("cuq_model_create: allocation failed (%s)", cudaGetErrorString(cudaGetLastError()));
+        cuq_model_free(m);
+        return nullptr;
+    }
+    return m;
+}
+
+static int check_linear_shape(const cuq_model *m, int role, uint32_t rows, uint32_t cols) {
+    const cuq_config &c = m->cfg;
+    uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    uint32_t er = 0, ec = 0;
+    switch (role) {
+    case CUQ_ROLE_Q: er = qd; ec = c.hidden; break;
+    case CUQ_ROLE_K: case CUQ_ROLE_V: er = kvd; ec = c.hidden; break;
+    case CUQ_ROLE_O: er = c.hidden; ec = qd; break;
+    case CUQ_ROLE_GATE: case CUQ_ROLE_UP: er = c.inter; ec = c.hidden; break;
+    case CUQ_ROLE_DOWN: er = c.hidden; ec = c.inter; break;
+    case CUQ_ROLE_EMBED: case CUQ_ROLE_OUTPUT: er = c.vocab; ec = c.hidden; break;
+    default: set_error("cuq_upload_tensor: role %d is not a linear tensor", role); return CUQ_EINVAL;
+    }
+    if (rows != er || cols != ec) {
+        set_error("DimensionMismatch: role %d is %u x %u, expected %u x %u", role, rows, cols, er, ec);
+        return CUQ_EINVAL;
+    }
+    return CUQ_OK;
+}
+
+int cuq_upload_tensor(cuq_model *m, int layer, int role, int ggml_type, const void *raw_host, size_t nbytes,
+                      uint32_t rows, uint32_t cols) {
+    CUQ_CHECK_ARG(m && raw_host, "cuq_upload_tensor: null argument");
+    if (m->finalized) {
+        set_error("cuq_upload_tensor: model already finalized");
+        return CUQ_EINVAL;
+    }
+    int rc = check_linear_shape(m, role, rows, cols);
+    if (rc) return rc;
+    int epb = block_elems(ggml_type), bpb = block_bytes(ggml_type);
+    if (!epb || !gemv_supported(ggml_type)) {
+        set_error("UnsupportedType: ggml type %d for role %d", ggml_type, role);
+        return CUQ_EUNSUPPORTED;
+    }
+    if (cols % epb || nbytes != (size_t)rows * (cols / epb) * bpb) {
+        set_error("InvalidTensorShape: %zu bytes for %u x %u of type %d", nbytes, rows, cols, ggml_type);
+        return CUQ_EINVAL;
+    }
+    PendingTensor *t;
+    if (role == CUQ_ROLE_EMBED)
+        t = &m->pend_embed;
+    else if (role == CUQ_ROLE_OUTPUT)
+        t = &m->pend_output;
+    else {
+        CUQ_CHECK_ARG(layer >= 0 && (uint32_t)layer < m->cfg.layers, "cuq_upload_tensor: layer %d out of range", layer);
+        t = &m->layers[layer].pend[role];
+    }
+    free_pending(*t);
+    t->type = ggml_type;
+    t->rows = rows;
+    t->cols = cols;
+    t->nbytes = nbytes;
+    CUQ_CUDA_TRY(cudaMalloc(&t->raw, nbytes));  // the GGUF bytes, as they are on disk
+    CUQ_CUDA_TRY(cudaMemcpy(t->raw, raw_host, nbytes, cudaMemcpyHostToDevice));
+    m->stats.weight_bytes += nbytes;
+    return CUQ_OK;
+}
+
+int cuq_upload_f32(cuq_model *m, int layer, int role, const float *v, size_t n) {
+    CUQ_CHECK_ARG(m && v, "cuq_upload_f32: null argument");
+    const cuq_config &c = m->cfg;
+    uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    float **slot = nullptr;
+    size_t want = 0, off = 0, total = 0;
+    if (role == CUQ_ROLE_FINAL_NORM) {
+        slot = &m->final_norm;
+        want = total = c.hidden;
+    } else {
+        CUQ_CHECK_ARG(layer >= 0 && (uint32_t)layer < c.layers, "cuq_upload_f32: layer %d out of range", layer);
+        Layer &L = m->layers[layer];
+        switch (role) {
+        case CUQ_ROLE_ATTN_NORM: slot = &L.attn_norm; want = total = c.hidden; break;
+        case CUQ_ROLE_FFN_NORM: slot = &L.ffn_norm; want = total = c.hidden; break;
+        case CUQ_ROLE_O_BIAS: slot = &L.o_bias; want = total = c.hidden; break;
+        case CUQ_ROLE_Q_BIAS: slot = &L.qkv_bias; want = qd; off = 0; total = qd + 2 * kvd; break;
+        case CUQ_ROLE_K_BIAS: slot = &L.qkv_bias; want = kvd; off = qd; total = qd + 2 * kvd; break;
+        case CUQ_ROLE_V_BIAS: slot = &L.qkv_bias; want = kvd; off = qd + kvd; total = qd + 2 * kvd; break;
+        default: set_error("cuq_upload_f32: role %d is not a vector", role); return CUQ_EINVAL;
+        }
+    }
+    if (n != want) {
+        set_error("DimensionMismatch: role %d has %zu values, expected %zu", role, n, want);
+        return CUQ_EINVAL;
+    }
+    if (!*slot) {
+        CUQ_CUDA_TRY(cudaMalloc(slot, sizeof(float) * total));
+        CUQ_CUDA_TRY(cudaMemset(*slot, 0, sizeof(float) * total));
+    }
+    CUQ_CUDA_TRY(cudaMemcpy(*slot + off, v, sizeof(float) * n, cudaMemcpyHostToDevice));
+    return CUQ_OK;
+}
+
+int cuq_model_finalize(cuq_model *m) {
+    CUQ_CHECK_ARG(m, "cuq_model_finalize: null model");
+    if (m->finalized) return CUQ_OK;
+    const cuq_config &c = m->cfg;
+    const uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    cudaStream_t s = m->stream;
+    int rc;
+    if (!m->pend_embed.raw) {
+        set_error("MissingTensor: token_embd.weight");
+        return CUQ_EINVAL;
+    }
+    if (!c.tie_embeddings && !m->pend_output.raw) {
+        set_error("MissingTensor: output.weight");
+        return CUQ_EINVAL;
+    }
+    if (!m->final_norm) {
+        set_error("MissingTensor: output_norm.weight");
+        return CUQ_EINVAL;
+    }
+    size_t ws_need = 0, ctr_need = 0;
+    auto account = [&](const Planes &p, int dual) {
+        int k = gemv_pick_ksplit(p, m->sm_count);
+        if (k > 1) {
+            size_t need = (size_t)k * p.rows * (dual ? 2 : 1);
+            if (need > ws_need) ws_need = need;
+        }
+        if (p.rows / 16 > ctr_need) ctr_need = p.rows / 16;
+    };
+    for (uint32_t l = 0; l < c.layers; l++) {
+        Layer &L = m->layers[l];
+        for (int r = 0; r < 7; r++)
+            if (!L.pend[r].raw) {
+                static const char *names[] = {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up",
+                                              "ffn_down"};
+                set_error("MissingTensor: blk.%u.%s.weight", l, names[r]);
+                return CUQ_EINVAL;
+            }
+        if (!L.attn_norm || !L.ffn_norm) {
+            set_error("MissingTensor: blk.%u norm weights", l);
+            return CUQ_EINVAL;
+        }
+        // q||k||v, fused where the types agree (load_gguf.zig:677-682)
+        PendingTensor *q = &L.pend[R_Q], *k = &L.pend[R_K], *v = &L.pend[R_V];
+        std::vector<std::vector<PendingTensor *>> groups;
+        std::vector<uint32_t> offs;
+        if (q->type == k->type && k->type == v->type) {
+            groups.push_back({q, k, v});
+            offs.push_back(0);
+        } else if (q->type == k->type) {
+            groups.push_back({q, k});
+            offs.push_back(0);
+            groups.push_back({v});
+            offs.push_back(qd + kvd);
+        } else {
+            groups.push_back({q});
+            offs.push_back(0);
+            groups.push_back({k});
+            offs.push_back(qd);
+            groups.push_back({v});
+            offs.push_back(qd + kvd);
+        }
+        L.qkv.resize(groups.size());
+        for (size_t gi = 0; gi < groups.size(); gi++) {
+            if ((rc = build_proj(L.qkv[gi], groups[gi], s))) return rc;
+            L.qkv[gi].row_off = offs[gi];
+            account(L.qkv[gi].p, 0);
+        }
+        if ((rc = build_proj(L.o, {&L.pend[R_O]}, s))) return rc;
+        if ((rc = build_proj(L.gate, {&L.pend[R_GATE]}, s))) return rc;
+        if ((rc = build_proj(L.up, {&L.pend[R_UP]}, s))) return rc;
+        if ((rc = build_proj(L.down, {&L.pend[R_DOWN]}, s))) return rc;
+        L.gate_up_dual = L.gate.p.type == L.up.p.type;
+        account(L.o.p, 0);
+        account(L.gate.p, L.gate_up_dual);
+        account(L.up.p, 0);
+        account(L.down.p, 0);
+        for (int r = 0; r < 7; r++) free_pending(L.pend[r]);
+    }
+    if ((rc = build_proj(m->embed, {&m->pend_embed}, s))) return rc;
+    free_pending(m->pend_embed);
+    if (!c.tie_embeddings) {
+        if ((rc = build_proj(m->output, {&m->pend_output}, s))) return rc;
+        free_pending(m->pend_output);
+        account(m->output.p, 0);
+    } else {
+        account(m->embed.p, 0);
+    }
+    m->ws_floats = ws_need;
+    m->n_counters = ctr_need + 1;
+    if (ws_need) CUQ_CUDA_TRY(cudaMalloc(&m->ws, sizeof(float) * ws_need));
+    CUQ_CUDA_TRY(cudaMalloc(&m->counters, sizeof(unsigned) * m->n_counters));
+    CUQ_CUDA_TRY(cudaMemset(m->counters, 0, sizeof(unsigned) * m->n_counters));
+    CUQ_CUDA_TRY(cudaDeviceSynchronize());
+    (void)qd;
+    (void)kvd;
+    m->finalized = true;
+    if (m->opt.use_graphs) {
+        CUQ_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
+        rc = enqueue_step(m);
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(s, &g);
+        if (rc != CUQ_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) {
+            set_error("graph capture: %s", cudaGetErrorString(e));
+            return CUQ_ECUDA;
+        }
+        m->graph = g;
+        CUQ_CUDA_TRY(cudaGraphInstantiate(&m->graph_exec, g, 0));
+    }
+    return CUQ_OK;
+}
+
+int cuq_model_get_config(const cuq_model *m, cuq_config *out) {
+    CUQ_CHECK_ARG(m && out, "cuq_model_get_config: null argument");
+    *out = m->cfg;
+    return CUQ_OK;
+}
+
+static int set_state(cuq_model *m, int token, int pos, int n_forced) {
+    m->state_host->token = token;
+    m->state_host->pos = pos;
+    m->state_host->step = 0;
+    m->state_host->n_forced = n_forced;
+    m->state_host->argmax64 = 0ull;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->state, m->state_host, sizeof(StepState), cudaMemcpyHostToDevice, m->stream));
+    return CUQ_OK;
+}
+
+static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint32_t *argmax_out, double *ms_out) {
+    CUQ_CUDA_TRY(cudaEventRecord(m->ev1, m->stream));
+    if (logits_host)
+        CUQ_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * m->cfg.vocab, cudaMemcpyDeviceToHost,
+                                     m->stream));
+    if (n_steps)
+        CUQ_CUDA_TRY(cudaMemcpyAsync(m->out_host, m->out_tokens, sizeof(uint32_t) * n_steps, cudaMemcpyDeviceToHost,
+                                     m->stream));
+    CUQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, m->ev0, m->ev1);
+    if (ms_out) *ms_out += ms;
+    if (argmax_out && n_steps) *argmax_out = m->out_host[n_steps - 1];
+    return CUQ_OK;
+}
+
+static int check_token(const cuq_model *m, uint32_t t) {
+    if (t >= m->cfg.vocab) {
+        set_error("token %u out of range (vocab %u)", t, m->cfg.vocab);
+        return CUQ_EINVAL;
+    }
+    return CUQ_OK;
+}
+
+int cuq_forward(cuq_model *m, uint32_t token, uint32_t pos, float *logits_host, uint32_t *argmax_out) {
+    CUQ_CHECK_ARG(m, "cuq_forward: null model");
+    if (!m->finalized) {
+        set_error("cuq_forward: model not finalized");
+        return CUQ_ENOTREADY;
+    }
+    if (pos >= m->opt.max_seq) {  // engine.zig:549
+        set_error("ContextOverflow: position %u >= max_seq %u", pos, m->opt.max_seq);
+        return CUQ_ECONTEXT;
+    }
+    int rc = check_token(m, token);
+    if (rc) return rc;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+    if ((rc = set_state(m, (int)token, (int)pos, 1))) return rc;
+    CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
+    if ((rc = run_steps(m, 1))) return rc;
+    m->stats.tokens += 1;
+    return finish_call(m, 1, logits_host, argmax_out, &m->stats.decode_ms);
+}
+
+int cuq_prefill(cuq_model *m, const uint32_t *ids, uint32_t n, uint32_t start_pos, float *logits_host,
+                uint32_t *argmax_out) {
+    CUQ_CHECK_ARG(m && (ids || n == 0), "cuq_prefill: null argument");
+    if (!m->finalized) {
+        set_error("cuq_prefill: model not finalized");
+        return CUQ_ENOTREADY;
+    }
+    if (n == 0) return CUQ_OK;
+    if ((uint64_t)start_pos + n > m->opt.max_seq) {  // engine.zig:981
+        set_error("ContextOverflow: %u + %u > max_seq %u", start_pos, n, m->opt.max_seq);
+        return CUQ_ECONTEXT;
+    }
+    int rc;
+    for (uint32_t i = 0; i < n; i++)
+        if ((rc = check_token(m, ids[i]))) return rc;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, m->stream));
+    if ((rc = set_state(m, (int)ids[0], (int)start_pos, (int)n))) return rc;
+    CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
+    if ((rc = run_steps(m, n))) return rc;
+    m->stats.prefill_tokens += n;
+    return finish_call(m, n, logits_host, argmax_out, &m->stats.prefill_ms);
+}
+
+int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_decode, uint32_t *out_tokens) {
+    CUQ_CHECK_ARG(m && ids && n_prompt > 0 && (out_tokens || n_decode == 0), "cuq_generate: bad argument");
+    if (!m->finalized) {
+        set_error("cuq_generate: model not finalized");
+        return CUQ_ENOTREADY;
+    }
+    if (n_decode == 0) return cuq_prefill(m, ids, n_prompt, 0, nullptr, nullptr);
+    uint32_t steps = n_prompt + n_decode - 1;  // the last generated token is not fed back
+    if (steps > m->opt.max_seq) {
+        set_error("ContextOverflow: %u prompt + %u decode > max_seq %u", n_prompt, n_decode, m->opt.max_seq);
+        return CUQ_ECONTEXT;
+    }
+    int rc;
+    for (uint32_t i = 0; i < n_prompt; i++)
+        if ((rc = check_token(m, ids[i]))) return rc;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids, sizeof(uint32_t) * n_prompt, cudaMemcpyHostToDevice, m->stream));
+    if ((rc = set_state(m, (int)ids[0], 0, (int)n_prompt))) return rc;
+    CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
+    if ((rc = run_steps(m, steps))) return rc;
+    m->stats.prefill_tokens += n_prompt;
+    m->stats.tokens += n_decode;
+    if ((rc = finish_call(m, steps, nullptr, nullptr, &m->stats.decode_ms))) return rc;
+    memcpy(out_tokens, m->out_host + (n_prompt - 1), sizeof(uint32_t) * n_decode);
+    return CUQ_OK;
+}
+
+int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps, uint32_t *out_tokens) {
+    CUQ_CHECK_ARG(m && (out_tokens || n_steps == 0), "cuq_decode_greedy: bad argument");
+    if (!m->finalized) {
+        set_error("cuq_decode_greedy: model not finalized");
+        return CUQ_ENOTREADY;
+    }
+    if (n_steps == 0) return CUQ_OK;
+    if ((uint64_t)pos + n_steps > m->opt.max_seq) {
+        set_error("ContextOverflow: %u + %u > max_seq %u", pos, n_steps, m->opt.max_seq);
+        return CUQ_ECONTEXT;
+    }
+    int rc = check_token(m, token);
+    if (rc) return rc;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+    if ((rc = set_state(m, (int)token, (int)pos, 1))) return rc;
+    CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
+    if ((rc = run_steps(m, n_steps))) return rc;
+    m->stats.tokens += n_steps;
+    if ((rc = finish_call(m, n_steps, nullptr, nullptr, &m->stats.decode_ms))) return rc;
+    memcpy(out_tokens, m->out_host, sizeof(uint32_t) * n_steps);
+    return CUQ_OK;
+}
+
+int cuq_reset(cuq_model *m) {
+    CUQ_CHECK_ARG(m, "cuq_reset: null model");
+    // Engine.reset (engine.zig:1479): the cache is simply overwritten from position 0
+    // by the next prefill; clearing it keeps stale rows from ever being read.
+    size_t kv_bytes = (size_t)m->cfg.kv_heads * m->opt.max_seq * m->cfg.head_dim * sizeof(__half);
+    for (auto &L : m->layers) {
+        CUQ_CUDA_TRY(cudaMemsetAsync(L.k_cache, 0, kv_bytes, m->stream));
+        CUQ_CUDA_TRY(cudaMemsetAsync(L.v_cache, 0, kv_bytes, m->stream));
+    }
+    CUQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return CUQ_OK;
+}
+
+int cuq_model_stats(const cuq_model *m, cuq_stats *out) {
+    CUQ_CHECK_ARG(m && out, "cuq_model_stats: null argument");
+    *out = m->stats;
+    return CUQ_OK;
+}
+
+void *cuq_model_stream(const cuq_model *m) { return m ? (void *)m->stream : nullptr; }
+
+void cuq_model_free(cuq_model *m) {
+    if (!m) return;
+    if (m->stream) cudaStreamSynchronize(m->stream);
+    if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
+    if (m->graph) cudaGraphDestroy(m->graph);
+    for (auto &L : m->layers) {
+        for (int r = 0; r < 7; r++) free_pending(L.pend[r]);
+        for (auto &seg : L.qkv) free_planes(seg.p);
+        free_planes(L.o.p);
+        free_planes(L.gate.p);
+        free_planes(L.up.p);
+        free_planes(L.down.p);
+        cudaFree(L.attn_norm);
+        cudaFree(L.ffn_norm);
+        cudaFree(L.qkv_bias);
+        cudaFree(L.o_bias);
+        cudaFree(L.k_cache);
+        cudaFree(L.v_cache);
+    }
+    free_pending(m->pend_embed);
+    free_pending(m->pend_output);
+    free_planes(m->embed.p);
+    free_planes(m->output.p);
+    void *bufs[] = {m->final_norm, m->x,      m->qkv,  m->q_rot,   m->logits,     m->attn_part, m->act,
+                    m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
+                    m->counters,   m->state,  m->forced, m->out_tokens};
+    for (void *b : bufs)
+        if (b) cudaFree(b);
+    if (m->state_host) cudaFreeHost(m->state_host);
+    if (m->out_host) cudaFreeHost(m->out_host);
+    if (m->ev0) cudaEventDestroy(m->ev0);
+    if (m->ev1) cudaEventDestroy(m->ev1);
+    if (m->stream) cudaStreamDestroy(m->stream);
+    delete m;
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+// model.h -- the device-resident engine behind cuq_model_* (include/cuq.h).
+#pragma once
+
+#include <vector>
+
+#include "common.cuh"
+
+namespace cuq {
+
+// One linear projection, possibly the row-concatenation of several GGUF
+// tensors of the same type (q||k||v like load_gguf.zig:677-682).
+struct Proj {
+    Planes p;
+    uint32_t row_off = 0;  // first output row inside the destination vector
+};
+
+struct PendingTensor {
+    int type = -1;
+    uint32_t rows = 0, cols = 0;
+    uint8_t *raw = nullptr;  // device staging copy of the GGUF payload
+    size_t nbytes = 0;
+};
+
+struct Layer {
+    PendingTensor pend[7];      // q k v o gate up down, until finalize
+    std::vector<Proj> qkv;      // 1..3 segments writing into the qkv vector
+    Proj o, gate, up, down;
+    bool gate_up_dual = false;  // same type/shape: one dual GEMV with the SiLU epilogue
+    float *attn_norm = nullptr, *ffn_norm = nullptr, *qkv_bias = nullptr, *o_bias = nullptr;
+    __half *k_cache = nullptr, *v_cache = nullptr;  // [kv_heads][max_seq][head_dim]
+};
+
+// Device-side step state, read and advanced by the graph itself.
+struct StepState {
+    int token;      // token fed to the next step
+    int pos;        // its position
+    int step;       // steps run since the last reset of `step`
+    int n_forced;   // steps whose next token comes from forced[] (prompt ids)
+    unsigned long long argmax64;  // packed (value, index) max of the lm_head
+};
+
+}  // namespace cuq
+
+struct cuq_model {
+    cuq_config cfg{};
+    cuq_options opt{};
+    bool finalized = false;
+    int sm_count = 148;
+    cudaStream_t stream = nullptr;
+    std::vector<cuq::Layer> layers;
+    cuq::PendingTensor pend_embed, pend_output;
+    cuq::Proj embed, output;     // output unused when tied
+    float *final_norm = nullptr;
+
+    // activations
+    float *x = nullptr, *qkv = nullptr, *q_rot = nullptr, *logits = nullptr, *attn_part = nullptr, *act = nullptr;
+    float *gate_buf = nullptr, *up_buf = nullptr;
+    __half *xq_h = nullptr, *xq_attn = nullptr, *xq_act = nullptr;
+    float *rope_cs = nullptr;                    // [max_seq][head_dim]
+    float *ws = nullptr;                         // split-K partials
+    unsigned int *counters = nullptr;
+    size_t ws_floats = 0, n_counters = 0;
+    int attn_nsplit = 1;
+    cuq::StepState *state = nullptr;             // device
+    cuq::StepState *state_host = nullptr;        // pinned
+    uint32_t *forced = nullptr, *out_tokens = nullptr;  // device, [max_seq]
+    uint32_t *out_host = nullptr;                // pinned [max_seq]
+
+    cudaGraph_t graph = nullptr;
+    cudaGraphExec_t graph_exec = nullptr;
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cuq_stats stats{};
+};

@@ -1,0 +1,131 @@
+"""Host-side mirror of the reference engine's interface over the C ABI.
+
+`Engine` keeps the shape of ``src/engine.zig``'s Engine -- ``forward(token,
+pos)`` (engine.zig:547), ``prefill(ids, start_pos)`` (engine.zig:975),
+``reset()`` (engine.zig:1479), ``stats`` -- and `Session.generate` follows
+``src/generate.zig:166-250`` for greedy decoding: truncate the prompt to the
+context, prefill, then decode on the device with no per-token host round-trip.
+Errors surface as `CuqError` with the library's status code (``ECONTEXT`` is
+the reference's ``error.ContextOverflow``).
+"""
+
+import ctypes
+
+import numpy as np
+
+from . import runtime as rt
+
+
+def _ptr(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+class Engine:
+    """A model resident on one GPU, built from a GGUF file or uploaded tensors."""
+
+    def __init__(self, handle, cfg):
+        self._h = handle
+        self.cfg = cfg  # CuqConfig
+
+    @classmethod
+    def from_gguf(cls, path, max_seq=2048, use_graphs=True, device=0):
+        L = rt.load()
+        rt.init(device)
+        opts = rt.CuqOptions(max_seq=max_seq, max_chunk=512, use_graphs=int(use_graphs), tp_rank=0, tp_size=1)
+        h = L.cuq_model_load_gguf(path.encode(), ctypes.byref(opts))
+        if not h:
+            raise rt.CuqError(rt.EINVAL, rt.last_error())
+        cfg = rt.CuqConfig()
+        rt.check(L.cuq_model_get_config(h, ctypes.byref(cfg)))
+        return cls(h, cfg)
+
+    @classmethod
+    def from_synth(cls, model, max_seq=None, use_graphs=True, device=0):
+        """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads)."""
+        L = rt.load()
+        rt.init(device)
+        c = model.cfg
+        cfg = rt.CuqConfig(hidden=c.hidden, layers=c.layers, heads=c.heads, kv_heads=c.kv_heads,
+                           head_dim=c.head_dim, inter=c.inter, vocab=c.vocab, eps=c.eps, rope_theta=c.rope_theta,
+                           rope_adjacent=int(c.rope_adjacent), tie_embeddings=int(c.tie_embeddings))
+        opts = rt.CuqOptions(max_seq=max_seq or c.max_seq, max_chunk=512, use_graphs=int(use_graphs), tp_rank=0,
+                             tp_size=1)
+        h = L.cuq_model_create(ctypes.byref(cfg), ctypes.byref(opts))
+        if not h:
+            raise rt.CuqError(rt.EINVAL, rt.last_error())
+        eng = cls(h, cfg)
+        try:
+            for t in model.tensors():
+                buf = np.frombuffer(t.data, dtype=np.uint8)
+                if t.role in ("attn_norm", "ffn_norm", "final_norm", "q_bias", "k_bias", "v_bias", "o_bias"):
+                    v = np.frombuffer(t.data, dtype=np.float32)
+                    rt.check(L.cuq_upload_f32(h, t.layer, rt.ROLE[t.role], _ptr(v), v.size))
+                else:
+                    rt.check(L.cuq_upload_tensor(h, t.layer, rt.ROLE[t.role], t.ggml_type, _ptr(buf), buf.size,
+                                                 t.rows, t.cols))
+            rt.check(L.cuq_model_finalize(h))
+        except Exception:
+            eng.close()
+            raise
+        return eng
+
+    def close(self):
+        if getattr(self, "_h", None):
+            rt.load().cuq_model_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def forward(self, token, pos, want_logits=True):
+        """Engine.forward: one decode step; returns (logits or None, argmax)."""
+        logits = np.empty(self.cfg.vocab, dtype=np.float32) if want_logits else None
+        am = ctypes.c_uint32(0)
+        rt.check(rt.load().cuq_forward(self._h, token, pos, _ptr(logits) if want_logits else None,
+                                       ctypes.byref(am)))
+        return logits, am.value
+
+    def prefill(self, ids, start_pos=0, want_logits=True):
+        """Engine.prefill: logits (and argmax) of the last prompt token."""
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        logits = np.empty(self.cfg.vocab, dtype=np.float32) if want_logits else None
+        am = ctypes.c_uint32(0)
+        rt.check(rt.load().cuq_prefill(self._h, _ptr(ids), ids.size, start_pos,
+                                       _ptr(logits) if want_logits else None, ctypes.byref(am)))
+        return logits, am.value
+
+    def decode_greedy(self, token, pos, n_steps):
+        out = np.empty(n_steps, dtype=np.uint32)
+        rt.check(rt.load().cuq_decode_greedy(self._h, token, pos, n_steps, _ptr(out)))
+        return out
+
+    def reset(self):
+        rt.check(rt.load().cuq_reset(self._h))
+
+    @property
+    def stats(self):
+        s = rt.CuqStats()
+        rt.check(rt.load().cuq_model_stats(self._h, ctypes.byref(s)))
+        return s
+
+    @property
+    def stream(self):
+        return rt.load().cuq_model_stream(self._h)
+
+
+class Session:
+    """Session.generate (generate.zig:166-250), greedy: the decode loop runs on the device."""
+
+    def __init__(self, engine, max_seq):
+        self.engine = engine
+        self.max_seq = max_seq
+
+    def generate(self, ids, n_decode):
+        ids = np.ascontiguousarray(ids, dtype=np.uint32)
+        # generate.zig:171-185: keep the tail of a prompt that does not fit
+        room = self.max_seq - n_decode + 1
+        if ids.size > room:
+            ids = ids[ids.size - room:]
+        out = np.empty(n_decode, dtype=np.uint32)
+        rt.check(rt.load().cuq_generate(self.engine._h, _ptr(ids), ids.size, n_decode, _ptr(out)))
+        return out

@@ -1,0 +1,232 @@
+/* cuq.h -- C ABI of the B200 (sm_100a) CUDA backend for ANEDVD's quantized-weight path.
+ *
+ * This header is the drop-in boundary.  It sits where the reference's ANE
+ * shim sits (src/ane/shim.h:49-116) and keeps that shim's conventions:
+ * opaque handles, int status codes, a thread-local last-error string, plain
+ * pointers and sizes, no C++ or torch types.  The engine-level calls mirror
+ * src/engine.zig's Engine (init / forward / prefill / reset / stats) so the
+ * Zig engine can call them where it evaluates ANE kernels today.
+ *
+ * Memory conventions:
+ *   - "host" arguments are ordinary CPU memory owned by the caller;
+ *   - "dev" arguments are CUDA device pointers on the current device;
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
+ *     op entry points only enqueue work and return.
+ * Status: CUQ_OK (0) on success, a negative CUQ_E* code on failure, with
+ * cuq_last_error() describing it.
+ */
+#ifndef CUQ_H
+#define CUQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------ status ---- */
+#define CUQ_OK 0
+#define CUQ_EINVAL (-1)       /* bad argument / shape (engine.zig WrongShape, gguf InvalidTensorShape) */
+#define CUQ_ENOMEM (-2)       /* device or host allocation failed */
+#define CUQ_ECUDA (-3)        /* a CUDA runtime call failed */
+#define CUQ_ECONTEXT (-4)     /* position past max_seq: engine.zig:549,981 error.ContextOverflow */
+#define CUQ_EUNSUPPORTED (-5) /* ggml type not handled here: gguf.zig error.UnsupportedType */
+#define CUQ_ETIMEOUT (-6)     /* a bounded device-side wait gave up */
+#define CUQ_EFORMAT (-7)      /* malformed GGUF: gguf.zig NotGgufFile / TruncatedFile / ... */
+#define CUQ_ENOTREADY (-8)    /* cuq_init not called / model not finalized */
+
+/* ggml type ids as stored in GGUF (src/gguf.zig:30-46). */
+#define CUQ_F32 0
+#define CUQ_F16 1
+#define CUQ_Q4_0 2
+#define CUQ_Q4_1 3
+#define CUQ_Q5_0 6
+#define CUQ_Q5_1 7
+#define CUQ_Q8_0 8
+#define CUQ_Q8_1 9
+#define CUQ_Q2_K 10
+#define CUQ_Q3_K 11
+#define CUQ_Q4_K 12
+#define CUQ_Q5_K 13
+#define CUQ_Q6_K 14
+#define CUQ_Q8_K 15
+#define CUQ_BF16 30
+
+/* ------------------------------------------------------- lifecycle ---- */
+
+/* Select `device` and create the library's context on it.
+ * Replaces ane_shim_init (src/ane/shim.h:53-54): 0 on success, <0 on failure. */
+int cuq_init(int device);
+/* 1 if cuq_init succeeded on this thread's current device (ane_shim_ready, shim.h:57). */
+int cuq_ready(void);
+/* Thread-local description of the last failure (ane_shim_last_error, shim.h:60). */
+const char *cuq_last_error(void);
+/* Library build string (git-free: compiler + arch). */
+const char *cuq_version(void);
+
+/* Block geometry (gguf.zig:49-77); 0 for unsupported types. */
+int cuq_block_elems(int ggml_type);
+int cuq_block_bytes(int ggml_type);
+
+/* --------------------------------------------------- dequantisation ---- */
+
+/* gguf.dequantizeRange (gguf.zig:694-728) on the device: `out_n` float32
+ * values starting at element `elem_offset` of the raw GGUF blocks at
+ * `raw_dev` (`raw_bytes` long).  Bit-exact with the reference for all 15
+ * types.  All pointers dev. */
+int cuq_dequant(int ggml_type, const void *raw_dev, size_t raw_bytes, uint64_t elem_offset,
+                float *out_dev, size_t out_n, void *stream);
+
+/* ------------------------------------------------------------ weights --- */
+
+/* A weight matrix resident in HBM in its quantized form.  Replaces the fp16
+ * [out][in] expansion of load_gguf.loadLinear (load_gguf.zig:358-386): the raw
+ * GGUF payload (row-major [rows][cols], blocks along cols) is copied to the
+ * device as-is and losslessly regrouped there into per-field planes (quants,
+ * scales) so every warp load is an aligned 128-bit access.  Same byte count as
+ * the file; cuq_weight_export_raw gives back the identical bytes. */
+typedef struct cuq_weight cuq_weight;
+
+/* raw_host: host pointer to the GGUF payload. NULL on failure (see cuq_last_error). */
+cuq_weight *cuq_weight_create(int ggml_type, const void *raw_host, size_t nbytes, uint32_t rows,
+                              uint32_t cols);
+/* Rebuild the original GGUF payload (host buffer of cuq_weight_nbytes bytes). */
+int cuq_weight_export_raw(const cuq_weight *w, void *raw_host, size_t nbytes);
+size_t cuq_weight_nbytes(const cuq_weight *w);
+void cuq_weight_free(cuq_weight *w);
+
+/* y[rows] = W x: quantized GEMV, batch 1 (the decode projection).  x_dev is
+ * float32 [cols], y_dev float32 [rows].  Results follow the reference's
+ * matmulF16 (main.zig:320-326) on fp16-rounded weights within 1e-3 relative. */
+int cuq_gemv(const cuq_weight *w, const float *x_dev, float *y_dev, void *stream);
+
+/* The GEMV's activation operand, prepared once: x split into fp16 hi + lo
+ * parts (x = hi + lo to ~22 bits) in the column order the tensor-core
+ * fragments read.  cuq_xq_halves(n) halves of device memory hold it. */
+size_t cuq_xq_halves(uint32_t n);
+int cuq_prepare_x(const float *x_dev, uint32_t n, uint16_t *xq_dev, void *stream);
+/* cuq_gemv on an already prepared activation (one kernel launch). */
+int cuq_gemv_prepared(const cuq_weight *w, const uint16_t *xq_dev, float *y_dev, void *stream);
+
+/* Y[n][rows] = X[n][cols] W^T for a chunk of n tokens (the prefill projection,
+ * engine.zig:975-1329).  X, Y float32 row-major, dev. */
+int cuq_gemm(const cuq_weight *w, const float *x_dev, uint32_t n, float *y_dev, void *stream);
+
+/* Dequantise W to fp16 [rows][cols] exactly as Gguf.readF16 (gguf.zig:554-578) does:
+ * reference fp32 value, then round to nearest even. out_dev holds rows*cols halves. */
+int cuq_weight_dequant_f16(const cuq_weight *w, uint16_t *out_dev, void *stream);
+
+/* --------------------------------------------------------- dense ops ---- */
+
+/* cpu.rmsnorm (cpu.zig:11-18) on `n_rows` rows of length n: out = x * rsqrt(mean(x^2)+eps) * w. */
+int cuq_rmsnorm(float *out_dev, const float *x_dev, const float *w_dev, uint32_t n, uint32_t n_rows,
+                float eps, void *stream);
+/* cpu.rope / cpu.ropeAdjacent (cpu.zig:22-62), in place on `heads` heads of `hd`. */
+int cuq_rope(float *v_dev, uint32_t heads, uint32_t hd, uint32_t pos, float theta, int adjacent,
+             void *stream);
+/* cpu.siluMul (cpu.zig:65-70). */
+int cuq_silu_mul(float *out_dev, const float *g_dev, const float *u_dev, uint32_t n, void *stream);
+/* cpu.attentionDecode (cpu.zig:323-395): q [heads*hd] f32; k/v fp16 caches laid
+ * out [kv_heads][cache_stride][hd] (position-major inside each head); attends to
+ * positions [0, n_past).  Split over positions on the device. */
+int cuq_attention_decode(float *out_dev, const float *q_dev, const uint16_t *k_dev,
+                         const uint16_t *v_dev, uint32_t n_past, uint32_t cache_stride,
+                         uint32_t heads, uint32_t kv_heads, uint32_t hd, void *stream);
+/* cpu.argmax (cpu.zig:477-483): first index of the maximum, written to *out_dev (u32). */
+int cuq_argmax(const float *v_dev, uint32_t n, uint32_t *out_dev, void *stream);
+
+/* ------------------------------------------------------------ engine ---- */
+
+/* Model geometry: the fields of model.Config (model.zig:10-244) this path uses. */
+typedef struct {
+    uint32_t hidden, layers, heads, kv_heads, head_dim, inter, vocab;
+    float eps, rope_theta;
+    int32_t rope_adjacent;   /* load_gguf.zig:81-90: llama -> 1, qwen2 -> 0 */
+    int32_t tie_embeddings;  /* no output.weight: lm_head reads token_embd (load_gguf.zig:141) */
+} cuq_config;
+
+/* Engine options (engine.zig:28-51 Options, plus device-side knobs). */
+typedef struct {
+    uint32_t max_seq;        /* KV-cache positions (engine.zig:447-458); default 2048 */
+    uint32_t max_chunk;      /* largest prefill chunk; default 512 */
+    int32_t use_graphs;      /* capture the decode step in a CUDA graph (default 1) */
+    int32_t tp_rank, tp_size;/* tensor parallel slot (tp_size 1 = single GPU) */
+} cuq_options;
+
+/* Tensor roles for cuq_upload_*. */
+#define CUQ_ROLE_Q 0
+#define CUQ_ROLE_K 1
+#define CUQ_ROLE_V 2
+#define CUQ_ROLE_O 3
+#define CUQ_ROLE_GATE 4
+#define CUQ_ROLE_UP 5
+#define CUQ_ROLE_DOWN 6
+#define CUQ_ROLE_ATTN_NORM 7
+#define CUQ_ROLE_FFN_NORM 8
+#define CUQ_ROLE_Q_BIAS 9
+#define CUQ_ROLE_K_BIAS 10
+#define CUQ_ROLE_V_BIAS 11
+#define CUQ_ROLE_O_BIAS 12
+#define CUQ_ROLE_EMBED 13
+#define CUQ_ROLE_OUTPUT 14
+#define CUQ_ROLE_FINAL_NORM 15
+
+typedef struct cuq_model cuq_model;
+
+/* Per-call statistics (engine.zig:83-131 Stats): device time per node class. */
+typedef struct {
+    uint64_t tokens;           /* decode steps run */
+    uint64_t prefill_tokens;   /* prompt tokens prefilled */
+    double decode_ms;          /* device time in decode steps */
+    double prefill_ms;         /* device time in prefill */
+    uint64_t weight_bytes;     /* quantized weight bytes resident */
+    uint64_t kv_bytes;         /* KV-cache bytes */
+    uint64_t graph_replays;
+    uint64_t kernels_per_step; /* kernel launches in one decode step */
+} cuq_stats;
+
+/* Engine.init (engine.zig:320-521) without weights: allocates the KV cache and
+ * activation buffers.  NULL on failure. */
+cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts);
+/* Upload one tensor's raw GGUF payload (load_gguf.loadLayer, load_gguf.zig:650-713,
+ * minus the fp16 expansion).  `layer` is ignored for EMBED/OUTPUT.  Copied; the
+ * caller keeps ownership of raw_host (e.g. its mmap). */
+int cuq_upload_tensor(cuq_model *m, int layer, int role, int ggml_type, const void *raw_host,
+                      size_t nbytes, uint32_t rows, uint32_t cols);
+/* Norm weights and biases (float32, host). */
+int cuq_upload_f32(cuq_model *m, int layer, int role, const float *v_host, size_t n);
+/* Check every tensor is present and build the device-resident step. */
+int cuq_model_finalize(cuq_model *m);
+/* Parse a GGUF v2/v3 file (gguf.zig:328-656), read its config (load_gguf.loadConfig,
+ * load_gguf.zig:96-302) and upload every tensor raw.  Returns a finalized model. */
+cuq_model *cuq_model_load_gguf(const char *path, const cuq_options *opts);
+int cuq_model_get_config(const cuq_model *m, cuq_config *out);
+
+/* Engine.forward (engine.zig:547-819): one decode step for `token` at `pos`.
+ * logits_host (vocab floats) may be NULL; argmax_out (host u32) may be NULL. */
+int cuq_forward(cuq_model *m, uint32_t token, uint32_t pos, float *logits_host, uint32_t *argmax_out);
+/* Engine.prefill (engine.zig:975-1329): run `n` prompt ids starting at start_pos;
+ * logits/argmax of the LAST token (engine.zig:1310-1316). */
+int cuq_prefill(cuq_model *m, const uint32_t *ids, uint32_t n, uint32_t start_pos,
+                float *logits_host, uint32_t *argmax_out);
+/* Session.generate (generate.zig:166-250) for greedy decoding: prefill `ids`, then
+ * `n_decode` steps entirely on the device (the argmax feeds the next step with
+ * no host round-trip).  out_tokens (host, n_decode u32) gets the generated ids. */
+int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_decode,
+                 uint32_t *out_tokens);
+/* Decode `n_steps` greedy tokens from the device-resident state left by a
+ * prefill/forward at position `pos` with next token `token` (no prefill). */
+int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps,
+                      uint32_t *out_tokens);
+/* Engine.reset (engine.zig:1479): forget the KV cache. */
+int cuq_reset(cuq_model *m);
+int cuq_model_stats(const cuq_model *m, cuq_stats *out);
+/* The stream the model enqueues on (cudaStream_t as void*). */
+void *cuq_model_stream(const cuq_model *m);
+void cuq_model_free(cuq_model *m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* CUQ_H */

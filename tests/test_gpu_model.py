@@ -1,0 +1,142 @@
+"""Whole-model parity on the GPU: the device-resident engine against the CPU
+oracle's refForward (teacher-forced, every position compared).
+
+Bars: logits within 2e-3 relative error
+(rel = max|a-b| / max|b|, main.zig:1920-1930); greedy tokens identical wherever
+the oracle's top-2 margin exceeds that tolerance.
+"""
+import numpy as np
+import pytest
+
+from anedvd_b200 import engine as E
+from anedvd_b200 import runtime as rt
+from anedvd_b200 import synth
+from oracle import oracle as orc
+
+from .gpu_util import rel_err
+
+pytestmark = pytest.mark.gpu
+LOGIT_TOL = 2e-3
+
+SMALL = [("smollm2-135m", dict(layers=2, vocab=1024)), ("qwen2.5-0.5b", dict(layers=2, vocab=1024)),
+         ("qwen2.5-1.5b", dict(layers=3, vocab=1024)), ("llama3-8b", dict(layers=1, vocab=1024))]
+
+
+def _prompt(cfg, n, salt=0):
+    rng = np.random.default_rng(1234 + salt)
+    return rng.integers(0, cfg.vocab, size=n).astype(np.uint32)
+
+
+def _margin_ok(logits, tol):
+    top = np.sort(logits)[-2:]
+    return (top[1] - top[0]) > tol * np.max(np.abs(logits))
+
+
+def _compare(model, n_prompt, n_decode, threads=8, use_graphs=True):
+    cfg = model.cfg
+    ref = orc.Model(cfg, threads=threads, max_seq=n_prompt + n_decode + 1)
+    ref.load(model)
+    eng = E.Engine.from_synth(model, max_seq=n_prompt + n_decode + 1, use_graphs=use_graphs)
+    ids = _prompt(cfg, n_prompt)
+    errs = []
+    # prefill: the reference's CPU path feeds the prompt token by token (main.zig:1255-1262)
+    for p, t in enumerate(ids):
+        want = ref.forward(int(t), p)
+    got, am = eng.prefill(ids, 0)
+    errs.append(rel_err(got, want))
+    if _margin_ok(want, LOGIT_TOL):
+        assert am == orc.argmax(want)
+    # decode, teacher-forced with the oracle's greedy tokens
+    tok = orc.argmax(want)
+    for s in range(n_decode):
+        pos = n_prompt + s
+        want = ref.forward(tok, pos)
+        got, am = eng.forward(tok, pos)
+        errs.append(rel_err(got, want))
+        if _margin_ok(want, LOGIT_TOL):
+            assert am == orc.argmax(want), (s, am, orc.argmax(want))
+        tok = orc.argmax(want)
+    eng.close()
+    return max(errs)
+
+
+@pytest.mark.parametrize("name,kw", SMALL, ids=[s[0] for s in SMALL])
+def test_small_models_match_reference(name, kw):
+    e = _compare(synth.model(name, **kw), n_prompt=9, n_decode=6)
+    assert e < LOGIT_TOL, e
+
+
+def test_smollm2_full_size_matches_reference():
+    """BASELINE config 2 at full size (30 layers, vocab 49152), 16-token prompt."""
+    e = _compare(synth.model("smollm2-135m"), n_prompt=16, n_decode=8)
+    assert e < LOGIT_TOL, e
+
+
+def test_graph_and_eager_agree():
+    m = synth.model("qwen2.5-0.5b", layers=2, vocab=1024)
+    ids = _prompt(m.cfg, 7)
+    a = E.Engine.from_synth(m, max_seq=32, use_graphs=True)
+    b = E.Engine.from_synth(m, max_seq=32, use_graphs=False)
+    la, _ = a.prefill(ids)
+    lb, _ = b.prefill(ids)
+    assert np.array_equal(la, lb)
+
+
+def test_device_generate_equals_step_by_step():
+    m = synth.model("smollm2-135m", layers=2, vocab=1024)
+    ids = _prompt(m.cfg, 5)
+    eng = E.Engine.from_synth(m, max_seq=64)
+    gen = E.Session(eng, 64).generate(ids, 12)
+    eng.reset()
+    _, am = eng.prefill(ids)
+    steps = [am]
+    for s in range(11):
+        _, am = eng.forward(steps[-1], len(ids) + s)
+        steps.append(am)
+    assert list(gen) == steps
+
+
+def test_gguf_loader_matches_upload(tmp_path):
+    m = synth.model("qwen2.5-0.5b", layers=2, vocab=1024)
+    path = str(tmp_path / "m.gguf")
+    m.write_gguf(path)
+    ids = _prompt(m.cfg, 6)
+    a = E.Engine.from_gguf(path, max_seq=16)
+    b = E.Engine.from_synth(m, max_seq=16)
+    la, _ = a.prefill(ids)
+    lb, _ = b.prefill(ids)
+    assert np.array_equal(la, lb)
+    assert a.cfg.rope_adjacent == 0 and a.cfg.tie_embeddings == 1 and a.cfg.vocab == 1024
+
+
+def test_context_overflow_and_bad_token():
+    m = synth.model("smollm2-135m", layers=1, vocab=1024)
+    eng = E.Engine.from_synth(m, max_seq=8)
+    with pytest.raises(rt.CuqError) as ei:
+        eng.forward(1, 8)
+    assert ei.value.code == rt.ECONTEXT  # error.ContextOverflow, engine.zig:549
+    with pytest.raises(rt.CuqError) as ei:
+        eng.prefill(np.arange(9, dtype=np.uint32))
+    assert ei.value.code == rt.ECONTEXT  # engine.zig:981
+    with pytest.raises(rt.CuqError) as ei:
+        eng.forward(5000, 0)
+    assert ei.value.code == rt.EINVAL
+    # still usable afterwards
+    lg, am = eng.forward(3, 0)
+    assert np.isfinite(lg).all()
+
+
+def test_missing_tensor_is_reported():
+    L = rt.load()
+    rt.init(0)
+    import ctypes
+    c = synth.CONFIGS["smollm2-135m"]
+    cfg = rt.CuqConfig(hidden=c.hidden, layers=1, heads=c.heads, kv_heads=c.kv_heads, head_dim=c.head_dim,
+                       inter=c.inter, vocab=1024, eps=c.eps, rope_theta=c.rope_theta, rope_adjacent=1,
+                       tie_embeddings=1)
+    opts = rt.CuqOptions(max_seq=8, max_chunk=8, use_graphs=1, tp_rank=0, tp_size=1)
+    h = L.cuq_model_create(ctypes.byref(cfg), ctypes.byref(opts))
+    assert h
+    assert L.cuq_model_finalize(h) == rt.EINVAL
+    assert "MissingTensor" in rt.last_error()
+    L.cuq_model_free(h)
