@@ -42,6 +42,7 @@ SIGNATURES = [
     ("cuq_rope", I32, [P, U32, U32, U32, F32, I32, P]),
     ("cuq_silu_mul", I32, [P, P, P, U32, P]),
     ("cuq_attention_decode", I32, [P, P, P, P, U32, U32, U32, U32, U32, P]),
+    ("cuq_attention_decode_noalloc", I32, [P, P, P, P, U32, U32, U32, U32, U32, P]),
     ("cuq_argmax", I32, [P, U32, P, P]),
     ("cuq_model_create", P, [P, P]),
     ("cuq_upload_tensor", I32, [P, I32, I32, I32, P, SZ, U32, U32]),

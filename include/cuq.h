@@ -133,6 +133,19 @@ int cuq_silu_mul(float *out_dev, const float *g_dev, const float *u_dev, uint32_
 int cuq_attention_decode(float *out_dev, const float *q_dev, const uint16_t *k_dev,
                          const uint16_t *v_dev, uint32_t n_past, uint32_t cache_stride,
                          uint32_t heads, uint32_t kv_heads, uint32_t hd, void *stream);
+/* cuq_attention_decode without any allocation.  No counterpart in the
+ * reference: it exists for callers that may not allocate device memory while
+ * they run (an engine that reserved all device memory up front, or a loop that
+ * cannot afford an allocator call between steps).  Its split scratch lives in a
+ * fixed 1 MiB array inside the library (262,144 floats, held on every GPU that
+ * loads the library until exit); calls whose heads * (hd + 2) exceeds that are
+ * rejected with CUQ_EINVAL.  The first call on each device looks the array's
+ * device address up (cudaGetSymbolAddress), so make that first call before any
+ * stream capture.  All calls share the one array: calls that overlap on the GPU
+ * (other streams, other threads) race and must be serialised by the caller. */
+int cuq_attention_decode_noalloc(float *out_dev, const float *q_dev, const uint16_t *k_dev,
+                                 const uint16_t *v_dev, uint32_t n_past, uint32_t cache_stride,
+                                 uint32_t heads, uint32_t kv_heads, uint32_t hd, void *stream);
 /* cpu.argmax (cpu.zig:477-483): first index of the maximum, written to *out_dev (u32). */
 int cuq_argmax(const float *v_dev, uint32_t n, uint32_t *out_dev, void *stream);
 
