@@ -7,6 +7,7 @@
 
 #include <cstdio>
 #include <string>
+#include <utility>
 
 #include "../../include/cuq.h"
 
@@ -122,7 +123,7 @@ int launch_dequant_planes_f16(const Planes &p, __half *out, cudaStream_t s);
 // 16 columns (the K-quant GEMV subtracts its per-sub-block minimum as
 // m1 * sum(x) in fp32).  `n_vec` vectors are stored back to back with a stride
 // of xq_halves(cols) halves.
-inline uint32_t xq_pad(uint32_t cols) { return (cols + 255u) & ~255u; }
+__host__ __device__ inline uint32_t xq_pad(uint32_t cols) { return (cols + 255u) & ~255u; }
 inline size_t xq_halves(uint32_t cols) {
     size_t k = xq_pad(cols);
     return 2 * k + k / 8;
@@ -138,7 +139,57 @@ int launch_to_xq(const float *x, uint32_t n, uint32_t n_vec, uint32_t x_stride, 
 int launch_rmsnorm_xq(const float *x, const float *w, uint32_t n, uint32_t n_rows, float eps, __half *xq,
                       float *h_out, cudaStream_t s);
 
+// Device-side decode-step state, read and advanced by the step's kernels.
+struct StepState {
+    int token;      // token fed to the next step
+    int pos;        // its position
+    int step;       // steps run since the state was last set by the host
+    int n_forced;   // steps whose next token comes from forced[] (prompt ids)
+    unsigned long long argmax64;  // packed (value, index) max of the lm_head
+};
+
+// Programmatic dependent launch: wait for the preceding kernel's results
+// (no-op when launched without the attribute) / let the next kernel start.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch `kernel` with the programmatic-stream-serialization attribute when pdl is set.
+template <typename... KArgsT, typename... ActT>
+cudaError_t launch_maybe_pdl(void (*kernel)(KArgsT...), dim3 grid, dim3 block, size_t smem, cudaStream_t s, bool pdl,
+                             ActT &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<ActT>(args)...);
+}
+
 // ------------------------------------------------------------------ GEMV ---
+
+// Work the CTA that completes a GEMV's last tile does after the whole output is
+// written: the next RMSNorm (of the residual x into xq), or the end of a decode
+// step (argmax -> next token).
+enum GemvPostOp : int { POST_NONE = 0, POST_RMSNORM = 1, POST_FINISH = 2 };
+
+struct GemvPost {
+    int op = POST_NONE;
+    unsigned int *done = nullptr;  // grid completion counter (self-resetting)
+    // POST_RMSNORM: xq_out = split(rmsnorm(x, w, eps)), n = len(x)
+    const float *x = nullptr, *w = nullptr;
+    uint32_t n = 0;
+    float eps = 0.f;
+    __half *xq = nullptr;
+    // POST_FINISH
+    StepState *state = nullptr;
+    const uint32_t *forced = nullptr;
+    uint32_t *out_tokens = nullptr;
+};
 
 enum GemvEpilogue : int {
     EPI_STORE = 0,     // y = acc (+ bias)
@@ -158,7 +209,61 @@ struct GemvArgs {
     float *ws = nullptr;          // split-K partials [ksplit][rows]
     unsigned int *counters = nullptr;  // one per 16-row tile, self-resetting
     int ksplit = 1;
+    bool pdl = false;             // launch as a programmatic dependent of the previous kernel
+    GemvPost post;
 };
+
+// Position of column i inside an xq half-vector: (0, 2, 1, 3) in each group of 4.
+__device__ __forceinline__ uint32_t xq_pos(uint32_t i) { return (i & ~3u) | ((i & 1u) << 1) | ((i >> 1) & 1u); }
+
+// The block-level RMSNorm -> xq writer shared by the standalone kernel, the
+// GEMV post-op and the embedding kernel: cpu.rmsnorm (cpu.zig:11-18),
+// out = (x * (1 / sqrt(mean(x^2) + eps))) * w, then the xq split and per-16
+// sums.  Reads x through L2 (it may have been written by other SMs).  Every
+// thread of the block must call it.
+__device__ __forceinline__ void rmsnorm_xq_block(const float *x, const float *w, uint32_t n, float eps, __half *xq,
+                                                 uint32_t kpad, float *h_out) {
+    __shared__ float part[32];
+    float acc = 0.f;
+    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
+        float v = __ldcg(x + i);
+        acc += v * v;
+    }
+#pragma unroll
+    for (int o2 = 16; o2 > 0; o2 >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
+    __syncthreads();  // `part` may still be in use by a previous call in this block
+    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float s = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
+#pragma unroll
+        for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
+        if (threadIdx.x == 0) part[0] = s;
+    }
+    __syncthreads();
+    const float mean = part[0] / (float)n;
+    const float inv = 1.0f / sqrtf(mean + eps);
+    float *sums = xq_sums(xq, kpad);
+    // kpad is a multiple of 256 and blockDim a multiple of 16, so every thread
+    // runs the same number of iterations and each aligned group of 16 lanes
+    // holds 16 consecutive columns: their sum is a 16-lane shuffle reduction.
+    for (uint32_t i = threadIdx.x; i < kpad; i += blockDim.x) {
+        float f = 0.f;
+        if (i < n) {
+            f = (__ldcg(x + i) * inv) * w[i];
+            if (h_out) h_out[i] = f;
+        }
+        __half hi = __float2half_rn(f);
+        __half lo = __float2half_rn(f - __half2float(hi));
+        uint32_t pos = xq_pos(i);
+        xq[pos] = hi;
+        xq[kpad + pos] = lo;
+        float a = f;
+#pragma unroll
+        for (int o2 = 1; o2 < 16; o2 <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o2);
+        if ((i & 15u) == 0) sums[i >> 4] = a;
+    }
+}
 
 int launch_gemv(const GemvArgs &a, int epilogue, cudaStream_t s);
 // Scratch a GEMV of this weight needs for a given ksplit (floats, counters).

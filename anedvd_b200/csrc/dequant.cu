@@ -4,6 +4,7 @@
 // Every multiply/add is an explicit round-to-nearest intrinsic so the compiler
 // cannot contract `a*b - c` into one FMA: the reference rounds after each op.
 #include "common.cuh"
+#include "ops.cuh"
 
 namespace cuq {
 
@@ -238,6 +239,27 @@ __global__ void embed_row_kernel(PlanesView p, const int *__restrict__ token_ptr
     }
 }
 
+// Decode-step start: the embedding row of state->token (as embed_row_kernel)
+// followed by the first layer's RMSNorm into the qkv projection's xq input.
+__global__ void embed_norm_kernel(PlanesView p, const StepState *__restrict__ st, float *__restrict__ x,
+                                  const float *__restrict__ nw, uint32_t n, float eps, __half *__restrict__ xq,
+                                  int epb) {
+    griddep_wait();
+    griddep_launch();
+    const uint32_t r = (uint32_t)st->token;
+    uint8_t blk[212];
+    if (r < p.rows) {
+        for (uint32_t b = threadIdx.x; b < p.cols / epb; b += blockDim.x) {
+            block_move(p, blk, r, b, 1);
+            for (int j = 0; j < epb; j++)
+                x[(size_t)b * epb + j] = __half2float(__float2half_rn(dq_elem(p.type, blk, j)));
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    rmsnorm_xq_block(x, nw, n, eps, xq, xq_pad(n), nullptr);
+}
+
 PlanesView view(const Planes &p) {
     return PlanesView{p.type, p.rows, p.cols, p.base, p.off_q, p.off_q2, p.off_s, p.off_s2};
 }
@@ -331,6 +353,17 @@ int launch_unpack(const Planes &p, uint8_t *raw, cudaStream_t s) {
     size_t total = (size_t)p.rows * (p.cols / epb);
     repack_kernel<<<grid_for(total, 128), 128, 0, s>>>(view(p), nullptr, raw, 1, epb, bpb);
     CUQ_CUDA_TRY(cudaGetLastError());
+    return CUQ_OK;
+}
+
+int launch_embed_norm(const Planes &p, const StepState *state, float *x, const float *norm_w, uint32_t n, float eps,
+                      __half *xq, bool pdl, cudaStream_t s) {
+    cudaError_t e = launch_maybe_pdl(embed_norm_kernel, dim3(1), dim3(256), 0, s, pdl, view(p), state, x, norm_w, n,
+                                     eps, xq, block_elems(p.type));
+    if (e != cudaSuccess) {
+        set_error("embed launch: %s", cudaGetErrorString(e));
+        return CUQ_ECUDA;
+    }
     return CUQ_OK;
 }
 

@@ -376,6 +376,7 @@ struct KArgs {
     float *ws;
     unsigned int *counters;
     int ksplit;
+    GemvPost post;
 };
 
 __device__ __forceinline__ unsigned long long pack_argmax(float v, uint32_t idx) {
@@ -384,7 +385,19 @@ __device__ __forceinline__ unsigned long long pack_argmax(float v, uint32_t idx)
     return ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
 }
 
-__device__ __forceinline__ uint32_t xq_pos(uint32_t i) { return (i & ~3u) | ((i & 1u) << 1) | ((i >> 1) & 1u); }
+// End of a decode step (engine.zig:865-900 + generate.zig:217-244, greedy):
+// the packed argmax becomes the step's output token and, past the forced
+// prompt, the next step's input.
+__device__ void finish_step(StepState *st, const uint32_t *forced, uint32_t *out_tokens) {
+    unsigned long long a = st->argmax64;
+    uint32_t idx = 0xFFFFFFFFu - (uint32_t)(a & 0xFFFFFFFFull);
+    st->argmax64 = 0ull;
+    int s = st->step;
+    out_tokens[s] = idx;
+    st->step = s + 1;
+    st->pos = st->pos + 1;
+    st->token = (s + 1 < st->n_forced) ? (int)forced[s + 1] : (int)idx;
+}
 
 template <class TT, int EPI>
 __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
@@ -399,30 +412,55 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     const int per = (ni + p.ksplit - 1) / p.ksplit;
     const int it0 = blockIdx.y * per, it1 = min(ni, it0 + per);
 
-    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);
+    // The weights do not depend on the previous kernel: start streaming the
+    // warp's first iteration before waiting for the activation.
+    // One iteration in flight per warp beyond the one computing: deeper register
+    // rings cost more occupancy than they hide (measured).
+    constexpr int D = 1;
+    typename TT::Raw ring[D], ring2[D];
+#pragma unroll
+    for (int j = 0; j < D; j++) {
+        const int itj = it0 + warp + 4 * j;
+        if (itj < it1) {
+            TT::load(ring[j], p.w, r0, itj, tig);
+            if (DUAL) TT::load(ring2[j], p.w2, r0, itj, tig);
+        }
+    }
+    griddep_wait();
+    griddep_launch();
+
+    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);  // B fragments: L1-cached, shared by the SM's CTAs
     const bool bl = g < 2;
 
     float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
     float k0 = 0.f, k1 = 0.f, k20 = 0.f, k21 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
-    for (int it = it0 + warp; it < it1; it += 4) {
-        typename TT::Raw R, R2;
-        TT::load(R, p.w, r0, it, tig);
-        if (DUAL) TT::load(R2, p.w2, r0, it, tig);
+    for (int base = it0 + warp; base < it1; base += 4 * D) {
 #pragma unroll
-        for (int s = 0; s < TT::KSTEPS; s++) {
-            uint2 b = make_uint2(0u, 0u);
-            if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
-            uint32_t a[4];
-            TT::frag(R, s, a);
-            mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
-            if (DUAL) {
-                TT::frag(R2, s, a);
-                mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
+        for (int j = 0; j < D; j++) {
+            const int it = base + 4 * j;
+            if (it >= it1) break;  // uniform across the warp
+            typename TT::Raw R = ring[j], R2 = ring2[j];
+            const int itn = it + 4 * D;
+            if (itn < it1) {  // refill this slot while the iteration computes
+                TT::load(ring[j], p.w, r0, itn, tig);
+                if (DUAL) TT::load(ring2[j], p.w2, r0, itn, tig);
             }
-        }
-        if (TT::HAS_CORR) {
-            TT::correct(R, p.xsum, it, tig, k0, k1);
-            if (DUAL) TT::correct(R2, p.xsum, it, tig, k20, k21);
+#pragma unroll
+            for (int s = 0; s < TT::KSTEPS; s++) {
+                uint2 b = make_uint2(0u, 0u);
+                if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
+                uint32_t a[4];
+                TT::frag(R, s, a);
+                mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
+                if (DUAL) {
+                    TT::frag(R2, s, a);
+                    mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
+                }
+            }
+            if (TT::HAS_CORR) {
+                TT::correct(R, p.xsum, it, tig, k0, k1);
+                if (DUAL) TT::correct(R2, p.xsum, it, tig, k20, k21);
+            }
         }
     }
     if (TT::HAS_CORR) {  // the four lanes of a row hold different sub-blocks: sum them
@@ -474,9 +512,9 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     }
     if (EPI == EPI_SILU_XQ) {
         __shared__ float gu[32];
+        __shared__ float act16[16];
         if (t < 32) gu[t] = v;
         __syncthreads();
-        __shared__ float act16[16];
         if (t < 16) {
             uint32_t row = row0 + t;
             float gt = gu[t], ut = gu[16 + t];
@@ -497,31 +535,48 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
             for (int j = 0; j < 16; j++) acc += act16[j];
             xq_sums(p.xq_out, p.kpad_out)[tile] = acc;
         }
-        return;
-    }
-    if (t < 16) {
-        uint32_t row = row0 + t;
-        if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
-            if (p.bias) v = v + p.bias[row];
-            p.y[row] = v;
-        } else if (EPI == EPI_ADD) {
-            if (p.bias) v = v + p.bias[row];
-            p.y[row] = p.y[row] + v;
-        }
-    }
-    if (EPI == EPI_ARGMAX) {
-        // first index of the maximum within the tile (cpu.zig:477-483), then a
-        // packed 64-bit max across tiles: larger value wins, then smaller index.
-        if (t < 32) {
-            unsigned long long key = t < 16 ? pack_argmax(v, row0 + t) : 0ull;
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) {
-                unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
-                key = other > key ? other : key;
+    } else {
+        if (t < 16) {
+            uint32_t row = row0 + t;
+            if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
+                if (p.bias) v = v + p.bias[row];
+                p.y[row] = v;
+            } else if (EPI == EPI_ADD) {
+                if (p.bias) v = v + p.bias[row];
+                p.y[row] = p.y[row] + v;
             }
-            if (t == 0) atomicMax(p.argmax64, key);
+        }
+        if (EPI == EPI_ARGMAX) {
+            // first index of the maximum within the tile (cpu.zig:477-483), then a
+            // packed 64-bit max across tiles: larger value wins, then smaller index.
+            if (t < 32) {
+                unsigned long long key = t < 16 ? pack_argmax(v, row0 + t) : 0ull;
+#pragma unroll
+                for (int o = 8; o > 0; o >>= 1) {
+                    unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                    key = other > key ? other : key;
+                }
+                if (t == 0) atomicMax(p.argmax64, key);
+            }
         }
     }
+    if (p.post.op == POST_NONE) return;
+    // Grid completion: the CTA that finishes the last tile runs the post-op.
+    __threadfence();
+    __syncthreads();
+    if (t == 0) {
+        unsigned int prev = atomicAdd(p.post.done, 1u);
+        is_last = (prev == gridDim.x - 1u);
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    if (p.post.op == POST_RMSNORM) {
+        rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
+    } else if (p.post.op == POST_FINISH) {
+        if (t == 0) finish_step(p.post.state, p.post.forced, p.post.out_tokens);
+    }
+    if (t == 0) *p.post.done = 0u;
 }
 
 template <class TT>
@@ -540,15 +595,21 @@ int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
     k.ws = a.ws;
     k.counters = a.counters;
     k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
+    k.post = a.post;
     dim3 grid(a.w->rows / 16, k.ksplit);
+    const size_t smem = 0;
+    cudaError_t e;
     switch (epi) {
-    case EPI_STORE: gemv_kernel<TT, EPI_STORE><<<grid, 128, 0, s>>>(k); break;
-    case EPI_ADD: gemv_kernel<TT, EPI_ADD><<<grid, 128, 0, s>>>(k); break;
-    case EPI_SILU_XQ: gemv_kernel<TT, EPI_SILU_XQ><<<grid, 128, 0, s>>>(k); break;
-    case EPI_ARGMAX: gemv_kernel<TT, EPI_ARGMAX><<<grid, 128, 0, s>>>(k); break;
+    case EPI_STORE: e = launch_maybe_pdl(gemv_kernel<TT, EPI_STORE>, grid, dim3(128), smem, s, a.pdl, k); break;
+    case EPI_ADD: e = launch_maybe_pdl(gemv_kernel<TT, EPI_ADD>, grid, dim3(128), smem, s, a.pdl, k); break;
+    case EPI_SILU_XQ: e = launch_maybe_pdl(gemv_kernel<TT, EPI_SILU_XQ>, grid, dim3(128), smem, s, a.pdl, k); break;
+    case EPI_ARGMAX: e = launch_maybe_pdl(gemv_kernel<TT, EPI_ARGMAX>, grid, dim3(128), smem, s, a.pdl, k); break;
     default: set_error("bad epilogue %d", epi); return CUQ_EINVAL;
     }
-    CUQ_CUDA_TRY(cudaGetLastError());
+    if (e != cudaSuccess) {
+        set_error("gemv launch: %s", cudaGetErrorString(e));
+        return CUQ_ECUDA;
+    }
     return CUQ_OK;
 }
 
@@ -559,6 +620,9 @@ __global__ void to_xq_kernel(const float *__restrict__ x, uint32_t n, uint32_t x
     const uint32_t v = blockIdx.y;
     const float *xv = x + (size_t)v * x_stride;
     __half *o = xq + (size_t)v * vec_stride;
+    float *sums = xq_sums(o, kpad);
+    // launched with exactly kpad threads per vector (kpad % 256 == 0): one
+    // column each, and 16 consecutive columns in each aligned group of 16 lanes
     for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < kpad; i += gridDim.x * blockDim.x) {
         float f = i < n ? xv[i] : 0.f;
         __half hi = __float2half_rn(f);
@@ -566,57 +630,20 @@ __global__ void to_xq_kernel(const float *__restrict__ x, uint32_t n, uint32_t x
         uint32_t pos = xq_pos(i);
         o[pos] = hi;
         o[kpad + pos] = lo;
-    }
-    float *sums = xq_sums(o, kpad);
-    for (uint32_t u = blockIdx.x * blockDim.x + threadIdx.x; u < kpad / 16; u += gridDim.x * blockDim.x) {
-        float acc = 0.f;
-        for (uint32_t j = 16 * u; j < 16 * u + 16; j++) acc += j < n ? xv[j] : 0.f;
-        sums[u] = acc;
+        float a = f;
+#pragma unroll
+        for (int o2 = 1; o2 < 16; o2 <<= 1) a += __shfl_xor_sync(0xffffffffu, a, o2);
+        if ((i & 15u) == 0) sums[i >> 4] = a;
     }
 }
 
 // One CTA per row: cpu.rmsnorm (cpu.zig:11-18), then the xq split.
 __global__ void rmsnorm_xq_kernel(const float *__restrict__ x, const float *__restrict__ w, uint32_t n, float eps,
                                   __half *__restrict__ xq, uint32_t kpad, size_t vec_stride, float *h_out) {
-    const float *xr = x + (size_t)blockIdx.x * n;
-    __half *o = xq + (size_t)blockIdx.x * vec_stride;
-    __shared__ float part[32];
-    float acc = 0.f;
-    for (uint32_t i = threadIdx.x; i < n; i += blockDim.x) {
-        float v = xr[i];
-        acc += v * v;
-    }
-#pragma unroll
-    for (int o2 = 16; o2 > 0; o2 >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
-    if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = acc;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float s = threadIdx.x < (blockDim.x >> 5) ? part[threadIdx.x] : 0.f;
-#pragma unroll
-        for (int o2 = 16; o2 > 0; o2 >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o2);
-        if (threadIdx.x == 0) part[0] = s;
-    }
-    __syncthreads();
-    const float mean = part[0] / (float)n;
-    const float inv = 1.0f / sqrtf(mean + eps);
-    for (uint32_t i = threadIdx.x; i < kpad; i += blockDim.x) {
-        float f = 0.f;
-        if (i < n) {
-            f = (xr[i] * inv) * w[i];
-            if (h_out) h_out[(size_t)blockIdx.x * n + i] = f;
-        }
-        __half hi = __float2half_rn(f);
-        __half lo = __float2half_rn(f - __half2float(hi));
-        uint32_t pos = xq_pos(i);
-        o[pos] = hi;
-        o[kpad + pos] = lo;
-    }
-    float *sums = xq_sums(o, kpad);
-    for (uint32_t u = threadIdx.x; u < kpad / 16; u += blockDim.x) {
-        float acc = 0.f;
-        for (uint32_t j = 16 * u; j < 16 * u + 16 && j < n; j++) acc += (xr[j] * inv) * w[j];
-        sums[u] = acc;
-    }
+    griddep_wait();
+    griddep_launch();
+    rmsnorm_xq_block(x + (size_t)blockIdx.x * n, w, n, eps, xq + (size_t)blockIdx.x * vec_stride, kpad,
+                     h_out ? h_out + (size_t)blockIdx.x * n : nullptr);
 }
 
 }  // namespace

@@ -1,14 +1,19 @@
 // model.cu -- the engine: Engine.init / forward / prefill / reset (src/engine.zig)
 // and Session.generate's greedy loop (src/generate.zig:166-250), device-resident.
 //
-// A decode step is one fixed launch sequence (captured once in a CUDA graph):
-//   embed row -> per layer [rmsnorm->xq, qkv GEMV(+bias), RoPE + fp16 KV write,
-//   split attention + combine->xq, o GEMV (+= residual), rmsnorm->xq,
-//   gate|up GEMV with SiLU*mul epilogue->xq, down GEMV (+= residual)] ->
-//   final rmsnorm->xq, lm_head GEMV with fused argmax -> finish kernel.
-// The step reads its token and position from device memory and the finish
-// kernel writes the next ones, so consecutive steps (a prompt fed token by
-// token, then greedy decoding) replay the graph with no host round-trip.
+// A decode step is one fixed launch sequence (captured once in a CUDA graph),
+// 2 + 5 launches per layer:
+//   embed row + RMSNorm -> per layer [qkv GEMV (+bias);
+//   attention (RoPE, fp16 KV write, split softmax, combine -> xq);
+//   o GEMV (+= residual, last CTA: ffn RMSNorm -> xq);
+//   gate|up GEMV with the SiLU*mul epilogue -> xq;
+//   down GEMV (+= residual, last CTA: next RMSNorm -> xq)] ->
+//   lm_head GEMV with the fused argmax (last CTA: next token).
+// Every launch is a programmatic dependent of the one before: a GEMV starts
+// streaming its weights while its predecessor finishes, then waits for the
+// activation (griddepcontrol.wait).  The step reads its token and position from
+// device memory and writes the next ones, so consecutive steps (a prompt fed
+// token by token, then greedy decoding) replay the graph with no host round-trip.
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -74,120 +79,97 @@ int build_proj(Proj &out, std::vector<PendingTensor *> parts, cudaStream_t s) {
     return rc;
 }
 
-__global__ void finish_step_kernel(StepState *st, const uint32_t *forced, uint32_t *out_tokens) {
-    unsigned long long a = st->argmax64;
-    uint32_t idx = 0xFFFFFFFFu - (uint32_t)(a & 0xFFFFFFFFull);
-    st->argmax64 = 0ull;
-    int s = st->step;
-    out_tokens[s] = idx;
-    st->step = s + 1;
-    st->pos = st->pos + 1;
-    st->token = (s + 1 < st->n_forced) ? (int)forced[s + 1] : (int)idx;
-}
-
 }  // namespace
 
 static int enqueue_step(cuq_model *m) {
     const cuq_config &c = m->cfg;
     cudaStream_t s = m->stream;
-    const int *pos_ptr = &m->state->pos;
-    const uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    const bool pdl = true;  // every launch below waits for its predecessor with griddepcontrol.wait
     int rc;
-    uint64_t nk = 0;  // kernel launches in the step (each launcher below enqueues one, attention two)
+    uint64_t nk = 0;  // kernel launches in the step
 #define TRY(x)                       \
     do {                             \
         rc = (x);                    \
         if (rc != CUQ_OK) return rc; \
         nk++;                        \
     } while (0)
-    TRY(launch_embed_row(m->embed.p, &m->state->token, m->x, s));
+    auto gemv = [&](const Planes &w, const __half *xq, float *y, const float *bias, int epi) {
+        GemvArgs a;
+        a.w = &w;
+        a.xq = xq;
+        a.y = y;
+        a.bias = bias;
+        a.ws = m->ws;
+        a.counters = m->counters;
+        a.ksplit = gemv_pick_ksplit(w, m->sm_count);
+        a.pdl = pdl;
+        a.post.done = m->done;
+        return a;
+    };
+    // engine.zig:561-564 embedding, then layer 0's attention RMSNorm
+    TRY(launch_embed_norm(m->embed.p, m->state, m->x, m->layers[0].attn_norm, c.hidden, c.eps, m->xq_h, pdl, s));
     for (uint32_t l = 0; l < c.layers; l++) {
         Layer &L = m->layers[l];
-        // attention half (main.zig:434-485 / engine.zig:569-620)
-        TRY(launch_rmsnorm_xq(m->x, L.attn_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, s));
+        // qkv projection + bias (main.zig:435-436)
         for (auto &seg : L.qkv) {
-            GemvArgs a;
-            a.w = &seg.p;
-            a.xq = m->xq_h;
-            a.y = m->qkv + seg.row_off;
-            a.bias = L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr;
-            a.ws = m->ws;
-            a.counters = m->counters;
-            a.ksplit = gemv_pick_ksplit(seg.p, m->sm_count);
+            GemvArgs a = gemv(seg.p, m->xq_h, m->qkv + seg.row_off, L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr,
+                              EPI_STORE);
             TRY(launch_gemv(a, EPI_STORE, s));
         }
-        TRY(launch_rope_cache(m->qkv, qd + 2 * kvd, m->q_rot, L.k_cache, L.v_cache, m->opt.max_seq, m->rope_cs,
-                              pos_ptr, 0, 1, c.heads, c.kv_heads, c.head_dim, c.rope_adjacent, s));
-        TRY(launch_attention_decode(m->q_rot, L.k_cache, L.v_cache, m->opt.max_seq, pos_ptr, 0, c.heads, c.kv_heads,
-                                    c.head_dim, m->attn_part, m->attn_nsplit, nullptr, m->xq_attn, s));
+        // RoPE + fp16 KV write + attention (main.zig:457-472)
+        TRY(launch_attention_step(m->qkv, m->rope_cs, m->state, L.k_cache, L.v_cache, m->opt.max_seq, c.heads,
+                                  c.kv_heads, c.head_dim, c.rope_adjacent, m->attn_part, m->attn_nsplit, m->tickets,
+                                  m->xq_attn, pdl, s));
+        // o projection + o_bias into the residual (main.zig:477-485), then ffn RMSNorm (main.zig:487)
         {
-            GemvArgs a;
-            a.w = &L.o.p;
-            a.xq = m->xq_attn;
-            a.y = m->x;
-            a.bias = L.o_bias;
-            a.ws = m->ws;
-            a.counters = m->counters;
-            a.ksplit = gemv_pick_ksplit(L.o.p, m->sm_count);
+            GemvArgs a = gemv(L.o.p, m->xq_attn, m->x, L.o_bias, EPI_ADD);
+            a.post.op = POST_RMSNORM;
+            a.post.x = m->x;
+            a.post.w = L.ffn_norm;
+            a.post.n = c.hidden;
+            a.post.eps = c.eps;
+            a.post.xq = m->xq_h;
             TRY(launch_gemv(a, EPI_ADD, s));
         }
-        // feed-forward half (engine.zig:622-700, split path with cpu.gateMul)
-        TRY(launch_rmsnorm_xq(m->x, L.ffn_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, s));
+        // gate/up with the SiLU*mul epilogue (engine.zig:645-668 split path)
         if (L.gate_up_dual) {
-            GemvArgs a;
-            a.w = &L.gate.p;
+            GemvArgs a = gemv(L.gate.p, m->xq_h, nullptr, nullptr, EPI_SILU_XQ);
             a.w2 = &L.up.p;
-            a.xq = m->xq_h;
-            a.y = nullptr;
             a.xq_out = m->xq_act;
-            a.ws = m->ws;
-            a.counters = m->counters;
-            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count);
             TRY(launch_gemv(a, EPI_SILU_XQ, s));
         } else {
-            GemvArgs a;
-            a.xq = m->xq_h;
-            a.ws = m->ws;
-            a.counters = m->counters;
-            a.w = &L.gate.p;
-            a.y = m->gate_buf;
-            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count);
+            GemvArgs a = gemv(L.gate.p, m->xq_h, m->gate_buf, nullptr, EPI_STORE);
             TRY(launch_gemv(a, EPI_STORE, s));
-            a.w = &L.up.p;
-            a.y = m->up_buf;
-            a.ksplit = gemv_pick_ksplit(L.up.p, m->sm_count);
+            a = gemv(L.up.p, m->xq_h, m->up_buf, nullptr, EPI_STORE);
             TRY(launch_gemv(a, EPI_STORE, s));
             TRY(launch_silu_mul(m->act, m->gate_buf, m->up_buf, c.inter, s));
             TRY(launch_to_xq(m->act, c.inter, 1, c.inter, m->xq_act, s));
         }
+        // down projection into the residual, then the next RMSNorm (next layer's
+        // attention norm, or the final norm before the lm_head, main.zig:532)
         {
-            GemvArgs a;
-            a.w = &L.down.p;
-            a.xq = m->xq_act;
-            a.y = m->x;
-            a.ws = m->ws;
-            a.counters = m->counters;
-            a.ksplit = gemv_pick_ksplit(L.down.p, m->sm_count);
+            GemvArgs a = gemv(L.down.p, m->xq_act, m->x, nullptr, EPI_ADD);
+            a.post.op = POST_RMSNORM;
+            a.post.x = m->x;
+            a.post.w = l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm;
+            a.post.n = c.hidden;
+            a.post.eps = c.eps;
+            a.post.xq = m->xq_h;
             TRY(launch_gemv(a, EPI_ADD, s));
         }
     }
-    // final norm + lm_head (main.zig:532-534, engine.zig:865-900) with the argmax fused
-    TRY(launch_rmsnorm_xq(m->x, m->final_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, s));
+    // lm_head with the fused argmax (main.zig:534, cpu.zig:477-483); the last CTA
+    // turns the argmax into the next step's token (generate.zig:217-244).
     {
         const Proj &head = c.tie_embeddings ? m->embed : m->output;
-        GemvArgs a;
-        a.w = &head.p;
-        a.xq = m->xq_h;
-        a.y = m->logits;
+        GemvArgs a = gemv(head.p, m->xq_h, m->logits, nullptr, EPI_ARGMAX);
         a.argmax64 = &m->state->argmax64;
-        a.ws = m->ws;
-        a.counters = m->counters;
-        a.ksplit = gemv_pick_ksplit(head.p, m->sm_count);
+        a.post.op = POST_FINISH;
+        a.post.state = m->state;
+        a.post.forced = m->forced;
+        a.post.out_tokens = m->out_tokens;
         TRY(launch_gemv(a, EPI_ARGMAX, s));
     }
-    finish_step_kernel<<<1, 1, 0, s>>>(m->state, m->forced, m->out_tokens);
-    CUQ_CUDA_TRY(cudaGetLastError());
-    nk += 1 + c.layers;  // finish kernel + the combine launch inside each attention
     m->stats.kernels_per_step = nk;
 #undef TRY
     return CUQ_OK;
@@ -269,6 +251,10 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
         build_rope_table(cs.data(), o.max_seq, c.head_dim, c.rope_theta);
         if (cudaMalloc(&m->rope_cs, sizeof(float) * cs.size()) != cudaSuccess) break;
         if (cudaMemcpy(m->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice) != cudaSuccess) break;
+        if (cudaMalloc(&m->done, sizeof(unsigned int)) != cudaSuccess) break;
+        if (cudaMalloc(&m->tickets, sizeof(unsigned int) * c.kv_heads) != cudaSuccess) break;
+        cudaMemset(m->done, 0, sizeof(unsigned int));
+        cudaMemset(m->tickets, 0, sizeof(unsigned int) * c.kv_heads);
         if (cudaMalloc(&m->state, sizeof(StepState)) != cudaSuccess) break;
         cudaMemset(m->state, 0, sizeof(StepState));
         if (cudaMallocHost(&m->state_host, sizeof(StepState)) != cudaSuccess) break;
@@ -671,7 +657,7 @@ void cuq_model_free(cuq_model *m) {
     free_planes(m->output.p);
     void *bufs[] = {m->final_norm, m->x,      m->qkv,  m->q_rot,   m->logits,     m->attn_part, m->act,
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
-                    m->counters,   m->state,  m->forced, m->out_tokens};
+                    m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (m->state_host) cudaFreeHost(m->state_host);

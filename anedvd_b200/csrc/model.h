@@ -30,15 +30,6 @@ struct Layer {
     __half *k_cache = nullptr, *v_cache = nullptr;  // [kv_heads][max_seq][head_dim]
 };
 
-// Device-side step state, read and advanced by the graph itself.
-struct StepState {
-    int token;      // token fed to the next step
-    int pos;        // its position
-    int step;       // steps run since the last reset of `step`
-    int n_forced;   // steps whose next token comes from forced[] (prompt ids)
-    unsigned long long argmax64;  // packed (value, index) max of the lm_head
-};
-
 }  // namespace cuq
 
 struct cuq_model {
@@ -59,6 +50,8 @@ struct cuq_model {
     float *rope_cs = nullptr;                    // [max_seq][head_dim]
     float *ws = nullptr;                         // split-K partials
     unsigned int *counters = nullptr;
+    unsigned int *done = nullptr;                // GEMV grid-completion counter (post-ops)
+    unsigned int *tickets = nullptr;             // attention combine tickets, one per KV head
     size_t ws_floats = 0, n_counters = 0;
     int attn_nsplit = 1;
     cuq::StepState *state = nullptr;             // device

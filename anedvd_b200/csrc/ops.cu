@@ -10,8 +10,6 @@ namespace cuq {
 
 namespace {
 
-__device__ __forceinline__ uint32_t xq_pos(uint32_t i) { return (i & ~3u) | ((i & 1u) << 1) | ((i >> 1) & 1u); }
-
 // -------------------------------------------------------------- RMSNorm ---
 // cpu.rmsnorm (cpu.zig:11-18): one CTA per row.
 __global__ void rmsnorm_kernel(float *out, const float *__restrict__ x, const float *__restrict__ w, uint32_t n,
@@ -269,6 +267,213 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, int nsplit, 
     }
 }
 
+// ---------------------------------------------------- fused decode attention
+// One decode step's attention for one layer, in one launch (engine.zig:595-612
+// + ropeAndCache 952-970 + cpu.attentionDecode 323-395):
+//   * every CTA rotates its KV group's queries from the qkv vector itself
+//     (RoPE from the host-built cos|sin table, cpu.zig:22-62);
+//   * the CTA whose split holds the step's position rotates k, rounds k and v
+//     to fp16 and writes them into the cache before it reads that position;
+//   * splits run the online softmax as attn_decode_kernel does;
+//   * the last split CTA of each KV group to finish (atomic ticket) merges the
+//     group's splits and writes the o projection's xq input directly.
+struct AttnStepArgs {
+    const float *qkv;            // [q | k | v] after bias
+    const float *cs;             // [max_seq][hd] cos | sin
+    const StepState *state;      // pos
+    __half *k_cache, *v_cache;   // [kv_heads][cache_stride][hd]
+    uint32_t cache_stride, heads, kv_heads;
+    int adjacent, nsplit;
+    float *part;                 // [nsplit][heads][hd + 2]
+    unsigned int *tickets;       // [kv_heads], self-resetting
+    __half *xq;                  // o-projection input (heads*hd columns)
+};
+
+template <int HD>
+__device__ __forceinline__ float rope_elem(const float *v, uint32_t d, const float *csr, int adjacent) {
+    // rotated element d of one head vector `v` (cpu.zig:33-36 / 57-60)
+    constexpr uint32_t half = HD / 2;
+    if (adjacent) {
+        uint32_t j = d >> 1;
+        float a = v[2 * j], b = v[2 * j + 1], c = csr[j], s = csr[half + j];
+        return (d & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
+    }
+    uint32_t i = d < half ? d : d - half;
+    float a = v[i], b = v[i + half], c = csr[i], s = csr[half + i];
+    return d < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(128) attn_step_kernel(const AttnStepArgs p) {
+    constexpr int E = 8, LPP = HD / E, PPW = 32 / LPP;
+    griddep_wait();
+    griddep_launch();
+    const uint32_t kvh = blockIdx.x, split = blockIdx.y;
+    const uint32_t pos = (uint32_t)p.state->pos, n = pos + 1u;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lp = lane % LPP, pg = lane / LPP;
+    uint32_t chunk = (n + p.nsplit - 1) / p.nsplit;
+    chunk = (chunk + 15u) & ~15u;
+    const uint32_t p0 = split * chunk, p1 = min(n, p0 + chunk);
+    const float scale = 1.0f / sqrtf((float)HD);
+    const uint32_t qd = p.heads * HD, kvd = p.kv_heads * HD;
+    const float *csr = p.cs + (size_t)pos * HD;
+    __half *kh = p.k_cache + (size_t)kvh * p.cache_stride * HD;
+    __half *vh = p.v_cache + (size_t)kvh * p.cache_stride * HD;
+
+    if (pos >= p0 && pos < p1) {  // this CTA owns the new position: write its K/V row
+        const float *kin = p.qkv + qd + (size_t)kvh * HD;
+        const float *vin = p.qkv + qd + kvd + (size_t)kvh * HD;
+        for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
+            kh[(size_t)pos * HD + d] = __float2half_rn(rope_elem<HD>(kin, d, csr, p.adjacent));
+            vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
+        }
+        __threadfence_block();
+    }
+    float qr[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        const float *qh = p.qkv + (size_t)(kvh * G + g) * HD;
+#pragma unroll
+        for (int e = 0; e < E; e++) qr[g][e] = rope_elem<HD>(qh, lp * E + e, csr, p.adjacent);
+    }
+    __syncthreads();  // the K/V row written above is read below
+
+    float m[G], l[G], o[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; e++) o[g][e] = 0.f;
+    }
+    for (uint32_t pb = p0 + warp * PPW; pb < p1; pb += 4 * PPW) {  // warp-uniform bound
+        const uint32_t pp = pb + pg;
+        const bool valid = pp < p1;
+        float kf[E], vf[E];
+        uint4 ku = make_uint4(0u, 0u, 0u, 0u), vu = make_uint4(0u, 0u, 0u, 0u);
+        if (valid) {
+            ku = *reinterpret_cast<const uint4 *>(kh + (size_t)pp * HD + lp * E);
+            vu = *reinterpret_cast<const uint4 *>(vh + (size_t)pp * HD + lp * E);
+        }
+        const __half2 *k2 = reinterpret_cast<const __half2 *>(&ku);
+        const __half2 *v2 = reinterpret_cast<const __half2 *>(&vu);
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            float2 kk = __half22float2(k2[j]), vv = __half22float2(v2[j]);
+            kf[2 * j] = kk.x;
+            kf[2 * j + 1] = kk.y;
+            vf[2 * j] = vv.x;
+            vf[2 * j + 1] = vv.y;
+        }
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            float d = 0.f;
+#pragma unroll
+            for (int e = 0; e < E; e++) d = fmaf(qr[g][e], kf[e], d);
+#pragma unroll
+            for (int sh = 1; sh < LPP; sh <<= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
+            if (valid) {
+                float s = d * scale;
+                float mn = fmaxf(m[g], s);
+                float corr = expf(m[g] - mn);
+                float pe = expf(s - mn);
+                l[g] = l[g] * corr + pe;
+#pragma unroll
+                for (int e = 0; e < E; e++) o[g][e] = o[g][e] * corr + pe * vf[e];
+                m[g] = mn;
+            }
+        }
+    }
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+#pragma unroll
+        for (int sh = LPP; sh < 32; sh <<= 1) {
+            float mo = __shfl_xor_sync(0xffffffffu, m[g], sh);
+            float lo = __shfl_xor_sync(0xffffffffu, l[g], sh);
+            float mn = fmaxf(m[g], mo);
+            float ca = mn == -INFINITY ? 0.f : expf(m[g] - mn);
+            float cb = mn == -INFINITY ? 0.f : expf(mo - mn);
+            l[g] = l[g] * ca + lo * cb;
+#pragma unroll
+            for (int e = 0; e < E; e++) {
+                float oo = __shfl_xor_sync(0xffffffffu, o[g][e], sh);
+                o[g][e] = o[g][e] * ca + oo * cb;
+            }
+            m[g] = mn;
+        }
+    }
+    __shared__ float sm_m[4][G], sm_l[4][G], sm_o[4][G][HD];
+    if (pg == 0) {
+#pragma unroll
+        for (int g = 0; g < G; g++) {
+            if (lp == 0) {
+                sm_m[warp][g] = m[g];
+                sm_l[warp][g] = l[g];
+            }
+#pragma unroll
+            for (int e = 0; e < E; e++) sm_o[warp][g][lp * E + e] = o[g][e];
+        }
+    }
+    __syncthreads();
+    const size_t stride = HD + 2;
+    for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
+        int g = t / HD, dd = t % HD;
+        float mm = fmaxf(fmaxf(sm_m[0][g], sm_m[1][g]), fmaxf(sm_m[2][g], sm_m[3][g]));
+        float acc = 0.f, ll = 0.f;
+#pragma unroll
+        for (int w = 0; w < 4; w++) {
+            float c = mm == -INFINITY ? 0.f : expf(sm_m[w][g] - mm);
+            acc += sm_o[w][g][dd] * c;
+            ll += sm_l[w][g] * c;
+        }
+        float *pp = p.part + ((size_t)split * p.heads + kvh * G + g) * stride;
+        pp[dd] = acc;
+        if (dd == 0) {
+            pp[HD] = mm;
+            pp[HD + 1] = ll;
+        }
+    }
+    // the last split of this KV group merges the group's heads
+    __shared__ int is_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(&p.tickets[kvh], 1u) == (unsigned)p.nsplit - 1u;
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    const uint32_t kpad = xq_pad(qd);
+    __shared__ float res[G * HD];
+    for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
+        int g = t / HD, dd = t % HD;
+        uint32_t h = kvh * G + g;
+        float M = -INFINITY;
+        for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, __ldcg(p.part + ((size_t)s * p.heads + h) * stride + HD));
+        float acc = 0.f, L = 0.f;
+        for (int s = 0; s < p.nsplit; s++) {
+            const float *pp = p.part + ((size_t)s * p.heads + h) * stride;
+            float ms = __ldcg(pp + HD);
+            float c = ms == -INFINITY ? 0.f : expf(ms - M);
+            acc += __ldcg(pp + dd) * c;
+            L += __ldcg(pp + HD + 1) * c;
+        }
+        float r = acc / L;
+        uint32_t i = h * HD + dd;
+        __half hi = __float2half_rn(r);
+        __half lo = __float2half_rn(r - __half2float(hi));
+        p.xq[xq_pos(i)] = hi;
+        p.xq[kpad + xq_pos(i)] = lo;
+        res[t] = r;
+    }
+    __syncthreads();
+    for (int u = threadIdx.x; u < G * HD / 16; u += blockDim.x) {  // per-16 sums (HD % 16 == 0)
+        float a = 0.f;
+        for (int j = 0; j < 16; j++) a += res[16 * u + j];
+        xq_sums(p.xq, kpad)[(kvh * G * HD) / 16 + u] = a;
+    }
+    if (threadIdx.x == 0) p.tickets[kvh] = 0u;
+}
+
 // --------------------------------------------------------------- others ---
 
 __global__ void silu_mul_kernel(float *out, const float *g, const float *u, uint32_t n) {
@@ -369,6 +574,35 @@ int launch_attention_decode(const float *q, const __half *k_cache, const __half 
     CUQ_CUDA_TRY(cudaGetLastError());
     attn_combine_kernel<<<heads, hd, 0, s>>>(part, nsplit, heads, hd, out, xq, xq ? xq_pad(heads * hd) : 0);
     CUQ_CUDA_TRY(cudaGetLastError());
+    return CUQ_OK;
+}
+
+int launch_attention_step(const float *qkv, const float *cs, const StepState *state, __half *k_cache,
+                          __half *v_cache, uint32_t cache_stride, uint32_t heads, uint32_t kv_heads, uint32_t hd,
+                          int adjacent, float *part, int nsplit, unsigned int *tickets, __half *xq, bool pdl,
+                          cudaStream_t s) {
+    if (kv_heads == 0 || heads % kv_heads) {
+        set_error("attention: heads (%u) must be a multiple of kv_heads (%u)", heads, kv_heads);
+        return CUQ_EINVAL;
+    }
+    AttnStepArgs a{qkv, cs, state, k_cache, v_cache, cache_stride, heads, kv_heads, adjacent, nsplit, part, tickets,
+                   xq};
+    uint32_t G = heads / kv_heads;
+    dim3 grid(kv_heads, nsplit);
+    cudaError_t e = cudaErrorInvalidValue;
+#define CUQ_ATS(HDV, GV) \
+    if (hd == HDV && G == GV) e = launch_maybe_pdl(attn_step_kernel<HDV, GV>, grid, dim3(128), 0, s, pdl, a); else
+    CUQ_ATS(64, 1) CUQ_ATS(64, 2) CUQ_ATS(64, 3) CUQ_ATS(64, 4) CUQ_ATS(64, 6) CUQ_ATS(64, 7) CUQ_ATS(64, 8)
+    CUQ_ATS(128, 1) CUQ_ATS(128, 2) CUQ_ATS(128, 3) CUQ_ATS(128, 4) CUQ_ATS(128, 6) CUQ_ATS(128, 7)
+    CUQ_ATS(128, 8) {
+        set_error("attention: unsupported head_dim %u / group %u (head_dim 64 or 128, group 1-8)", hd, G);
+        return CUQ_EUNSUPPORTED;
+    }
+#undef CUQ_ATS
+    if (e != cudaSuccess) {
+        set_error("attention launch: %s", cudaGetErrorString(e));
+        return CUQ_ECUDA;
+    }
     return CUQ_OK;
 }
 

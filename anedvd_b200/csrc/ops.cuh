@@ -16,6 +16,15 @@ int attn_pick_nsplit(uint32_t kv_heads, uint32_t max_seq, int sm_count);
 int launch_attention_decode(const float *q, const __half *k_cache, const __half *v_cache, uint32_t cache_stride,
                             const int *pos_ptr, uint32_t n_val, uint32_t heads, uint32_t kv_heads, uint32_t hd,
                             float *part, int nsplit, float *out, __half *xq, cudaStream_t s);
+// The decode step's fused attention (RoPE, KV write, split attention, combine -> xq).
+// tickets: kv_heads counters, zero-initialised once (self-resetting).
+int launch_attention_step(const float *qkv, const float *cs, const StepState *state, __half *k_cache,
+                          __half *v_cache, uint32_t cache_stride, uint32_t heads, uint32_t kv_heads, uint32_t hd,
+                          int adjacent, float *part, int nsplit, unsigned int *tickets, __half *xq, bool pdl,
+                          cudaStream_t s);
+// Embedding row + the first layer's RMSNorm -> xq, one CTA (decode step start).
+int launch_embed_norm(const Planes &p, const StepState *state, float *x, const float *norm_w, uint32_t n, float eps,
+                      __half *xq, bool pdl, cudaStream_t s);
 int launch_silu_mul(float *out, const float *g, const float *u, uint32_t n, cudaStream_t s);
 int launch_argmax(const float *v, uint32_t n, uint32_t *out, cudaStream_t s);
 // Embedding row (token from *token_ptr): x = f32(RN16(dequant(row))) (load_gguf.zig:578-647 + engine.zig:561-564).
