@@ -260,6 +260,18 @@ __global__ void embed_norm_kernel(PlanesView p, const StepState *__restrict__ st
     rmsnorm_xq_block(x, nw, n, eps, xq, xq_pad(n), nullptr);
 }
 
+// Prefill: embedding rows of ids[0..n) into x[n][cols], one CTA per token.
+__global__ void embed_rows_kernel(PlanesView p, const uint32_t *__restrict__ ids, float *__restrict__ x, int epb) {
+    const uint32_t r = ids[blockIdx.x];
+    float *xr = x + (size_t)blockIdx.x * p.cols;
+    if (r >= p.rows) return;
+    uint8_t blk[212];
+    for (uint32_t b = threadIdx.x; b < p.cols / epb; b += blockDim.x) {
+        block_move(p, blk, r, b, 1);
+        for (int j = 0; j < epb; j++) xr[(size_t)b * epb + j] = __half2float(__float2half_rn(dq_elem(p.type, blk, j)));
+    }
+}
+
 PlanesView view(const Planes &p) {
     return PlanesView{p.type, p.rows, p.cols, p.base, p.off_q, p.off_q2, p.off_s, p.off_s2};
 }
@@ -364,6 +376,13 @@ int launch_embed_norm(const Planes &p, const StepState *state, float *x, const f
         set_error("embed launch: %s", cudaGetErrorString(e));
         return CUQ_ECUDA;
     }
+    return CUQ_OK;
+}
+
+int launch_embed_rows(const Planes &p, const uint32_t *ids, uint32_t n, float *x, cudaStream_t s) {
+    if (n == 0) return CUQ_OK;
+    embed_rows_kernel<<<n, 128, 0, s>>>(view(p), ids, x, block_elems(p.type));
+    CUQ_CUDA_TRY(cudaGetLastError());
     return CUQ_OK;
 }
 

@@ -1,9 +1,7 @@
-// gemm.cu -- cuq_gemm, the prefill projection Y[n][rows] = X[n][cols] W^T.
-//
-// First version: each token is a batch-1 GEMV over the quantized planes (the
-// weight is re-streamed per token).  Correct, and the reference for the
-// tensor-core prefill path that replaces it.
+// gemm.cu -- cuq_gemm, the prefill projection Y[n][rows] = X[n][cols] W^T, on
+// the tcgen05 tensor-core kernel (qgemm_tc.cu).
 #include "common.cuh"
+#include "qgemm.cuh"
 
 struct cuq_weight;
 
@@ -25,20 +23,36 @@ extern "C" int cuq_gemm(const cuq_weight *w, const float *x_dev, uint32_t n, flo
     }
     if (n == 0) return CUQ_OK;
     cudaStream_t s = (cudaStream_t)stream;
-    size_t kp = xq_halves(p->cols);
-    __half *xq = nullptr;
-    CUQ_CUDA_TRY(cudaMallocAsync(&xq, sizeof(__half) * kp * n, s));
-    int rc = launch_to_xq(x_dev, p->cols, n, p->cols, xq, s);
-    for (uint32_t t = 0; rc == CUQ_OK && t < n; t++) {
-        GemvArgs a;
-        a.w = p;
-        a.xq = xq + kp * t;
-        a.y = y_dev + (size_t)t * p->rows;
-        a.ws = ws;
-        a.counters = ctr;
-        a.ksplit = ksplit;
-        rc = launch_gemv(a, EPI_STORE, s);
+    size_t cnt = (size_t)n * p->cols;
+    __half *xh = nullptr;
+    int *err = nullptr;
+    CUQ_CUDA_TRY(cudaMallocAsync(&xh, sizeof(__half) * 2 * cnt + 16, s));
+    CUQ_CUDA_TRY(cudaMallocAsync(&err, sizeof(int), s));
+    CUQ_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
+    int rc = launch_split_hilo(x_dev, cnt, xh, xh + cnt, s);
+    if (rc == CUQ_OK) {
+        QgemmArgs g;
+        g.w = p;
+        g.xh = xh;
+        g.xl = xh + cnt;
+        g.n = n;
+        g.y = y_dev;
+        g.err = err;
+        rc = launch_qgemm(g, EPI_STORE, s);
     }
-    cudaFreeAsync(xq, s);
+    int herr = 0;
+    if (rc == CUQ_OK) {
+        cudaError_t e = cudaMemcpyAsync(&herr, err, sizeof(int), cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) {
+            set_error("cuq_gemm: %s", cudaGetErrorString(e));
+            rc = CUQ_ECUDA;
+        } else if (herr) {
+            set_error("cuq_gemm: a tensor-core pipeline wait timed out");
+            rc = CUQ_ETIMEOUT;
+        }
+    }
+    cudaFreeAsync(xh, s);
+    cudaFreeAsync(err, s);
     return rc;
 }

@@ -20,6 +20,7 @@
 
 #include "model.h"
 #include "ops.cuh"
+#include "qgemm.cuh"
 
 using namespace cuq;
 
@@ -188,6 +189,158 @@ static int run_steps(cuq_model *m, uint32_t n) {
     return CUQ_OK;
 }
 
+// The lm_head over the residual row `x_row` (final RMSNorm first), with the
+// argmax and the step-finish post-op (main.zig:532-534, generate.zig:217-244).
+static int enqueue_head(cuq_model *m, const float *x_row, bool pdl) {
+    const cuq_config &c = m->cfg;
+    int rc = launch_rmsnorm_xq(x_row, m->final_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, m->stream);
+    if (rc) return rc;
+    const Proj &head = c.tie_embeddings ? m->embed : m->output;
+    GemvArgs a;
+    a.w = &head.p;
+    a.xq = m->xq_h;
+    a.y = m->logits;
+    a.argmax64 = &m->state->argmax64;
+    a.ws = m->ws;
+    a.counters = m->counters;
+    a.ksplit = gemv_pick_ksplit(head.p, m->sm_count);
+    a.pdl = pdl;
+    a.post.done = m->done;
+    a.post.op = POST_FINISH;
+    a.post.state = m->state;
+    a.post.forced = m->forced;
+    a.post.out_tokens = m->out_tokens;
+    return launch_gemv(a, EPI_ARGMAX, m->stream);
+}
+
+// Engine.prefill for one chunk of n <= max_chunk prompt positions starting at
+// pos0 (ids already on the device): every projection is one tensor-core GEMM
+// over the chunk, attention is causal over the cache.  When `last` is set the
+// chunk's final position goes through the lm_head and sets the decode state.
+static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint32_t pos0, bool last) {
+    const cuq_config &c = m->cfg;
+    cudaStream_t s = m->stream;
+    const uint32_t qd = q_dim(c), kvd = kv_dim(c), qkvd = qd + 2 * kvd;
+    int rc;
+#define PTRY(x)                      \
+    do {                             \
+        rc = (x);                    \
+        if (rc != CUQ_OK) return rc; \
+    } while (0)
+    PTRY(launch_embed_rows(m->embed.p, ids_dev, n, m->pf_x, s));
+    for (uint32_t l = 0; l < c.layers; l++) {
+        Layer &L = m->layers[l];
+        PTRY(launch_rmsnorm_hilo(m->pf_x, L.attn_norm, c.hidden, n, c.eps, m->pf_h, m->pf_l, s));
+        for (auto &seg : L.qkv) {
+            QgemmArgs g;
+            g.w = &seg.p;
+            g.xh = m->pf_h;
+            g.xl = m->pf_l;
+            g.n = n;
+            g.y = m->pf_qkv + seg.row_off;
+            g.ldy = qkvd;
+            g.bias = L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr;
+            g.err = m->gemm_err;
+            PTRY(launch_qgemm(g, EPI_STORE, s));
+        }
+        PTRY(launch_rope_cache(m->pf_qkv, qkvd, m->pf_q, L.k_cache, L.v_cache, m->opt.max_seq, m->rope_cs, nullptr,
+                               pos0, n, c.heads, c.kv_heads, c.head_dim, c.rope_adjacent, s));
+        PTRY(launch_attention_prefill(m->pf_q, L.k_cache, L.v_cache, m->opt.max_seq, pos0, n, c.heads, c.kv_heads,
+                                      c.head_dim, m->pf_h, m->pf_l, s));
+        {
+            QgemmArgs g;
+            g.w = &L.o.p;
+            g.xh = m->pf_h;
+            g.xl = m->pf_l;
+            g.n = n;
+            g.y = m->pf_x;
+            g.ldy = c.hidden;
+            g.bias = L.o_bias;
+            g.err = m->gemm_err;
+            PTRY(launch_qgemm(g, EPI_ADD, s));
+        }
+        PTRY(launch_rmsnorm_hilo(m->pf_x, L.ffn_norm, c.hidden, n, c.eps, m->pf_h, m->pf_l, s));
+        if (L.gate_up_dual) {
+            QgemmArgs g;
+            g.w = &L.gate.p;
+            g.w2 = &L.up.p;
+            g.xh = m->pf_h;
+            g.xl = m->pf_l;
+            g.n = n;
+            g.oh = m->pf_ah;
+            g.ol = m->pf_al;
+            g.err = m->gemm_err;
+            PTRY(launch_qgemm(g, EPI_SILU_XQ, s));
+        } else {
+            QgemmArgs g;
+            g.xh = m->pf_h;
+            g.xl = m->pf_l;
+            g.n = n;
+            g.err = m->gemm_err;
+            g.w = &L.gate.p;
+            g.y = m->pf_g;
+            PTRY(launch_qgemm(g, EPI_STORE, s));
+            g.w = &L.up.p;
+            g.y = m->pf_u;
+            PTRY(launch_qgemm(g, EPI_STORE, s));
+            PTRY(launch_silu_hilo(m->pf_g, m->pf_u, (size_t)n * c.inter, m->pf_ah, m->pf_al, s));
+        }
+        {
+            QgemmArgs g;
+            g.w = &L.down.p;
+            g.xh = m->pf_ah;
+            g.xl = m->pf_al;
+            g.n = n;
+            g.y = m->pf_x;
+            g.ldy = c.hidden;
+            g.err = m->gemm_err;
+            PTRY(launch_qgemm(g, EPI_ADD, s));
+        }
+    }
+    if (last) PTRY(enqueue_head(m, m->pf_x + (size_t)(n - 1) * c.hidden, false));
+#undef PTRY
+    return CUQ_OK;
+}
+
+static int set_state(cuq_model *m, int token, int pos, int n_forced) {
+    m->state_host->token = token;
+    m->state_host->pos = pos;
+    m->state_host->step = 0;
+    m->state_host->n_forced = n_forced;
+    m->state_host->argmax64 = 0ull;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->state, m->state_host, sizeof(StepState), cudaMemcpyHostToDevice, m->stream));
+    return CUQ_OK;
+}
+
+
+// Prefill ids[0..n) at start_pos in chunks; leaves the state ready for decoding
+// (token = argmax of the last position, pos = start_pos + n, step = 1,
+// out_tokens[0] = that argmax).
+static int prefill_batched(cuq_model *m, const uint32_t *ids, uint32_t n, uint32_t start_pos) {
+    int rc;
+    const uint32_t C = m->opt.max_chunk;
+    for (uint32_t off = 0; off < n; off += C) {
+        const uint32_t cn = n - off < C ? n - off : C;
+        const bool last = off + cn == n;
+        CUQ_CUDA_TRY(cudaMemcpyAsync(m->pf_ids, ids + off, sizeof(uint32_t) * cn, cudaMemcpyHostToDevice, m->stream));
+        if (last && (rc = set_state(m, 0, (int)(start_pos + off + cn - 1), 1))) return rc;
+        if ((rc = prefill_chunk(m, m->pf_ids, cn, start_pos + off, last))) return rc;
+        if (!last) CUQ_CUDA_TRY(cudaStreamSynchronize(m->stream));  // pf_ids is reused by the next chunk
+    }
+    return CUQ_OK;
+}
+
+static int check_gemm_err(cuq_model *m) {
+    int herr = 0;
+    CUQ_CUDA_TRY(cudaMemcpy(&herr, m->gemm_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (herr) {
+        cudaMemset(m->gemm_err, 0, sizeof(int));
+        set_error("prefill: a tensor-core pipeline wait timed out");
+        return CUQ_ETIMEOUT;
+    }
+    return CUQ_OK;
+}
+
 extern "C" {
 
 cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
@@ -261,6 +414,22 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
         if (cudaMalloc(&m->forced, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
         if (cudaMalloc(&m->out_tokens, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
         if (cudaMallocHost(&m->out_host, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
+        {
+            const size_t C = o.max_chunk;
+            const size_t wide = c.hidden > qd ? c.hidden : qd;
+            if (cudaMalloc(&m->pf_x, sizeof(float) * C * c.hidden) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_qkv, sizeof(float) * C * (qd + 2 * kvd)) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_q, sizeof(float) * C * qd) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_g, sizeof(float) * C * c.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_u, sizeof(float) * C * c.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_h, sizeof(__half) * C * wide) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_l, sizeof(__half) * C * wide) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_ah, sizeof(__half) * C * c.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_al, sizeof(__half) * C * c.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_ids, sizeof(uint32_t) * C) != cudaSuccess) break;
+            if (cudaMalloc(&m->gemm_err, sizeof(int)) != cudaSuccess) break;
+            cudaMemset(m->gemm_err, 0, sizeof(int));
+        }
         if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess) break;
         ok = true;
     } while (0);
@@ -485,16 +654,6 @@ int cuq_model_get_config(const cuq_model *m, cuq_config *out) {
     return CUQ_OK;
 }
 
-static int set_state(cuq_model *m, int token, int pos, int n_forced) {
-    m->state_host->token = token;
-    m->state_host->pos = pos;
-    m->state_host->step = 0;
-    m->state_host->n_forced = n_forced;
-    m->state_host->argmax64 = 0ull;
-    CUQ_CUDA_TRY(cudaMemcpyAsync(m->state, m->state_host, sizeof(StepState), cudaMemcpyHostToDevice, m->stream));
-    return CUQ_OK;
-}
-
 static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint32_t *argmax_out, double *ms_out) {
     CUQ_CUDA_TRY(cudaEventRecord(m->ev1, m->stream));
     if (logits_host)
@@ -554,12 +713,17 @@ int cuq_prefill(cuq_model *m, const uint32_t *ids, uint32_t n, uint32_t start_po
     int rc;
     for (uint32_t i = 0; i < n; i++)
         if ((rc = check_token(m, ids[i]))) return rc;
-    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids, sizeof(uint32_t) * n, cudaMemcpyHostToDevice, m->stream));
-    if ((rc = set_state(m, (int)ids[0], (int)start_pos, (int)n))) return rc;
     CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
-    if ((rc = run_steps(m, n))) return rc;
+    if (n == 1) {  // a single position is one decode step
+        CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids, sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+        if ((rc = set_state(m, (int)ids[0], (int)start_pos, 1))) return rc;
+        if ((rc = run_steps(m, 1))) return rc;
+    } else if ((rc = prefill_batched(m, ids, n, start_pos))) {
+        return rc;
+    }
     m->stats.prefill_tokens += n;
-    return finish_call(m, n, logits_host, argmax_out, &m->stats.prefill_ms);
+    if ((rc = finish_call(m, 1, logits_host, argmax_out, &m->stats.prefill_ms))) return rc;
+    return check_gemm_err(m);
 }
 
 int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_decode, uint32_t *out_tokens) {
@@ -577,15 +741,21 @@ int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t 
     int rc;
     for (uint32_t i = 0; i < n_prompt; i++)
         if ((rc = check_token(m, ids[i]))) return rc;
-    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids, sizeof(uint32_t) * n_prompt, cudaMemcpyHostToDevice, m->stream));
-    if ((rc = set_state(m, (int)ids[0], 0, (int)n_prompt))) return rc;
     CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
-    if ((rc = run_steps(m, steps))) return rc;
+    if (n_prompt == 1) {
+        CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids, sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+        if ((rc = set_state(m, (int)ids[0], 0, 1))) return rc;
+        if ((rc = run_steps(m, 1))) return rc;
+    } else if ((rc = prefill_batched(m, ids, n_prompt, 0))) {
+        return rc;
+    }
+    // the prefill left token = first generated id, step = 1: decode the rest on the device
+    if ((rc = run_steps(m, n_decode - 1))) return rc;
     m->stats.prefill_tokens += n_prompt;
     m->stats.tokens += n_decode;
-    if ((rc = finish_call(m, steps, nullptr, nullptr, &m->stats.decode_ms))) return rc;
-    memcpy(out_tokens, m->out_host + (n_prompt - 1), sizeof(uint32_t) * n_decode);
-    return CUQ_OK;
+    if ((rc = finish_call(m, n_decode, nullptr, nullptr, &m->stats.decode_ms))) return rc;
+    memcpy(out_tokens, m->out_host, sizeof(uint32_t) * n_decode);
+    return check_gemm_err(m);
 }
 
 int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps, uint32_t *out_tokens) {
@@ -657,7 +827,9 @@ void cuq_model_free(cuq_model *m) {
     free_planes(m->output.p);
     void *bufs[] = {m->final_norm, m->x,      m->qkv,  m->q_rot,   m->logits,     m->attn_part, m->act,
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
-                    m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets};
+                    m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets,
+                    m->pf_x,       m->pf_qkv, m->pf_q, m->pf_g, m->pf_u, m->pf_h, m->pf_l, m->pf_ah, m->pf_al,
+                    m->pf_ids,     m->gemm_err};
     for (void *b : bufs)
         if (b) cudaFree(b);
     if (m->state_host) cudaFreeHost(m->state_host);

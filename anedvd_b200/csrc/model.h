@@ -59,6 +59,12 @@ struct cuq_model {
     uint32_t *forced = nullptr, *out_tokens = nullptr;  // device, [max_seq]
     uint32_t *out_host = nullptr;                // pinned [max_seq]
 
+    // batched prefill (chunks of opt.max_chunk tokens)
+    float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_g = nullptr, *pf_u = nullptr;
+    __half *pf_h = nullptr, *pf_l = nullptr, *pf_ah = nullptr, *pf_al = nullptr;
+    uint32_t *pf_ids = nullptr;
+    int *gemm_err = nullptr;
+
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;
     cudaEvent_t ev0 = nullptr, ev1 = nullptr;

@@ -25,6 +25,16 @@ int launch_attention_step(const float *qkv, const float *cs, const StepState *st
 // Embedding row + the first layer's RMSNorm -> xq, one CTA (decode step start).
 int launch_embed_norm(const Planes &p, const StepState *state, float *x, const float *norm_w, uint32_t n, float eps,
                       __half *xq, bool pdl, cudaStream_t s);
+// Prefill: RMSNorm rows -> fp16 hi/lo; causal attention for n_q prompt positions
+// starting at pos0 (K/V already in the cache) -> hi/lo; SiLU*mul -> hi/lo;
+// embedding rows of ids[0..n) -> x[n][hidden].
+int launch_rmsnorm_hilo(const float *x, const float *w, uint32_t n, uint32_t n_rows, float eps, __half *hi,
+                        __half *lo, cudaStream_t s);
+int launch_attention_prefill(const float *q, const __half *k_cache, const __half *v_cache, uint32_t cache_stride,
+                             uint32_t pos0, uint32_t n_q, uint32_t heads, uint32_t kv_heads, uint32_t hd,
+                             __half *oh, __half *ol, cudaStream_t s);
+int launch_silu_hilo(const float *g, const float *u, size_t count, __half *hi, __half *lo, cudaStream_t s);
+int launch_embed_rows(const Planes &p, const uint32_t *ids, uint32_t n, float *x, cudaStream_t s);
 int launch_silu_mul(float *out, const float *g, const float *u, uint32_t n, cudaStream_t s);
 int launch_argmax(const float *v, uint32_t n, uint32_t *out, cudaStream_t s);
 // Embedding row (token from *token_ptr): x = f32(RN16(dequant(row))) (load_gguf.zig:578-647 + engine.zig:561-564).

@@ -28,10 +28,10 @@ class Engine:
         self.cfg = cfg  # CuqConfig
 
     @classmethod
-    def from_gguf(cls, path, max_seq=2048, use_graphs=True, device=0):
+    def from_gguf(cls, path, max_seq=2048, use_graphs=True, device=0, max_chunk=512):
         L = rt.load()
         rt.init(device)
-        opts = rt.CuqOptions(max_seq=max_seq, max_chunk=512, use_graphs=int(use_graphs), tp_rank=0, tp_size=1)
+        opts = rt.CuqOptions(max_seq=max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs), tp_rank=0, tp_size=1)
         h = L.cuq_model_load_gguf(path.encode(), ctypes.byref(opts))
         if not h:
             raise rt.CuqError(rt.EINVAL, rt.last_error())
@@ -40,7 +40,7 @@ class Engine:
         return cls(h, cfg)
 
     @classmethod
-    def from_synth(cls, model, max_seq=None, use_graphs=True, device=0):
+    def from_synth(cls, model, max_seq=None, use_graphs=True, device=0, max_chunk=512):
         """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads)."""
         L = rt.load()
         rt.init(device)
@@ -48,8 +48,8 @@ class Engine:
         cfg = rt.CuqConfig(hidden=c.hidden, layers=c.layers, heads=c.heads, kv_heads=c.kv_heads,
                            head_dim=c.head_dim, inter=c.inter, vocab=c.vocab, eps=c.eps, rope_theta=c.rope_theta,
                            rope_adjacent=int(c.rope_adjacent), tie_embeddings=int(c.tie_embeddings))
-        opts = rt.CuqOptions(max_seq=max_seq or c.max_seq, max_chunk=512, use_graphs=int(use_graphs), tp_rank=0,
-                             tp_size=1)
+        opts = rt.CuqOptions(max_seq=max_seq or c.max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs),
+                             tp_rank=0, tp_size=1)
         h = L.cuq_model_create(ctypes.byref(cfg), ctypes.byref(opts))
         if not h:
             raise rt.CuqError(rt.EINVAL, rt.last_error())

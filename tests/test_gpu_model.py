@@ -32,11 +32,11 @@ def _margin_ok(logits, tol):
     return (top[1] - top[0]) > tol * np.max(np.abs(logits))
 
 
-def _compare(model, n_prompt, n_decode, threads=8, use_graphs=True):
+def _compare(model, n_prompt, n_decode, threads=8, use_graphs=True, max_chunk=512):
     cfg = model.cfg
     ref = orc.Model(cfg, threads=threads, max_seq=n_prompt + n_decode + 1)
     ref.load(model)
-    eng = E.Engine.from_synth(model, max_seq=n_prompt + n_decode + 1, use_graphs=use_graphs)
+    eng = E.Engine.from_synth(model, max_seq=n_prompt + n_decode + 1, use_graphs=use_graphs, max_chunk=max_chunk)
     ids = _prompt(cfg, n_prompt)
     errs = []
     # prefill: the reference's CPU path feeds the prompt token by token (main.zig:1255-1262)
@@ -70,6 +70,32 @@ def test_smollm2_full_size_matches_reference():
     """BASELINE config 2 at full size (30 layers, vocab 49152), 16-token prompt."""
     e = _compare(synth.model("smollm2-135m"), n_prompt=16, n_decode=8)
     assert e < LOGIT_TOL, e
+
+
+@pytest.mark.parametrize("chunk", [1, 4, 7])
+def test_chunked_prefill_matches_reference(chunk):
+    """The prompt split into several tensor-core chunks (the last one ragged)."""
+    e = _compare(synth.model("qwen2.5-0.5b", layers=2, vocab=1024), n_prompt=11, n_decode=3, max_chunk=chunk)
+    assert e < LOGIT_TOL, e
+
+
+def test_batched_prefill_cache_feeds_decode():
+    """A prefill at start_pos > 0 after an earlier one: the KV cache rows written by
+    the batched path are the ones the decode step reads."""
+    m = synth.model("smollm2-135m", layers=2, vocab=1024)
+    ref = orc.Model(m.cfg, threads=8, max_seq=32)
+    ref.load(m)
+    eng = E.Engine.from_synth(m, max_seq=32, max_chunk=8)
+    a, b = _prompt(m.cfg, 6, 1), _prompt(m.cfg, 9, 2)
+    eng.prefill(a, 0)
+    got, _ = eng.prefill(b, len(a))
+    for p, t in enumerate(np.concatenate([a, b])):
+        want = ref.forward(int(t), p)
+    assert rel_err(got, want) < LOGIT_TOL
+    got, _ = eng.forward(7, len(a) + len(b))
+    want = ref.forward(7, len(a) + len(b))
+    assert rel_err(got, want) < LOGIT_TOL
+    eng.close()
 
 
 def test_graph_and_eager_agree():
