@@ -97,87 +97,112 @@ __global__ void rope_cache_kernel(const float *__restrict__ qkv, uint32_t qkv_st
 }
 
 // ------------------------------------------------------------ attention ---
-// cpu.attentionDecode (cpu.zig:323-395) as split-position flash decoding: CTA
-// (kv head, split) covers a contiguous position range for all query heads of
-// that KV group (GQA: query head h reads KV head h / (heads / kv_heads)).
-// hd/8 lanes share one position (8 dims each, one 16-byte K and V load); a warp
-// walks 32/(hd/8) positions at a time with an online softmax; partial (m, l, o)
-// go to `part` and the combine kernel merges the splits.  Scores are dot(q, k) * (1 / sqrt(hd)) in fp32.
-template <int HD, int G>
-__global__ void __launch_bounds__(128) attn_decode_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
-                                                           const __half *__restrict__ vc, uint32_t cache_stride,
-                                                           const int *pos_ptr, uint32_t n_val, uint32_t heads,
-                                                           uint32_t kv_heads, float *part, int nsplit) {
-    constexpr int E = 8;            // dims per lane: one 16-byte load of K and of V
-    constexpr int LPP = HD / E;     // lanes per position (8 at hd 64, 16 at hd 128)
-    constexpr int PPW = 32 / LPP;   // positions a warp walks at once
-    const uint32_t kvh = blockIdx.x, split = blockIdx.y;
-    const uint32_t n = pos_ptr ? (uint32_t)(*pos_ptr) + 1u : n_val;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int lp = lane % LPP, pg = lane / LPP;
-    uint32_t chunk = (n + nsplit - 1) / nsplit;
+// cpu.attentionDecode (cpu.zig:323-395) as split-position flash decoding.  CTA
+// (kv head, split) covers a contiguous range of cache positions for every query
+// head of that KV group (GQA: query head h reads KV head h / (heads / kv_heads)).
+// hd/8 lanes share one position (8 dims each: one 16-byte K and V load); a warp
+// walks U * 32/(hd/8) positions per iteration with all their loads issued before
+// the math, and keeps an online softmax (m, l, o).  Scores are dot(q, k) *
+// (1 / sqrt(hd)) in fp32.  Splits write partial (o, m, l) to `part`:
+//   part[s][h][hd] (unnormalised o), then at part + nsplit*heads*hd: [s][h][2] (m, l).
+// Splits cover at least ATT_MIN_CHUNK positions, so a short context uses few
+// splits and the merge reads few partials.
+constexpr uint32_t ATT_MIN_CHUNK = 32;
+constexpr int ATT_MAX_SPLIT = 64;
+
+struct SplitRange {
+    uint32_t p0, p1, nact;
+};
+
+__device__ __forceinline__ SplitRange split_range(uint32_t n, int nsplit, uint32_t split) {
+    uint32_t chunk = (n + (uint32_t)nsplit - 1) / (uint32_t)nsplit;
     chunk = (chunk + 15u) & ~15u;
-    const uint32_t p0 = split * chunk, p1 = min(n, p0 + chunk);
+    if (chunk < ATT_MIN_CHUNK) chunk = ATT_MIN_CHUNK;
+    SplitRange r;
+    r.nact = (n + chunk - 1) / chunk;
+    r.p0 = split * chunk;
+    r.p1 = min(n, r.p0 + chunk);
+    return r;
+}
+
+// Walk positions [p0, p1) of one KV head with this CTA's 4 warps.  Warp-uniform
+// loop bound: every lane reaches every shuffle; lanes past the end load zeros
+// and score -inf.
+template <int HD, int G>
+__device__ __forceinline__ void attn_walk(const float (&qr)[G][8], const __half *kh, const __half *vh, uint32_t p0,
+                                          uint32_t p1, int warp, int lp, int pg, float (&m)[G], float (&l)[G],
+                                          float (&o)[G][8]) {
+    constexpr int E = 8, LPP = HD / E, PPW = 32 / LPP, U = G <= 4 ? 4 : 2;
     const float scale = 1.0f / sqrtf((float)HD);
-
-    float qr[G][E];
+    for (uint32_t pb = p0 + (uint32_t)warp * PPW * U; pb < p1; pb += 4u * PPW * U) {
+        uint4 ku[U], vu[U];
 #pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int e = 0; e < E; e++) qr[g][e] = q[(size_t)(kvh * G + g) * HD + lp * E + e];
-
-    float m[G], l[G], o[G][E];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; e++) o[g][e] = 0.f;
-    }
-    const __half *kh = kc + (size_t)kvh * cache_stride * HD;
-    const __half *vh = vc + (size_t)kvh * cache_stride * HD;
-    // The loop bound depends only on the warp, so every lane reaches every
-    // shuffle below; lanes whose position is past the end compute on zeros and
-    // skip the softmax update.
-    for (uint32_t pb = p0 + warp * PPW; pb < p1; pb += 4 * PPW) {
-        const uint32_t p = pb + pg;
-        const bool valid = p < p1;
-        float kf[E], vf[E];
-        uint4 ku = make_uint4(0u, 0u, 0u, 0u), vu = make_uint4(0u, 0u, 0u, 0u);
-        if (valid) {
-            ku = *reinterpret_cast<const uint4 *>(kh + (size_t)p * HD + lp * E);
-            vu = *reinterpret_cast<const uint4 *>(vh + (size_t)p * HD + lp * E);
+        for (int u = 0; u < U; u++) {
+            const uint32_t p = pb + u * PPW + pg;
+            ku[u] = make_uint4(0u, 0u, 0u, 0u);
+            vu[u] = ku[u];
+            if (p < p1) {
+                ku[u] = *reinterpret_cast<const uint4 *>(kh + (size_t)p * HD + lp * E);
+                vu[u] = *reinterpret_cast<const uint4 *>(vh + (size_t)p * HD + lp * E);
+            }
         }
-        const __half2 *k2 = reinterpret_cast<const __half2 *>(&ku);
-        const __half2 *v2 = reinterpret_cast<const __half2 *>(&vu);
+        float s[U][G];
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-            float2 kk = __half22float2(k2[j]), vv = __half22float2(v2[j]);
-            kf[2 * j] = kk.x;
-            kf[2 * j + 1] = kk.y;
-            vf[2 * j] = vv.x;
-            vf[2 * j + 1] = vv.y;
+        for (int u = 0; u < U; u++) {
+            const __half2 *k2 = reinterpret_cast<const __half2 *>(&ku[u]);
+            float kf[E];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                float2 kk = __half22float2(k2[j]);
+                kf[2 * j] = kk.x;
+                kf[2 * j + 1] = kk.y;
+            }
+            const bool valid = pb + u * PPW + pg < p1;
+#pragma unroll
+            for (int g = 0; g < G; g++) {
+                float d = 0.f;
+#pragma unroll
+                for (int e = 0; e < E; e++) d = fmaf(qr[g][e], kf[e], d);
+#pragma unroll
+                for (int sh = 1; sh < LPP; sh <<= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
+                s[u][g] = valid ? d * scale : -INFINITY;
+            }
         }
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float d = 0.f;
+            float mx = s[0][g];
 #pragma unroll
-            for (int e = 0; e < E; e++) d = fmaf(qr[g][e], kf[e], d);
+            for (int u = 1; u < U; u++) mx = fmaxf(mx, s[u][g]);
+            const float mn = fmaxf(m[g], mx);
+            if (mn == -INFINITY) continue;  // nothing valid yet (no shuffles below)
+            const float corr = expf(m[g] - mn);
+            l[g] *= corr;
 #pragma unroll
-            for (int sh = 1; sh < LPP; sh <<= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
-            if (valid) {  // no shuffles inside: divergence here is harmless
-                float s = d * scale;
-                float mn = fmaxf(m[g], s);
-                float corr = expf(m[g] - mn);  // exp(-inf) = 0 on the first position
-                float pe = expf(s - mn);
-                l[g] = l[g] * corr + pe;
+            for (int e = 0; e < E; e++) o[g][e] *= corr;
 #pragma unroll
-                for (int e = 0; e < E; e++) o[g][e] = o[g][e] * corr + pe * vf[e];
-                m[g] = mn;
+            for (int u = 0; u < U; u++) {
+                const float pe = expf(s[u][g] - mn);  // 0 for an invalid lane
+                const __half2 *v2 = reinterpret_cast<const __half2 *>(&vu[u]);
+                l[g] += pe;
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    float2 vv = __half22float2(v2[j]);
+                    o[g][2 * j] = fmaf(pe, vv.x, o[g][2 * j]);
+                    o[g][2 * j + 1] = fmaf(pe, vv.y, o[g][2 * j + 1]);
+                }
             }
+            m[g] = mn;
         }
     }
-    // merge the position groups of the warp (lanes lp, lp + LPP, ...)
+}
+
+// Merge the lanes of each warp and the CTA's 4 warps; write the split's partial
+// (o, m, l) for query heads kvh*G .. kvh*G+G-1.
+template <int HD, int G>
+__device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], float (&o)[G][8], int warp, int lp,
+                                                 int pg, float *part, uint32_t split, int nsplit, uint32_t heads,
+                                                 uint32_t kvh) {
+    constexpr int E = 8, LPP = HD / E;
 #pragma unroll
     for (int g = 0; g < G; g++) {
 #pragma unroll
@@ -196,7 +221,6 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float *__restric
             m[g] = mn;
         }
     }
-    // merge the 4 warps through shared memory
     __shared__ float sm_m[4][G], sm_l[4][G], sm_o[4][G][HD];
     if (pg == 0) {
 #pragma unroll
@@ -210,61 +234,149 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float *__restric
         }
     }
     __syncthreads();
-    const size_t stride = HD + 2;
+    float *po = part + ((size_t)split * heads + kvh * G) * HD;
+    float *pml = part + (size_t)nsplit * heads * HD + ((size_t)split * heads + kvh * G) * 2;
     for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
-        int g = t / HD, dd = t % HD;
-        float mm = fmaxf(fmaxf(sm_m[0][g], sm_m[1][g]), fmaxf(sm_m[2][g], sm_m[3][g]));
+        const int g = t / HD, dd = t % HD;
+        const float mm = fmaxf(fmaxf(sm_m[0][g], sm_m[1][g]), fmaxf(sm_m[2][g], sm_m[3][g]));
         float acc = 0.f, ll = 0.f;
 #pragma unroll
         for (int w = 0; w < 4; w++) {
-            float c = mm == -INFINITY ? 0.f : expf(sm_m[w][g] - mm);
+            const float c = mm == -INFINITY ? 0.f : expf(sm_m[w][g] - mm);
             acc += sm_o[w][g][dd] * c;
             ll += sm_l[w][g] * c;
         }
-        float *pp = part + ((size_t)split * heads + kvh * G + g) * stride;
-        pp[dd] = acc;
+        po[t] = acc;
         if (dd == 0) {
-            pp[HD] = mm;
-            pp[HD + 1] = ll;
+            pml[2 * g] = mm;
+            pml[2 * g + 1] = ll;
         }
     }
 }
 
-// Merge the splits: out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.
-__global__ void attn_combine_kernel(const float *__restrict__ part, int nsplit, uint32_t heads, uint32_t hd,
-                                    float *out, __half *xq, uint32_t kpad) {
-    const uint32_t h = blockIdx.x;
-    const size_t stride = hd + 2;
-    __shared__ float res[128];  // hd <= 128
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; s++) M = fmaxf(M, part[((size_t)s * heads + h) * stride + hd]);
-    for (uint32_t d = threadIdx.x; d < hd; d += blockDim.x) {
-        float acc = 0.f, L = 0.f;
-        for (int s = 0; s < nsplit; s++) {
-            const float *pp = part + ((size_t)s * heads + h) * stride;
-            float c = pp[hd] == -INFINITY ? 0.f : expf(pp[hd] - M);
-            acc += pp[d] * c;
-            L += pp[hd + 1] * c;
+// Merge the nact splits of query heads h0 .. h0+NH-1 (one CTA, any size):
+// out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.  Every split's weight is
+// computed once into shared memory, then each thread sums float4 columns with
+// independent loads.  `res` receives the NH*HD results.
+template <int HD, int NH>
+__device__ __forceinline__ void attn_merge(const float *part, int nsplit, uint32_t nact, uint32_t heads, uint32_t h0,
+                                           float *res) {
+    __shared__ float cw[ATT_MAX_SPLIT][NH];
+    __shared__ float inv_l[NH];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const float *pml = part + (size_t)nsplit * heads * HD;
+    for (int g = warp; g < NH; g += nw) {
+        const uint32_t h = h0 + g;
+        float ms[2], ls[2];
+        float M = -INFINITY;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const uint32_t s = lane + 32 * j;
+            ms[j] = s < nact ? __ldcg(pml + ((size_t)s * heads + h) * 2) : -INFINITY;
+            ls[j] = s < nact ? __ldcg(pml + ((size_t)s * heads + h) * 2 + 1) : 0.f;
+            M = fmaxf(M, ms[j]);
         }
-        float r = acc / L;
-        uint32_t i = h * hd + d;
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
+        float L = 0.f;
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const uint32_t s = lane + 32 * j;
+            const float c = ms[j] == -INFINITY ? 0.f : expf(ms[j] - M);
+            if (s < nact) cw[s][g] = c;
+            L += ls[j] * c;
+        }
+#pragma unroll
+        for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
+        if (lane == 0) inv_l[g] = 1.0f / L;
+    }
+    __syncthreads();
+    for (int t = threadIdx.x; t < NH * HD / 4; t += blockDim.x) {
+        const int g = t / (HD / 4), d4 = t % (HD / 4);
+        const float4 *src = reinterpret_cast<const float4 *>(part + (size_t)(h0 + g) * HD) + d4;
+        const size_t sstride = (size_t)heads * HD / 4;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+        for (uint32_t s = 0; s < nact; s++) {
+            const float4 v = __ldcg(src + s * sstride);
+            const float c = cw[s][g];
+            acc.x = fmaf(v.x, c, acc.x);
+            acc.y = fmaf(v.y, c, acc.y);
+            acc.z = fmaf(v.z, c, acc.z);
+            acc.w = fmaf(v.w, c, acc.w);
+        }
+        const float il = inv_l[g];
+        res[4 * t] = acc.x * il;
+        res[4 * t + 1] = acc.y * il;
+        res[4 * t + 2] = acc.z * il;
+        res[4 * t + 3] = acc.w * il;
+    }
+    __syncthreads();
+}
+
+// Write merged head outputs as the o projection's xq input (hi/lo + per-16 sums)
+// and/or fp32.  `res` holds NH*HD values for columns c0 .. c0+NH*HD-1.
+__device__ __forceinline__ void attn_emit(const float *res, uint32_t count, uint32_t c0, float *out, __half *xq,
+                                          uint32_t kpad) {
+    for (uint32_t t = threadIdx.x; t < count; t += blockDim.x) {
+        const float r = res[t];
+        const uint32_t i = c0 + t;
         if (out) out[i] = r;
         if (xq) {
-            __half hi = __float2half_rn(r);
-            __half lo = __float2half_rn(r - __half2float(hi));
+            const __half hi = __float2half_rn(r);
             xq[xq_pos(i)] = hi;
-            xq[kpad + xq_pos(i)] = lo;
-        }
-        if (d < 128) res[d] = r;
-    }
-    if (xq) {  // per-16 sums of this head's outputs (hd is a multiple of 16)
-        __syncthreads();
-        for (uint32_t u = threadIdx.x; u < hd / 16; u += blockDim.x) {
-            float acc = 0.f;
-            for (int j = 0; j < 16; j++) acc += res[16 * u + j];
-            xq_sums(xq, kpad)[(h * hd) / 16 + u] = acc;
+            xq[kpad + xq_pos(i)] = __float2half_rn(r - __half2float(hi));
         }
     }
+    if (xq) {  // c0 and count are multiples of 16
+        for (uint32_t u = threadIdx.x; u < count / 16; u += blockDim.x) {
+            float a = 0.f;
+            for (int j = 0; j < 16; j++) a += res[16 * u + j];
+            xq_sums(xq, kpad)[c0 / 16 + u] = a;
+        }
+    }
+}
+
+template <int HD, int G>
+__global__ void __launch_bounds__(128) attn_decode_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
+                                                           const __half *__restrict__ vc, uint32_t cache_stride,
+                                                           const int *pos_ptr, uint32_t n_val, uint32_t heads,
+                                                           float *part, int nsplit) {
+    constexpr int E = 8, LPP = HD / E;
+    const uint32_t kvh = blockIdx.x, split = blockIdx.y;
+    const uint32_t n = pos_ptr ? (uint32_t)(*pos_ptr) + 1u : n_val;
+    const SplitRange r = split_range(n, nsplit, split);
+    if (split >= r.nact) return;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int lp = lane % LPP, pg = lane / LPP;
+    float qr[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++)
+#pragma unroll
+        for (int e = 0; e < E; e++) qr[g][e] = q[(size_t)(kvh * G + g) * HD + lp * E + e];
+    float m[G], l[G], o[G][E];
+#pragma unroll
+    for (int g = 0; g < G; g++) {
+        m[g] = -INFINITY;
+        l[g] = 0.f;
+#pragma unroll
+        for (int e = 0; e < E; e++) o[g][e] = 0.f;
+    }
+    attn_walk<HD, G>(qr, kc + (size_t)kvh * cache_stride * HD, vc + (size_t)kvh * cache_stride * HD, r.p0, r.p1,
+                     warp, lp, pg, m, l, o);
+    attn_store_split<HD, G>(m, l, o, warp, lp, pg, part, split, nsplit, heads, kvh);
+}
+
+// Merge for the standalone decode attention: CTA per query head.
+template <int HD>
+__global__ void __launch_bounds__(128) attn_combine_kernel(const float *__restrict__ part, int nsplit,
+                                                            const int *pos_ptr, uint32_t n_val, uint32_t heads,
+                                                            float *out, __half *xq, uint32_t kpad) {
+    __shared__ float res[HD];
+    const uint32_t n = pos_ptr ? (uint32_t)(*pos_ptr) + 1u : n_val;
+    const SplitRange r = split_range(n, nsplit, 0);
+    attn_merge<HD, 1>(part, nsplit, r.nact, heads, blockIdx.x, res);
+    attn_emit(res, HD, blockIdx.x * HD, out, xq, kpad);
 }
 
 // ---------------------------------------------------- fused decode attention
@@ -274,7 +386,7 @@ __global__ void attn_combine_kernel(const float *__restrict__ part, int nsplit, 
 //     (RoPE from the host-built cos|sin table, cpu.zig:22-62);
 //   * the CTA whose split holds the step's position rotates k, rounds k and v
 //     to fp16 and writes them into the cache before it reads that position;
-//   * splits run the online softmax as attn_decode_kernel does;
+//   * splits run attn_walk as attn_decode_kernel does;
 //   * the last split CTA of each KV group to finish (atomic ticket) merges the
 //     group's splits and writes the o projection's xq input directly.
 struct AttnStepArgs {
@@ -284,7 +396,7 @@ struct AttnStepArgs {
     __half *k_cache, *v_cache;   // [kv_heads][cache_stride][hd]
     uint32_t cache_stride, heads, kv_heads;
     int adjacent, nsplit;
-    float *part;                 // [nsplit][heads][hd + 2]
+    float *part;                 // nsplit * heads * (hd + 2) floats
     unsigned int *tickets;       // [kv_heads], self-resetting
     __half *xq;                  // o-projection input (heads*hd columns)
 };
@@ -305,136 +417,48 @@ __device__ __forceinline__ float rope_elem(const float *v, uint32_t d, const flo
 
 template <int HD, int G>
 __global__ void __launch_bounds__(128) attn_step_kernel(const AttnStepArgs p) {
-    constexpr int E = 8, LPP = HD / E, PPW = 32 / LPP;
+    constexpr int E = 8, LPP = HD / E;
     griddep_wait();
     griddep_launch();
     const uint32_t kvh = blockIdx.x, split = blockIdx.y;
     const uint32_t pos = (uint32_t)p.state->pos, n = pos + 1u;
+    const SplitRange r = split_range(n, p.nsplit, split);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int lp = lane % LPP, pg = lane / LPP;
-    uint32_t chunk = (n + p.nsplit - 1) / p.nsplit;
-    chunk = (chunk + 15u) & ~15u;
-    const uint32_t p0 = split * chunk, p1 = min(n, p0 + chunk);
-    const float scale = 1.0f / sqrtf((float)HD);
     const uint32_t qd = p.heads * HD, kvd = p.kv_heads * HD;
     const float *csr = p.cs + (size_t)pos * HD;
     __half *kh = p.k_cache + (size_t)kvh * p.cache_stride * HD;
     __half *vh = p.v_cache + (size_t)kvh * p.cache_stride * HD;
 
-    if (pos >= p0 && pos < p1) {  // this CTA owns the new position: write its K/V row
-        const float *kin = p.qkv + qd + (size_t)kvh * HD;
-        const float *vin = p.qkv + qd + kvd + (size_t)kvh * HD;
-        for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
-            kh[(size_t)pos * HD + d] = __float2half_rn(rope_elem<HD>(kin, d, csr, p.adjacent));
-            vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
+    if (split < r.nact) {
+        if (pos >= r.p0 && pos < r.p1) {  // this CTA owns the new position: write its K/V row
+            const float *kin = p.qkv + qd + (size_t)kvh * HD;
+            const float *vin = p.qkv + qd + kvd + (size_t)kvh * HD;
+            for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
+                kh[(size_t)pos * HD + d] = __float2half_rn(rope_elem<HD>(kin, d, csr, p.adjacent));
+                vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
+            }
         }
-        __threadfence_block();
-    }
-    float qr[G][E];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        const float *qh = p.qkv + (size_t)(kvh * G + g) * HD;
-#pragma unroll
-        for (int e = 0; e < E; e++) qr[g][e] = rope_elem<HD>(qh, lp * E + e, csr, p.adjacent);
-    }
-    __syncthreads();  // the K/V row written above is read below
-
-    float m[G], l[G], o[G][E];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; e++) o[g][e] = 0.f;
-    }
-    for (uint32_t pb = p0 + warp * PPW; pb < p1; pb += 4 * PPW) {  // warp-uniform bound
-        const uint32_t pp = pb + pg;
-        const bool valid = pp < p1;
-        float kf[E], vf[E];
-        uint4 ku = make_uint4(0u, 0u, 0u, 0u), vu = make_uint4(0u, 0u, 0u, 0u);
-        if (valid) {
-            ku = *reinterpret_cast<const uint4 *>(kh + (size_t)pp * HD + lp * E);
-            vu = *reinterpret_cast<const uint4 *>(vh + (size_t)pp * HD + lp * E);
-        }
-        const __half2 *k2 = reinterpret_cast<const __half2 *>(&ku);
-        const __half2 *v2 = reinterpret_cast<const __half2 *>(&vu);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            float2 kk = __half22float2(k2[j]), vv = __half22float2(v2[j]);
-            kf[2 * j] = kk.x;
-            kf[2 * j + 1] = kk.y;
-            vf[2 * j] = vv.x;
-            vf[2 * j + 1] = vv.y;
-        }
+        float qr[G][E];
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            float d = 0.f;
+            const float *qh = p.qkv + (size_t)(kvh * G + g) * HD;
 #pragma unroll
-            for (int e = 0; e < E; e++) d = fmaf(qr[g][e], kf[e], d);
-#pragma unroll
-            for (int sh = 1; sh < LPP; sh <<= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
-            if (valid) {
-                float s = d * scale;
-                float mn = fmaxf(m[g], s);
-                float corr = expf(m[g] - mn);
-                float pe = expf(s - mn);
-                l[g] = l[g] * corr + pe;
-#pragma unroll
-                for (int e = 0; e < E; e++) o[g][e] = o[g][e] * corr + pe * vf[e];
-                m[g] = mn;
-            }
+            for (int e = 0; e < E; e++) qr[g][e] = rope_elem<HD>(qh, lp * E + e, csr, p.adjacent);
         }
-    }
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-#pragma unroll
-        for (int sh = LPP; sh < 32; sh <<= 1) {
-            float mo = __shfl_xor_sync(0xffffffffu, m[g], sh);
-            float lo = __shfl_xor_sync(0xffffffffu, l[g], sh);
-            float mn = fmaxf(m[g], mo);
-            float ca = mn == -INFINITY ? 0.f : expf(m[g] - mn);
-            float cb = mn == -INFINITY ? 0.f : expf(mo - mn);
-            l[g] = l[g] * ca + lo * cb;
-#pragma unroll
-            for (int e = 0; e < E; e++) {
-                float oo = __shfl_xor_sync(0xffffffffu, o[g][e], sh);
-                o[g][e] = o[g][e] * ca + oo * cb;
-            }
-            m[g] = mn;
-        }
-    }
-    __shared__ float sm_m[4][G], sm_l[4][G], sm_o[4][G][HD];
-    if (pg == 0) {
+        __syncthreads();  // the K/V row written above is read below
+        float m[G], l[G], o[G][E];
 #pragma unroll
         for (int g = 0; g < G; g++) {
-            if (lp == 0) {
-                sm_m[warp][g] = m[g];
-                sm_l[warp][g] = l[g];
-            }
+            m[g] = -INFINITY;
+            l[g] = 0.f;
 #pragma unroll
-            for (int e = 0; e < E; e++) sm_o[warp][g][lp * E + e] = o[g][e];
+            for (int e = 0; e < E; e++) o[g][e] = 0.f;
         }
+        attn_walk<HD, G>(qr, kh, vh, r.p0, r.p1, warp, lp, pg, m, l, o);
+        attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh);
     }
-    __syncthreads();
-    const size_t stride = HD + 2;
-    for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
-        int g = t / HD, dd = t % HD;
-        float mm = fmaxf(fmaxf(sm_m[0][g], sm_m[1][g]), fmaxf(sm_m[2][g], sm_m[3][g]));
-        float acc = 0.f, ll = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; w++) {
-            float c = mm == -INFINITY ? 0.f : expf(sm_m[w][g] - mm);
-            acc += sm_o[w][g][dd] * c;
-            ll += sm_l[w][g] * c;
-        }
-        float *pp = p.part + ((size_t)split * p.heads + kvh * G + g) * stride;
-        pp[dd] = acc;
-        if (dd == 0) {
-            pp[HD] = mm;
-            pp[HD + 1] = ll;
-        }
-    }
-    // the last split of this KV group merges the group's heads
+    // the last CTA of this KV group (active or not) merges the group's heads
     __shared__ int is_last;
     __threadfence();
     __syncthreads();
@@ -442,35 +466,9 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnStepArgs p) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    const uint32_t kpad = xq_pad(qd);
     __shared__ float res[G * HD];
-    for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
-        int g = t / HD, dd = t % HD;
-        uint32_t h = kvh * G + g;
-        float M = -INFINITY;
-        for (int s = 0; s < p.nsplit; s++) M = fmaxf(M, __ldcg(p.part + ((size_t)s * p.heads + h) * stride + HD));
-        float acc = 0.f, L = 0.f;
-        for (int s = 0; s < p.nsplit; s++) {
-            const float *pp = p.part + ((size_t)s * p.heads + h) * stride;
-            float ms = __ldcg(pp + HD);
-            float c = ms == -INFINITY ? 0.f : expf(ms - M);
-            acc += __ldcg(pp + dd) * c;
-            L += __ldcg(pp + HD + 1) * c;
-        }
-        float r = acc / L;
-        uint32_t i = h * HD + dd;
-        __half hi = __float2half_rn(r);
-        __half lo = __float2half_rn(r - __half2float(hi));
-        p.xq[xq_pos(i)] = hi;
-        p.xq[kpad + xq_pos(i)] = lo;
-        res[t] = r;
-    }
-    __syncthreads();
-    for (int u = threadIdx.x; u < G * HD / 16; u += blockDim.x) {  // per-16 sums (HD % 16 == 0)
-        float a = 0.f;
-        for (int j = 0; j < 16; j++) a += res[16 * u + j];
-        xq_sums(p.xq, kpad)[(kvh * G * HD) / 16 + u] = a;
-    }
+    attn_merge<HD, G>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res);
+    attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
     if (threadIdx.x == 0) p.tickets[kvh] = 0u;
 }
 
@@ -700,8 +698,9 @@ int launch_rope_cache(const float *qkv, uint32_t qkv_stride, float *q_out, __hal
 
 int attn_pick_nsplit(uint32_t kv_heads, uint32_t max_seq, int sm_count) {
     int want = (2 * sm_count + (int)kv_heads - 1) / (int)kv_heads;
-    int maxs = (int)((max_seq + 15) / 16);
+    int maxs = (int)((max_seq + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK);
     if (want > maxs) want = maxs;
+    if (want > ATT_MAX_SPLIT) want = ATT_MAX_SPLIT;
     if (want < 1) want = 1;
     return want;
 }
@@ -709,7 +708,7 @@ int attn_pick_nsplit(uint32_t kv_heads, uint32_t max_seq, int sm_count) {
 template <int HD, int G>
 static void attn_launch(const float *q, const __half *kc, const __half *vc, uint32_t cs, const int *pp, uint32_t nv,
                         uint32_t heads, uint32_t kvh, float *part, int nsplit, cudaStream_t s) {
-    attn_decode_kernel<HD, G><<<dim3(kvh, nsplit), 128, 0, s>>>(q, kc, vc, cs, pp, nv, heads, kvh, part, nsplit);
+    attn_decode_kernel<HD, G><<<dim3(kvh, nsplit), 128, 0, s>>>(q, kc, vc, cs, pp, nv, heads, part, nsplit);
 }
 
 int launch_attention_decode(const float *q, const __half *k_cache, const __half *v_cache, uint32_t cache_stride,
@@ -717,6 +716,10 @@ int launch_attention_decode(const float *q, const __half *k_cache, const __half 
                             float *part, int nsplit, float *out, __half *xq, cudaStream_t s) {
     if (kv_heads == 0 || heads % kv_heads) {
         set_error("attention: heads (%u) must be a multiple of kv_heads (%u)", heads, kv_heads);
+        return CUQ_EINVAL;
+    }
+    if (nsplit < 1 || nsplit > ATT_MAX_SPLIT) {
+        set_error("attention: nsplit %d outside 1..%d", nsplit, ATT_MAX_SPLIT);
         return CUQ_EINVAL;
     }
     uint32_t G = heads / kv_heads;
@@ -733,7 +736,12 @@ int launch_attention_decode(const float *q, const __half *k_cache, const __half 
     }
 #undef CUQ_ATT
     CUQ_CUDA_TRY(cudaGetLastError());
-    attn_combine_kernel<<<heads, hd, 0, s>>>(part, nsplit, heads, hd, out, xq, xq ? xq_pad(heads * hd) : 0);
+    if (hd == 64)
+        attn_combine_kernel<64><<<heads, 128, 0, s>>>(part, nsplit, pos_ptr, n_val, heads, out, xq,
+                                                       xq ? xq_pad(heads * hd) : 0);
+    else
+        attn_combine_kernel<128><<<heads, 128, 0, s>>>(part, nsplit, pos_ptr, n_val, heads, out, xq,
+                                                        xq ? xq_pad(heads * hd) : 0);
     CUQ_CUDA_TRY(cudaGetLastError());
     return CUQ_OK;
 }

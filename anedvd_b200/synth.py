@@ -125,11 +125,38 @@ class SynthTensor:
         return [self.cols] if self.rows == 1 else [self.cols, self.rows]
 
 
-class SynthModel:
-    """A synthetic model: config + raw GGUF tensors, generated lazily and cached."""
+TILE_SAMPLE = 1 << 16  # weights quantised per tensor in "tiled" payloads
 
-    def __init__(self, cfg):
+
+def tiled_blocks(ttype, key, n):
+    """Raw payload of n weights built from real quantised blocks: TILE_SAMPLE
+    N(0, 0.02) weights are quantised, then each block of the tensor is one of
+    those blocks picked by a seeded generator.  Every block is a valid block of
+    the type with the scale/min statistics quantisation of N(0, 0.02) gives;
+    generating an 8B model this way takes seconds instead of quantising 8e9
+    weights in numpy.  Throughput does not depend on the values."""
+    be, bb = gguf.LAYOUT[ttype]
+    m = min(n, TILE_SAMPLE)
+    sample = quant.quantize(ttype, seeded_normal(key + "/sample", m)).reshape(-1, bb)
+    if m == n:
+        return sample.tobytes()
+    rng = np.random.default_rng(zlib.crc32((key + "/tile").encode()))
+    idx = rng.integers(0, sample.shape[0], size=n // be)
+    return sample[idx].tobytes()
+
+
+class SynthModel:
+    """A synthetic model: config + raw GGUF tensors, generated lazily and cached.
+
+    payload "quantized": every weight drawn and quantised (the parity models);
+    "tiled": blocks drawn from a quantised sample (``tiled_blocks``), for the
+    multi-GB benchmark models."""
+
+    def __init__(self, cfg, payload="quantized", cache=True):
+        assert payload in ("quantized", "tiled")
         self.cfg = cfg
+        self.payload = payload
+        self.cache = cache
         self._cache = {}
 
     def _make(self, name, role, layer, rows, cols):
@@ -139,11 +166,14 @@ class SynthModel:
         t = tensor_type(self.cfg, role, layer)
         n = rows * cols
         if role in ("attn_norm", "ffn_norm", "final_norm"):
-            w = np.ones(n, dtype=np.float32)
+            data = quant.quantize(t, np.ones(n, dtype=np.float32)).tobytes()
+        elif self.payload == "tiled" and t != F32:
+            data = tiled_blocks(t, self.cfg.name + "/" + name, n)
         else:
-            w = seeded_normal(self.cfg.name + "/" + name, n)
-        st = SynthTensor(name, role, layer, t, rows, cols, quant.quantize(t, w).tobytes())
-        self._cache[key] = st
+            data = quant.quantize(t, seeded_normal(self.cfg.name + "/" + name, n)).tobytes()
+        st = SynthTensor(name, role, layer, t, rows, cols, data)
+        if self.cache:
+            self._cache[key] = st
         return st
 
     def tensor_list(self):
@@ -212,11 +242,11 @@ class SynthModel:
         return gguf.write(path, self.metadata(), ts)
 
 
-def model(name_or_cfg, **shrink_kw):
+def model(name_or_cfg, payload="quantized", cache=True, **shrink_kw):
     cfg = CONFIGS[name_or_cfg] if isinstance(name_or_cfg, str) else name_or_cfg
     if shrink_kw:
         cfg = shrink(cfg, **shrink_kw)
-    return SynthModel(cfg)
+    return SynthModel(cfg, payload=payload, cache=cache)
 
 
 def cached_gguf(m, directory=None):

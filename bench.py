@@ -46,6 +46,8 @@ def parse():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile", choices=["gemv"], default=None,
+                    help="run only the roofline kernel (a few launches) for an ncu capture, print nothing")
     return ap.parse_args()
 
 
@@ -170,7 +172,7 @@ def run_reference(args, world, rank):
     }), flush=True)
 
 
-def gemv_roofline(model, stream_ptr, pk):
+def gemv_roofline(model, stream_ptr, pk, reps=64):
     """Time the lm_head quant-GEMV alone: CUDA events around each launch, 8 rotating
     weight copies (240 MB > L2) so every launch streams from HBM."""
     import torch
@@ -188,7 +190,6 @@ def gemv_roofline(model, stream_ptr, pk):
     rt.check(L.cuq_prepare_x(ctypes.c_void_p(x.data_ptr()), t.cols, ctypes.c_void_p(xq.data_ptr()),
                              ctypes.c_void_p(stream_ptr)))
     evs = []
-    reps = 64
     for i in range(reps + 8):
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
@@ -198,6 +199,10 @@ def gemv_roofline(model, stream_ptr, pk):
         if i >= 8:
             evs.append((e0, e1))
     torch.cuda.synchronize()
+    if not evs:  # profile mode: launches only
+        for c in copies:
+            L.cuq_weight_free(c)
+        return None
     ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     for c in copies:
         L.cuq_weight_free(c)
@@ -306,8 +311,26 @@ def run_ours(args, world, rank, local):
     eng.close()
 
 
+def profile_case(args):
+    """A handful of launches of the roofline kernel alone (3 warm-up + 3), for
+    `ncu -k regex:gemv_kernel -s 3 -c 3`; nothing printed."""
+    import torch
+    from anedvd_b200 import runtime as rt
+    from anedvd_b200 import synth
+    rt.load()
+    rt.init(0)
+    torch.cuda.set_device(0)
+    if args.profile == "gemv":
+        s = torch.cuda.Stream()
+        gemv_roofline(synth.model(CONFIG), s.cuda_stream, peaks()[0], reps=-2)  # 6 launches
+    torch.cuda.synchronize()
+
+
 def main():
     args = parse()
+    if args.profile:
+        profile_case(args)
+        return
     world, rank, local = dist_init()
     try:
         if args.impl == "reference":
