@@ -268,5 +268,10 @@ __device__ __forceinline__ void rmsnorm_xq_block(const float *x, const float *w,
 int launch_gemv(const GemvArgs &a, int epilogue, cudaStream_t s);
 // Scratch a GEMV of this weight needs for a given ksplit (floats, counters).
 int gemv_pick_ksplit(const Planes &w, int sm_count);
+struct GemvPlan {
+    int kw = 4;      // warps per 16-row tile
+    int ksplit = 1;  // CTAs along K
+};
+GemvPlan gemv_pick_plan(const Planes &w, int sm_count);
 
 }  // namespace cuq

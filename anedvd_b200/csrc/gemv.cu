@@ -69,7 +69,7 @@ __device__ __forceinline__ uint32_t magic(uint32_t v, uint32_t mask) { return (v
 // the first column of the 4-column group the lane feeds at k-step s.
 
 struct TQ8_0 {
-    static constexpr int SPAN = 64, KSTEPS = 4;
+    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 2;
     static constexpr bool HAS_CORR = false;
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
@@ -105,7 +105,7 @@ struct TQ8_0 {
 // Legacy 32-blocks with 4-bit nibbles: one block per lane per iteration.
 template <int T>
 struct TQ4L {
-    static constexpr int SPAN = 128, KSTEPS = 8;
+    static constexpr int SPAN = 128, KSTEPS = 8, DEPTH = 2;
     static constexpr bool HAS_CORR = false;
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
@@ -180,16 +180,6 @@ struct TQ4L {
     __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 32 + (s & 1) * 16 + (s >> 1) * 4; }
 };
 
-__device__ __forceinline__ void scale_min_k4(int j, const uint8_t *q, int &d, int &m) {
-    if (j < 4) {
-        d = q[j] & 63;
-        m = q[j + 4] & 63;
-    } else {
-        d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
-    }
-}
-
 // Q4_K: one 256-superblock per iteration; lane tig owns the 32-byte group tig
 // (sub-blocks 2tig in the low nibbles and 2tig+1 in the high nibbles).
 // The reference weight is d1*q - m1 with d1 = d*sc, m1 = dmin*m, both exact in
@@ -199,7 +189,7 @@ __device__ __forceinline__ void scale_min_k4(int j, const uint8_t *q, int &d, in
 // is rounded).  The small remainder (m1 - m1h) * sum(x) over the sub-block is
 // subtracted after the MMA in fp32, so no scale error is shared by a sub-block.
 struct TQ4K {
-    static constexpr int SPAN = 256, KSTEPS = 16;
+    static constexpr int SPAN = 256, KSTEPS = 16, DEPTH = 1;
     static constexpr bool HAS_CORR = true;
     struct Raw { uint4 q[2][2]; __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
@@ -210,13 +200,17 @@ struct TQ4K {
             R.q[rr][0] = ldg_stream(qp);
             R.q[rr][1] = ldg_stream(qp + 16);
             uint4 meta = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
-            const uint8_t *mb = reinterpret_cast<const uint8_t *>(&meta);
             R.d[rr] = __half2half2(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
             float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
 #pragma unroll
             for (int part = 0; part < 2; part++) {
-                int sc, mm;
-                scale_min_k4(2 * tig + part, mb + 4, sc, mm);
+                // get_scale_min_k4 (gguf.zig:960-973) for sub-block j = 2*tig + part,
+                // from the 12 scale bytes held as words y, z, w (runtime shifts, so
+                // the lane-dependent byte index never touches local memory)
+                const int j = 2 * tig + part, sh = 8 * (j & 3);
+                const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
+                const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
+                const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
                 R.sc[rr][part] = __float2half2_rn((float)sc);
                 R.csc[rr][part] = __float2half2_rn(-1024.f * (float)sc);  // exact: |1024*63| < 65504
                 float m1 = dmin * (float)mm;                                // exact in fp32
@@ -256,7 +250,7 @@ struct TQ4K {
 // an fp16 pair s_hi + s_lo so each weight RN16((q-32) * d * sc) is rounded
 // once, like the reference's fp16 weight (gguf.zig:1036-1059, load_gguf.zig:371).
 struct TQ6K {
-    static constexpr int SPAN = 256, KSTEPS = 16;
+    static constexpr int SPAN = 256, KSTEPS = 16, DEPTH = 1;
     static constexpr bool HAS_CORR = false;
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
@@ -271,11 +265,14 @@ struct TQ6K {
             R.b[rr] = ldg_stream(ql + 32);
             R.h[rr] = ldg_stream(w.q2 + (size_t)r * (w.cols / 4) + (size_t)it * 64 + hh * 32 + lh);
             uint4 scv = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
-            const int8_t *sc = reinterpret_cast<const int8_t *>(&scv);
             float d = __half2float(reinterpret_cast<const __half *>(w.s2)[(size_t)it * w.rows + r]);
 #pragma unroll
             for (int t = 0; t < 4; t++) {
-                float scale = d * (float)sc[hh * 8 + 2 * t + (tig & 1)];  // exact
+                // int8 scale hh*8 + 2t + (tig&1), picked with a select and a runtime
+                // shift (no local-memory indexing)
+                const uint32_t wd = t < 2 ? (hh ? scv.z : scv.x) : (hh ? scv.w : scv.y);
+                const int sc = (int)(int8_t)((wd >> (8 * (2 * (t & 1) + (tig & 1)))) & 0xFFu);
+                float scale = d * (float)sc;  // exact
                 __half hi = __float2half_rn(scale);
                 R.s[rr][t] = __half2half2(hi);
                 R.sl[rr][t] = __float2half2_rn(scale - __half2float(hi));
@@ -321,7 +318,7 @@ struct TQ6K {
 // F16 / BF16: 16 weights per lane-row per iteration.
 template <int T>
 struct T16 {
-    static constexpr int SPAN = 64, KSTEPS = 4;
+    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 2;
     static constexpr bool HAS_CORR = false;
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
@@ -399,28 +396,33 @@ __device__ void finish_step(StepState *st, const uint32_t *forced, uint32_t *out
     st->token = (s + 1 < st->n_forced) ? (int)forced[s + 1] : (int)idx;
 }
 
-template <class TT, int EPI>
+// CTA of 4 warps = TPC = 4 / KW tiles of 16 rows, KW warps per tile splitting
+// the CTA's K range (iteration it goes to warp it % KW of the tile).  Each warp
+// keeps D iterations of loads in flight ahead of the one it computes.
+template <class TT, int EPI, int KW, int D>
 __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
-    __shared__ float red[4][DUAL ? 32 : 16];
+    constexpr int TPC = 4 / KW;           // tiles per CTA
+    constexpr int NV = DUAL ? 32 : 16;    // values per tile (gate rows then up rows)
+    __shared__ float red[4][NV];
     __shared__ int is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
-    const uint32_t tile = blockIdx.x, row0 = tile * 16;
-    const uint32_t r0 = row0 + g;
+    const int lt = warp / KW, kw = warp % KW;
+    const uint32_t ntiles = p.w.rows / 16;
+    const uint32_t tile = blockIdx.x * TPC + lt;
+    const bool active = tile < ntiles;
+    const uint32_t r0 = tile * 16 + g;
     const int ni = (int)((p.w.cols + TT::SPAN - 1) / TT::SPAN);
     const int per = (ni + p.ksplit - 1) / p.ksplit;
-    const int it0 = blockIdx.y * per, it1 = min(ni, it0 + per);
+    const int it0 = blockIdx.y * per, it1 = active ? min(ni, it0 + per) : it0;
 
     // The weights do not depend on the previous kernel: start streaming the
-    // warp's first iteration before waiting for the activation.
-    // One iteration in flight per warp beyond the one computing: deeper register
-    // rings cost more occupancy than they hide (measured).
-    constexpr int D = 1;
+    // warp's first D iterations before waiting for the activation.
     typename TT::Raw ring[D], ring2[D];
 #pragma unroll
     for (int j = 0; j < D; j++) {
-        const int itj = it0 + warp + 4 * j;
+        const int itj = it0 + kw + KW * j;
         if (itj < it1) {
             TT::load(ring[j], p.w, r0, itj, tig);
             if (DUAL) TT::load(ring2[j], p.w2, r0, itj, tig);
@@ -434,13 +436,13 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
 
     float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
     float k0 = 0.f, k1 = 0.f, k20 = 0.f, k21 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
-    for (int base = it0 + warp; base < it1; base += 4 * D) {
+    for (int base = it0 + kw; base < it1; base += KW * D) {
 #pragma unroll
         for (int j = 0; j < D; j++) {
-            const int it = base + 4 * j;
+            const int it = base + KW * j;
             if (it >= it1) break;  // uniform across the warp
             typename TT::Raw R = ring[j], R2 = ring2[j];
-            const int itn = it + 4 * D;
+            const int itn = it + KW * D;
             if (itn < it1) {  // refill this slot while the iteration computes
                 TT::load(ring[j], p.w, r0, itn, tig);
                 if (DUAL) TT::load(ring2[j], p.w2, r0, itn, tig);
@@ -481,43 +483,45 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
         }
     }
     __syncthreads();
-    constexpr int NV = DUAL ? 32 : 16;
+    // thread t < TPC * NV owns value vi of local tile tl
     const int t = threadIdx.x;
+    const int tl = t / NV, vi = t % NV;
+    const bool own = t < TPC * NV && blockIdx.x * TPC + tl < ntiles;
+    const uint32_t row = (blockIdx.x * TPC + tl) * 16 + (vi & 15);
     float v = 0.f;
-    if (t < NV) v = ((red[0][t] + red[1][t]) + red[2][t]) + red[3][t];
+    if (own) {
+#pragma unroll
+        for (int w = 0; w < KW; w++) v += red[tl * KW + w][vi];
+    }
     const uint32_t rows = p.w.rows;
     if (p.ksplit > 1) {
-        // split-K: publish the partial, the last CTA of this tile reduces in order.
-        if (t < NV) {
-            uint32_t row = row0 + (t & 15);
-            p.ws[((size_t)blockIdx.y * (DUAL ? 2 : 1) + (t >> 4)) * rows + row] = v;
-        }
+        // split-K: publish the partials, the last CTA of this column of the grid
+        // (atomic ticket per blockIdx.x) reduces them in a fixed order.
+        if (own) p.ws[((size_t)blockIdx.y * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row] = v;
         __threadfence();
         __syncthreads();
         if (t == 0) {
-            unsigned int prev = atomicAdd(&p.counters[tile], 1u);
+            unsigned int prev = atomicAdd(&p.counters[blockIdx.x], 1u);
             is_last = (prev == (unsigned)p.ksplit - 1u);
         }
         __syncthreads();
         if (!is_last) return;
         __threadfence();
-        if (t < NV) {
-            uint32_t row = row0 + (t & 15);
+        if (own) {
             float acc = 0.f;
             for (int ky = 0; ky < p.ksplit; ky++)
-                acc += __ldcg(&p.ws[((size_t)ky * (DUAL ? 2 : 1) + (t >> 4)) * rows + row]);
+                acc += __ldcg(&p.ws[((size_t)ky * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row]);
             v = acc;
         }
-        if (t == 0) p.counters[tile] = 0u;
+        if (t == 0) p.counters[blockIdx.x] = 0u;
     }
     if (EPI == EPI_SILU_XQ) {
-        __shared__ float gu[32];
-        __shared__ float act16[16];
-        if (t < 32) gu[t] = v;
+        __shared__ float gu[TPC][32];
+        __shared__ float act16[TPC][16];
+        if (own) gu[tl][vi] = v;
         __syncthreads();
-        if (t < 16) {
-            uint32_t row = row0 + t;
-            float gt = gu[t], ut = gu[16 + t];
+        if (own && vi < 16) {
+            float gt = gu[tl][vi], ut = gu[tl][16 + vi];
             // cpu.siluMul (cpu.zig:65-70): g * (1 / (1 + exp(-g))) * u
             float sg = 1.0f / (1.0f + expf(-gt));
             float act = (gt * sg) * ut;
@@ -527,17 +531,16 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
             uint32_t pos = xq_pos(row);
             p.xq_out[pos] = hi;
             p.xq_out[p.kpad_out + pos] = lo;
-            act16[t] = act;
+            act16[tl][vi] = act;
         }
         __syncthreads();
-        if (t == 0) {  // this tile's 16 rows are exactly one xq sum group
+        if (t < TPC && blockIdx.x * TPC + t < ntiles) {  // a tile's 16 rows are exactly one xq sum group
             float acc = 0.f;
-            for (int j = 0; j < 16; j++) acc += act16[j];
-            xq_sums(p.xq_out, p.kpad_out)[tile] = acc;
+            for (int j = 0; j < 16; j++) acc += act16[t][j];
+            xq_sums(p.xq_out, p.kpad_out)[blockIdx.x * TPC + t] = acc;
         }
     } else {
-        if (t < 16) {
-            uint32_t row = row0 + t;
+        if (own) {
             if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
                 if (p.bias) v = v + p.bias[row];
                 p.y[row] = v;
@@ -547,21 +550,22 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
             }
         }
         if (EPI == EPI_ARGMAX) {
-            // first index of the maximum within the tile (cpu.zig:477-483), then a
-            // packed 64-bit max across tiles: larger value wins, then smaller index.
-            if (t < 32) {
-                unsigned long long key = t < 16 ? pack_argmax(v, row0 + t) : 0ull;
+            // first index of the maximum (cpu.zig:477-483) as a packed 64-bit max
+            // across the CTA, then across CTAs: larger value wins, then smaller index.
+            if (t < TPC * 16) {  // TPC * 16 is 16, 32 or 64 threads
+                unsigned long long key = own ? pack_argmax(v, row) : 0ull;
+                constexpr unsigned mask = TPC == 1 ? 0x0000ffffu : 0xffffffffu;
 #pragma unroll
-                for (int o = 8; o > 0; o >>= 1) {
-                    unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+                for (int o = TPC == 1 ? 8 : 16; o > 0; o >>= 1) {
+                    unsigned long long other = __shfl_xor_sync(mask, key, o);
                     key = other > key ? other : key;
                 }
-                if (t == 0) atomicMax(p.argmax64, key);
+                if ((t & 31) == 0) atomicMax(p.argmax64, key);
             }
         }
     }
     if (p.post.op == POST_NONE) return;
-    // Grid completion: the CTA that finishes the last tile runs the post-op.
+    // Grid completion: the CTA that finishes last runs the post-op.
     __threadfence();
     __syncthreads();
     if (t == 0) {
@@ -577,6 +581,23 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
         if (t == 0) finish_step(p.post.state, p.post.forced, p.post.out_tokens);
     }
     if (t == 0) *p.post.done = 0u;
+}
+
+template <class TT, int EPI, int KW>
+cudaError_t launch_kw(const GemvArgs &a, const KArgs &k, cudaStream_t s) {
+    constexpr int D = EPI == EPI_SILU_XQ ? 1 : TT::DEPTH;
+    constexpr int TPC = 4 / KW;
+    dim3 grid((a.w->rows / 16 + TPC - 1) / TPC, k.ksplit);
+    return launch_maybe_pdl(gemv_kernel<TT, EPI, KW, D>, grid, dim3(128), 0, s, a.pdl, k);
+}
+
+template <class TT, int EPI>
+cudaError_t launch_epi(const GemvArgs &a, const KArgs &k, int kw, cudaStream_t s) {
+    switch (kw) {
+    case 1: return launch_kw<TT, EPI, 1>(a, k, s);
+    case 2: return launch_kw<TT, EPI, 2>(a, k, s);
+    default: return launch_kw<TT, EPI, 4>(a, k, s);
+    }
 }
 
 template <class TT>
@@ -596,14 +617,13 @@ int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
     k.counters = a.counters;
     k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
     k.post = a.post;
-    dim3 grid(a.w->rows / 16, k.ksplit);
-    const size_t smem = 0;
+    const int kw = gemv_pick_plan(*a.w, 0).kw;
     cudaError_t e;
     switch (epi) {
-    case EPI_STORE: e = launch_maybe_pdl(gemv_kernel<TT, EPI_STORE>, grid, dim3(128), smem, s, a.pdl, k); break;
-    case EPI_ADD: e = launch_maybe_pdl(gemv_kernel<TT, EPI_ADD>, grid, dim3(128), smem, s, a.pdl, k); break;
-    case EPI_SILU_XQ: e = launch_maybe_pdl(gemv_kernel<TT, EPI_SILU_XQ>, grid, dim3(128), smem, s, a.pdl, k); break;
-    case EPI_ARGMAX: e = launch_maybe_pdl(gemv_kernel<TT, EPI_ARGMAX>, grid, dim3(128), smem, s, a.pdl, k); break;
+    case EPI_STORE: e = launch_epi<TT, EPI_STORE>(a, k, kw, s); break;
+    case EPI_ADD: e = launch_epi<TT, EPI_ADD>(a, k, kw, s); break;
+    case EPI_SILU_XQ: e = launch_epi<TT, EPI_SILU_XQ>(a, k, kw, s); break;
+    case EPI_ARGMAX: e = launch_epi<TT, EPI_ARGMAX>(a, k, kw, s); break;
     default: set_error("bad epilogue %d", epi); return CUQ_EINVAL;
     }
     if (e != cudaSuccess) {
@@ -663,22 +683,34 @@ int launch_rmsnorm_xq(const float *x, const float *w, uint32_t n, uint32_t n_row
     return CUQ_OK;
 }
 
-int gemv_pick_ksplit(const Planes &w, int sm_count) {
+// Work split of a GEMV: KW warps per 16-row tile inside a CTA and ksplit CTAs
+// along K (chosen from a sweep of both over the decode shapes of the benchmark
+// configs).  KW depends on the shape only (not on sm_count), so callers that
+// size the split-K workspace with one sm_count and launch with another agree.
+GemvPlan gemv_pick_plan(const Planes &w, int sm_count) {
     int span;
     switch (w.type) {
     case CUQ_Q8_0: case CUQ_F16: case CUQ_BF16: span = 64; break;
     case CUQ_Q4_K: case CUQ_Q6_K: span = 256; break;
     default: span = 128; break;
     }
-    int ni = (int)((w.cols + span - 1) / span);
-    int tiles = (int)(w.rows / 16);
-    int want = (sm_count * 8 + tiles - 1) / tiles;  // ~8 CTAs of 4 warps per SM
-    int maxk = ni / 8;                              // keep >= 2 iterations per warp
+    const int ni = (int)((w.cols + span - 1) / span);
+    const int tiles = (int)(w.rows / 16);
+    GemvPlan pl;
+    // Very tall matrices (lm_head, embeddings) have tiles enough to fill the GPU
+    // many times over: two tiles per CTA with two warps each measured best.
+    pl.kw = tiles >= 2048 ? 2 : 4;
+    const int sm = sm_count > 0 ? sm_count : 148;
+    int want = (sm * 8 + tiles - 1) / tiles;  // ~8 CTAs of 4 warps per SM
+    int maxk = ni / 8;                        // keep >= 2 iterations per warp
     if (want > maxk) want = maxk;
     if (want > 16) want = 16;
     if (want < 1) want = 1;
-    return want;
+    pl.ksplit = want;
+    return pl;
 }
+
+int gemv_pick_ksplit(const Planes &w, int sm_count) { return gemv_pick_plan(w, sm_count).ksplit; }
 
 int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
     const Planes &w = *a.w;

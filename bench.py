@@ -173,8 +173,10 @@ def run_reference(args, world, rank):
 
 
 def gemv_roofline(model, stream_ptr, pk, reps=64):
-    """Time the lm_head quant-GEMV alone: CUDA events around each launch, 8 rotating
-    weight copies (240 MB > L2) so every launch streams from HBM."""
+    """Time the lm_head quant-GEMV alone: CUDA events around `reps` back-to-back
+    launches on the engine's stream over 8 rotating weight copies (240 MB > L2),
+    so every launch streams from HBM; the mean launch duration includes the
+    short gap between consecutive launches."""
     import torch
     from anedvd_b200 import runtime as rt
     L = rt.load()
@@ -189,21 +191,26 @@ def gemv_roofline(model, stream_ptr, pk, reps=64):
     stream = torch.cuda.ExternalStream(stream_ptr)
     rt.check(L.cuq_prepare_x(ctypes.c_void_p(x.data_ptr()), t.cols, ctypes.c_void_p(xq.data_ptr()),
                              ctypes.c_void_p(stream_ptr)))
-    evs = []
-    for i in range(reps + 8):
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
+    for i in range(8 if reps > 0 else 6):  # warm-up (profile mode: these are the only launches)
         rt.check(L.cuq_gemv_prepared(copies[i % 8], ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(y.data_ptr()),
                                      ctypes.c_void_p(stream_ptr)))
-        e1.record(stream)
-        if i >= 8:
-            evs.append((e0, e1))
-    torch.cuda.synchronize()
-    if not evs:  # profile mode: launches only
+    if reps <= 0:
+        torch.cuda.synchronize()
         for c in copies:
             L.cuq_weight_free(c)
         return None
-    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    # back-to-back launches on the engine's stream; a spin kernel first lets the
+    # host queue them all, so the events time the GPU, not the launch calls
+    with torch.cuda.stream(stream):
+        torch.cuda._sleep(4_000_000)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(reps):
+        L.cuq_gemv_prepared(copies[i % 8], ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                            ctypes.c_void_p(stream_ptr))
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
     for c in copies:
         L.cuq_weight_free(c)
     alg = t.rows * t.cols * 34 // 32 + 4 * t.cols + 4 * t.rows   # N*K*bpw + 4K + 4N (Q8_0 bpw 34/32)
@@ -322,7 +329,7 @@ def profile_case(args):
     torch.cuda.set_device(0)
     if args.profile == "gemv":
         s = torch.cuda.Stream()
-        gemv_roofline(synth.model(CONFIG), s.cuda_stream, peaks()[0], reps=-2)  # 6 launches
+        gemv_roofline(synth.model(CONFIG), s.cuda_stream, peaks()[0], reps=0)  # 6 launches
     torch.cuda.synchronize()
 
 
