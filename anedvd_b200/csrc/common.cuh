@@ -172,10 +172,30 @@ cudaError_t launch_maybe_pdl(void (*kernel)(KArgsT...), dim3 grid, dim3 block, s
 
 // ------------------------------------------------------------------ GEMV ---
 
+// Tensor parallelism (Megatron column/row split, one rank per GPU): every rank
+// maps every other rank's communication buffer (CUDA IPC over NVLink) and
+// pushes its partial sums into a slot of each peer's buffer with plain stores,
+// then counts its arrival with a system-scope atomic on each peer.  Layout of
+// one buffer: two phase regions (o and down projections alternate, so a rank
+// is never more than one phase ahead of its peers) of [size][slot_floats]
+// fp32, then [size] packed argmax keys, then arrival counters.
+constexpr int TP_MAX = 8;
+enum TpCounter : int { TP_CTR_PH0 = 0, TP_CTR_PH1 = 1, TP_CTR_ARGMAX = 2 };
+struct TpComm {
+    int rank = 0, size = 1;
+    uint8_t *peer[TP_MAX] = {};   // each rank's buffer as mapped in this process (own at [rank])
+    size_t slot_floats = 0;       // floats per source-rank slot
+    size_t off_phase[2] = {0, 0}; // byte offsets of the two phase regions
+    size_t off_am = 0;            // byte offset of the argmax keys
+    size_t off_ctr = 0;           // byte offset of the counters
+    int *err = nullptr;           // this rank's error flag: set when a wait gives up
+};
+
 // Work the CTA that completes a GEMV's last tile does after the whole output is
 // written: the next RMSNorm (of the residual x into xq), or the end of a decode
-// step (argmax -> next token).
-enum GemvPostOp : int { POST_NONE = 0, POST_RMSNORM = 1, POST_FINISH = 2 };
+// step (argmax -> next token); with tensor parallelism, first the cross-rank
+// reduction of the pushed partials (POST_TP_REDUCE) or argmax keys (POST_TP_FINISH).
+enum GemvPostOp : int { POST_NONE = 0, POST_RMSNORM = 1, POST_FINISH = 2, POST_TP_REDUCE = 3, POST_TP_FINISH = 4 };
 
 struct GemvPost {
     int op = POST_NONE;
@@ -189,13 +209,20 @@ struct GemvPost {
     StepState *state = nullptr;
     const uint32_t *forced = nullptr;
     uint32_t *out_tokens = nullptr;
+    // POST_TP_REDUCE: x += sum over ranks of the phase-`tp_phase` partials (+ bias),
+    // then the RMSNorm above.  POST_TP_FINISH: argmax across ranks, then POST_FINISH.
+    TpComm tp;
+    int tp_phase = 0;
+    float *xr = nullptr;          // residual updated by POST_TP_REDUCE
+    const float *bias = nullptr;
 };
 
 enum GemvEpilogue : int {
     EPI_STORE = 0,     // y = acc (+ bias)
     EPI_ADD = 1,       // y += (acc + bias)        (residual add, engine.zig:607-620)
     EPI_SILU_XQ = 2,   // dual weight: act = silu(gate) * up, written as xq (+ fp32)
-    EPI_ARGMAX = 3,    // y = acc; packed (value, index) max into *argmax64
+    EPI_ARGMAX = 3,    // y = acc; packed (value, row_base + index) max into *argmax64
+    EPI_TP_PUSH = 4,   // partial -> slot [rank] of phase post.tp_phase on every rank (see TpComm)
 };
 
 struct GemvArgs {
@@ -206,6 +233,7 @@ struct GemvArgs {
     const float *bias = nullptr;
     __half *xq_out = nullptr;     // EPI_SILU_XQ: act in xq form (kpad of w->rows)
     unsigned long long *argmax64 = nullptr;
+    uint32_t row_base = 0;        // EPI_ARGMAX: global index of this weight's row 0
     float *ws = nullptr;          // split-K partials [ksplit][rows]
     unsigned int *counters = nullptr;  // one per 16-row tile, self-resetting
     int ksplit = 1;

@@ -18,6 +18,7 @@
 //     reduces deterministically through a workspace: the last CTA of a tile
 //     (atomic ticket) sums the partials in a fixed order and resets the ticket.
 #include "common.cuh"
+#include "tp.cuh"
 
 namespace cuq {
 
@@ -370,6 +371,7 @@ struct KArgs {
     __half *xq_out;
     uint32_t kpad_out;
     unsigned long long *argmax64;
+    uint32_t row_base;
     float *ws;
     unsigned int *counters;
     int ksplit;
@@ -539,6 +541,13 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
             for (int j = 0; j < 16; j++) acc += act16[t][j];
             xq_sums(p.xq_out, p.kpad_out)[blockIdx.x * TPC + t] = acc;
         }
+    } else if (EPI == EPI_TP_PUSH) {
+        // this rank's partial of rows [row] into slot [rank] of every rank's buffer
+        if (own)
+            for (int q = 0; q < p.post.tp.size; q++) tp_slot(p.post.tp, q, p.post.tp_phase, p.post.tp.rank)[row] = v;
+        __threadfence_system();
+        __syncthreads();
+        if (t == 0) tp_signal(p.post.tp, p.post.tp_phase);
     } else {
         if (own) {
             if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
@@ -553,7 +562,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
             // first index of the maximum (cpu.zig:477-483) as a packed 64-bit max
             // across the CTA, then across CTAs: larger value wins, then smaller index.
             if (t < TPC * 16) {  // TPC * 16 is 16, 32 or 64 threads
-                unsigned long long key = own ? pack_argmax(v, row) : 0ull;
+                unsigned long long key = own ? pack_argmax(v, p.row_base + row) : 0ull;
                 constexpr unsigned mask = TPC == 1 ? 0x0000ffffu : 0xffffffffu;
 #pragma unroll
                 for (int o = TPC == 1 ? 8 : 16; o > 0; o >>= 1) {
@@ -575,10 +584,46 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    if (p.post.op == POST_RMSNORM) {
+    if (p.post.op == POST_TP_REDUCE) {
+        // every rank's CTAs pushed once: x += sum over ranks (+ bias), then the RMSNorm
+        const TpComm &tp = p.post.tp;
+        __shared__ int ok;
+        if (t == 0) ok = tp_wait(tp, p.post.tp_phase, (unsigned)tp.size * gridDim.x);
+        __syncthreads();
+        if (ok) {
+            for (uint32_t i = t; i < p.post.n; i += blockDim.x) {
+                float sum = tp_sum(tp, p.post.tp_phase, i);
+                if (p.post.bias) sum = sum + p.post.bias[i];
+                p.post.xr[i] = __ldcg(p.post.xr + i) + sum;
+            }
+        }
+        __threadfence();
+        __syncthreads();
+        if (t == 0) tp_reset(tp, p.post.tp_phase);
+        rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
+    } else if (p.post.op == POST_RMSNORM) {
         rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
     } else if (p.post.op == POST_FINISH) {
         if (t == 0) finish_step(p.post.state, p.post.forced, p.post.out_tokens);
+    } else if (p.post.op == POST_TP_FINISH) {
+        // cross-rank argmax: every rank publishes its packed key, all take the max
+        // (the packing keeps the reference's first-index tie rule, cpu.zig:477-483)
+        if (t == 0) {
+            const TpComm &tp = p.post.tp;
+            const unsigned long long mine = __ldcg(&p.post.state->argmax64);
+            for (int q = 0; q < tp.size; q++) tp_am(tp, q)[tp.rank] = mine;
+            tp_signal(tp, TP_CTR_ARGMAX);
+            unsigned long long best = mine;
+            if (tp_wait(tp, TP_CTR_ARGMAX, (unsigned)tp.size)) {
+                for (int r = 0; r < tp.size; r++) {
+                    const unsigned long long k = __ldcv(tp_am(tp, tp.rank) + r);
+                    best = k > best ? k : best;
+                }
+            }
+            tp_reset(tp, TP_CTR_ARGMAX);
+            p.post.state->argmax64 = best;
+            finish_step(p.post.state, p.post.forced, p.post.out_tokens);
+        }
     }
     if (t == 0) *p.post.done = 0u;
 }
@@ -613,6 +658,7 @@ int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
     k.xq_out = a.xq_out;
     k.kpad_out = xq_pad(a.w->rows);
     k.argmax64 = a.argmax64;
+    k.row_base = a.row_base;
     k.ws = a.ws;
     k.counters = a.counters;
     k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
@@ -624,6 +670,7 @@ int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
     case EPI_ADD: e = launch_epi<TT, EPI_ADD>(a, k, kw, s); break;
     case EPI_SILU_XQ: e = launch_epi<TT, EPI_SILU_XQ>(a, k, kw, s); break;
     case EPI_ARGMAX: e = launch_epi<TT, EPI_ARGMAX>(a, k, kw, s); break;
+    case EPI_TP_PUSH: e = launch_epi<TT, EPI_TP_PUSH>(a, k, kw, s); break;
     default: set_error("bad epilogue %d", epi); return CUQ_EINVAL;
     }
     if (e != cudaSuccess) {

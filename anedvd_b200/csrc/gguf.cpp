@@ -348,7 +348,9 @@ extern "C" cuq_model *cuq_model_load_gguf(const char *path, const cuq_options *o
             if (good && g.tensors.count(p + "attn_output.bias"))
                 good = vec(p + "attn_output.bias", l, CUQ_ROLE_O_BIAS, c.hidden, true);
         }
-        if (!good || cuq_model_finalize(m) != CUQ_OK) {
+        // a tensor-parallel model is finalized by the caller after cuq_tp_connect
+        const bool tp = opts && opts->tp_size > 1;
+        if (!good || (!tp && cuq_model_finalize(m) != CUQ_OK)) {
             cuq_model_free(m);
             m = nullptr;
         }

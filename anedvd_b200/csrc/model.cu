@@ -21,6 +21,7 @@
 #include "model.h"
 #include "ops.cuh"
 #include "qgemm.cuh"
+#include "tp.cuh"
 
 using namespace cuq;
 
@@ -33,6 +34,7 @@ namespace {
 enum { R_Q = 0, R_K, R_V, R_O, R_GATE, R_UP, R_DOWN };
 
 uint32_t q_dim(const cuq_config &c) { return c.heads * c.head_dim; }
+size_t round256(size_t x) { return (x + 255) & ~(size_t)255; }
 uint32_t kv_dim(const cuq_config &c) { return c.kv_heads * c.head_dim; }
 
 void free_pending(PendingTensor &t) {
@@ -82,8 +84,41 @@ int build_proj(Proj &out, std::vector<PendingTensor *> parts, cudaStream_t s) {
 
 }  // namespace
 
-static int enqueue_step(cuq_model *m) {
+// The lm_head weight: the embedding table when tied on one GPU, else `output`
+// (the untied head, or this rank's rows of the tied table).
+static const Proj &head_proj(const cuq_model *m) {
+    return (m->cfg.tie_embeddings && m->opt.tp_size == 1) ? m->embed : m->output;
+}
+
+// o / down projection output: on one GPU added into the residual with the next
+// RMSNorm as post-op; under tensor parallelism pushed to every rank and reduced
+// (+ bias, + residual, RMSNorm) by the post-op.
+static void residual_out(cuq_model *m, GemvArgs &a, int &epi, const float *bias, const float *next_norm, int phase) {
     const cuq_config &c = m->cfg;
+    a.post.x = m->x;
+    a.post.w = next_norm;
+    a.post.n = c.hidden;
+    a.post.eps = c.eps;
+    a.post.xq = m->xq_h;
+    if (m->opt.tp_size > 1) {
+        epi = EPI_TP_PUSH;
+        a.y = nullptr;
+        a.bias = nullptr;
+        a.post.op = POST_TP_REDUCE;
+        a.post.tp = m->tpc;
+        a.post.tp_phase = phase;
+        a.post.xr = m->x;
+        a.post.bias = bias;
+    } else {
+        epi = EPI_ADD;
+        a.y = m->x;
+        a.bias = bias;
+        a.post.op = POST_RMSNORM;
+    }
+}
+
+static int enqueue_step(cuq_model *m) {
+    const cuq_config &c = m->cfg, &lc = m->lc;
     cudaStream_t s = m->stream;
     const bool pdl = true;  // every launch below waits for its predecessor with griddepcontrol.wait
     int rc;
@@ -94,7 +129,7 @@ static int enqueue_step(cuq_model *m) {
         if (rc != CUQ_OK) return rc; \
         nk++;                        \
     } while (0)
-    auto gemv = [&](const Planes &w, const __half *xq, float *y, const float *bias, int epi) {
+    auto gemv = [&](const Planes &w, const __half *xq, float *y, const float *bias) {
         GemvArgs a;
         a.w = &w;
         a.xq = xq;
@@ -113,59 +148,52 @@ static int enqueue_step(cuq_model *m) {
         Layer &L = m->layers[l];
         // qkv projection + bias (main.zig:435-436)
         for (auto &seg : L.qkv) {
-            GemvArgs a = gemv(seg.p, m->xq_h, m->qkv + seg.row_off, L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr,
-                              EPI_STORE);
+            GemvArgs a = gemv(seg.p, m->xq_h, m->qkv + seg.row_off, L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr);
             TRY(launch_gemv(a, EPI_STORE, s));
         }
-        // RoPE + fp16 KV write + attention (main.zig:457-472)
-        TRY(launch_attention_step(m->qkv, m->rope_cs, m->state, L.k_cache, L.v_cache, m->opt.max_seq, c.heads,
-                                  c.kv_heads, c.head_dim, c.rope_adjacent, m->attn_part, m->attn_nsplit, m->tickets,
+        // RoPE + fp16 KV write + attention (main.zig:457-472), this rank's heads
+        TRY(launch_attention_step(m->qkv, m->rope_cs, m->state, L.k_cache, L.v_cache, m->opt.max_seq, lc.heads,
+                                  lc.kv_heads, c.head_dim, c.rope_adjacent, m->attn_part, m->attn_nsplit, m->tickets,
                                   m->xq_attn, pdl, s));
         // o projection + o_bias into the residual (main.zig:477-485), then ffn RMSNorm (main.zig:487)
         {
-            GemvArgs a = gemv(L.o.p, m->xq_attn, m->x, L.o_bias, EPI_ADD);
-            a.post.op = POST_RMSNORM;
-            a.post.x = m->x;
-            a.post.w = L.ffn_norm;
-            a.post.n = c.hidden;
-            a.post.eps = c.eps;
-            a.post.xq = m->xq_h;
-            TRY(launch_gemv(a, EPI_ADD, s));
+            GemvArgs a = gemv(L.o.p, m->xq_attn, nullptr, nullptr);
+            int epi;
+            residual_out(m, a, epi, L.o_bias, L.ffn_norm, 0);
+            TRY(launch_gemv(a, epi, s));
         }
         // gate/up with the SiLU*mul epilogue (engine.zig:645-668 split path)
         if (L.gate_up_dual) {
-            GemvArgs a = gemv(L.gate.p, m->xq_h, nullptr, nullptr, EPI_SILU_XQ);
+            GemvArgs a = gemv(L.gate.p, m->xq_h, nullptr, nullptr);
             a.w2 = &L.up.p;
             a.xq_out = m->xq_act;
             TRY(launch_gemv(a, EPI_SILU_XQ, s));
         } else {
-            GemvArgs a = gemv(L.gate.p, m->xq_h, m->gate_buf, nullptr, EPI_STORE);
+            GemvArgs a = gemv(L.gate.p, m->xq_h, m->gate_buf, nullptr);
             TRY(launch_gemv(a, EPI_STORE, s));
-            a = gemv(L.up.p, m->xq_h, m->up_buf, nullptr, EPI_STORE);
+            a = gemv(L.up.p, m->xq_h, m->up_buf, nullptr);
             TRY(launch_gemv(a, EPI_STORE, s));
-            TRY(launch_silu_mul(m->act, m->gate_buf, m->up_buf, c.inter, s));
-            TRY(launch_to_xq(m->act, c.inter, 1, c.inter, m->xq_act, s));
+            TRY(launch_silu_mul(m->act, m->gate_buf, m->up_buf, lc.inter, s));
+            TRY(launch_to_xq(m->act, lc.inter, 1, lc.inter, m->xq_act, s));
         }
         // down projection into the residual, then the next RMSNorm (next layer's
         // attention norm, or the final norm before the lm_head, main.zig:532)
         {
-            GemvArgs a = gemv(L.down.p, m->xq_act, m->x, nullptr, EPI_ADD);
-            a.post.op = POST_RMSNORM;
-            a.post.x = m->x;
-            a.post.w = l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm;
-            a.post.n = c.hidden;
-            a.post.eps = c.eps;
-            a.post.xq = m->xq_h;
-            TRY(launch_gemv(a, EPI_ADD, s));
+            GemvArgs a = gemv(L.down.p, m->xq_act, nullptr, nullptr);
+            int epi;
+            residual_out(m, a, epi, nullptr, l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm, 1);
+            TRY(launch_gemv(a, epi, s));
         }
     }
     // lm_head with the fused argmax (main.zig:534, cpu.zig:477-483); the last CTA
-    // turns the argmax into the next step's token (generate.zig:217-244).
+    // turns the argmax into the next step's token (generate.zig:217-244), after
+    // the cross-rank argmax under tensor parallelism.
     {
-        const Proj &head = c.tie_embeddings ? m->embed : m->output;
-        GemvArgs a = gemv(head.p, m->xq_h, m->logits, nullptr, EPI_ARGMAX);
+        GemvArgs a = gemv(head_proj(m).p, m->xq_h, m->logits, nullptr);
         a.argmax64 = &m->state->argmax64;
-        a.post.op = POST_FINISH;
+        a.row_base = m->vocab_base;
+        a.post.op = m->opt.tp_size > 1 ? POST_TP_FINISH : POST_FINISH;
+        a.post.tp = m->tpc;
         a.post.state = m->state;
         a.post.forced = m->forced;
         a.post.out_tokens = m->out_tokens;
@@ -195,22 +223,35 @@ static int enqueue_head(cuq_model *m, const float *x_row, bool pdl) {
     const cuq_config &c = m->cfg;
     int rc = launch_rmsnorm_xq(x_row, m->final_norm, c.hidden, 1, c.eps, m->xq_h, nullptr, m->stream);
     if (rc) return rc;
-    const Proj &head = c.tie_embeddings ? m->embed : m->output;
+    const Proj &head = head_proj(m);
     GemvArgs a;
     a.w = &head.p;
     a.xq = m->xq_h;
     a.y = m->logits;
     a.argmax64 = &m->state->argmax64;
+    a.row_base = m->vocab_base;
     a.ws = m->ws;
     a.counters = m->counters;
     a.ksplit = gemv_pick_ksplit(head.p, m->sm_count);
     a.pdl = pdl;
     a.post.done = m->done;
-    a.post.op = POST_FINISH;
+    a.post.op = m->opt.tp_size > 1 ? POST_TP_FINISH : POST_FINISH;
+    a.post.tp = m->tpc;
     a.post.state = m->state;
     a.post.forced = m->forced;
     a.post.out_tokens = m->out_tokens;
     return launch_gemv(a, EPI_ARGMAX, m->stream);
+}
+
+// Row-parallel projection output of a prefill chunk under tensor parallelism:
+// the partial [n][hidden] goes to every rank, then x += sum + bias.
+static int prefill_allreduce(cuq_model *m, uint32_t n, const float *bias, int phase) {
+    const size_t count = (size_t)n * m->cfg.hidden;
+    int grid = 0;
+    int rc = launch_tp_push(m->tpc, phase, m->pf_part, count, &grid, m->stream);
+    if (rc) return rc;
+    return launch_tp_reduce_add(m->tpc, phase, (unsigned)(m->tpc.size * grid), m->pf_x, bias, m->cfg.hidden, count,
+                                m->tp_done, m->stream);
 }
 
 // Engine.prefill for one chunk of n <= max_chunk prompt positions starting at
@@ -218,9 +259,10 @@ static int enqueue_head(cuq_model *m, const float *x_row, bool pdl) {
 // over the chunk, attention is causal over the cache.  When `last` is set the
 // chunk's final position goes through the lm_head and sets the decode state.
 static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint32_t pos0, bool last) {
-    const cuq_config &c = m->cfg;
+    const cuq_config &c = m->cfg, &lc = m->lc;
+    const bool tp = m->opt.tp_size > 1;
     cudaStream_t s = m->stream;
-    const uint32_t qd = q_dim(c), kvd = kv_dim(c), qkvd = qd + 2 * kvd;
+    const uint32_t qd = q_dim(lc), kvd = kv_dim(lc), qkvd = qd + 2 * kvd;
     int rc;
 #define PTRY(x)                      \
     do {                             \
@@ -244,8 +286,8 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             PTRY(launch_qgemm(g, EPI_STORE, s));
         }
         PTRY(launch_rope_cache(m->pf_qkv, qkvd, m->pf_q, L.k_cache, L.v_cache, m->opt.max_seq, m->rope_cs, nullptr,
-                               pos0, n, c.heads, c.kv_heads, c.head_dim, c.rope_adjacent, s));
-        PTRY(launch_attention_prefill(m->pf_q, L.k_cache, L.v_cache, m->opt.max_seq, pos0, n, c.heads, c.kv_heads,
+                               pos0, n, lc.heads, lc.kv_heads, c.head_dim, c.rope_adjacent, s));
+        PTRY(launch_attention_prefill(m->pf_q, L.k_cache, L.v_cache, m->opt.max_seq, pos0, n, lc.heads, lc.kv_heads,
                                       c.head_dim, m->pf_h, m->pf_l, s));
         {
             QgemmArgs g;
@@ -253,11 +295,12 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             g.xh = m->pf_h;
             g.xl = m->pf_l;
             g.n = n;
-            g.y = m->pf_x;
+            g.y = tp ? m->pf_part : m->pf_x;
             g.ldy = c.hidden;
-            g.bias = L.o_bias;
+            g.bias = tp ? nullptr : L.o_bias;
             g.err = m->gemm_err;
-            PTRY(launch_qgemm(g, EPI_ADD, s));
+            PTRY(launch_qgemm(g, tp ? EPI_STORE : EPI_ADD, s));
+            if (tp) PTRY(prefill_allreduce(m, n, L.o_bias, 0));
         }
         PTRY(launch_rmsnorm_hilo(m->pf_x, L.ffn_norm, c.hidden, n, c.eps, m->pf_h, m->pf_l, s));
         if (L.gate_up_dual) {
@@ -283,7 +326,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             g.w = &L.up.p;
             g.y = m->pf_u;
             PTRY(launch_qgemm(g, EPI_STORE, s));
-            PTRY(launch_silu_hilo(m->pf_g, m->pf_u, (size_t)n * c.inter, m->pf_ah, m->pf_al, s));
+            PTRY(launch_silu_hilo(m->pf_g, m->pf_u, (size_t)n * lc.inter, m->pf_ah, m->pf_al, s));
         }
         {
             QgemmArgs g;
@@ -291,10 +334,11 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             g.xh = m->pf_ah;
             g.xl = m->pf_al;
             g.n = n;
-            g.y = m->pf_x;
+            g.y = tp ? m->pf_part : m->pf_x;
             g.ldy = c.hidden;
             g.err = m->gemm_err;
-            PTRY(launch_qgemm(g, EPI_ADD, s));
+            PTRY(launch_qgemm(g, tp ? EPI_STORE : EPI_ADD, s));
+            if (tp) PTRY(prefill_allreduce(m, n, nullptr, 1));
         }
     }
     if (last) PTRY(enqueue_head(m, m->pf_x + (size_t)(n - 1) * c.hidden, false));
@@ -356,21 +400,40 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
                   c.hidden, c.heads, c.kv_heads, c.head_dim, c.inter, c.vocab);
         return nullptr;
     }
-    cuq_model *m = new cuq_model();
-    m->cfg = c;
     cuq_options o{};
     if (opts) o = *opts;
     if (!o.max_seq) o.max_seq = 2048;
     if (!o.max_chunk) o.max_chunk = 512;
     if (!o.tp_size) o.tp_size = 1;
+    {
+        // Megatron split (column-parallel q/k/v/gate/up and lm_head rows,
+        // row-parallel o/down columns): whole KV heads and 16-row tiles per rank
+        const uint32_t tp = (uint32_t)o.tp_size;
+        if (o.tp_size < 1 || o.tp_size > TP_MAX || o.tp_rank < 0 || o.tp_rank >= o.tp_size || c.kv_heads % tp ||
+            (c.inter / tp) % 64 || c.inter % tp || c.vocab % (16 * tp) || (c.heads / tp * c.head_dim) % 64) {
+            set_error("cuq_model_create: tensor parallel %d/%d does not divide the model (kv_heads %u, inter %u, "
+                      "vocab %u)",
+                      o.tp_rank, o.tp_size, c.kv_heads, c.inter, c.vocab);
+            return nullptr;
+        }
+    }
+    cuq_model *m = new cuq_model();
+    m->cfg = c;
+    m->lc = c;
+    m->lc.heads = c.heads / o.tp_size;
+    m->lc.kv_heads = c.kv_heads / o.tp_size;
+    m->lc.inter = c.inter / o.tp_size;
+    m->lc.vocab = c.vocab / o.tp_size;
+    m->vocab_base = m->lc.vocab * (uint32_t)o.tp_rank;
     m->opt = o;
     m->sm_count = sm_count_current();
     m->layers.resize(c.layers);
-    const uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    const cuq_config &lc = m->lc;
+    const uint32_t qd = q_dim(lc), kvd = kv_dim(lc);
     bool ok = false;
     do {
         if (cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking) != cudaSuccess) break;
-        size_t kv_bytes = (size_t)c.kv_heads * o.max_seq * c.head_dim * sizeof(__half);
+        size_t kv_bytes = (size_t)lc.kv_heads * o.max_seq * c.head_dim * sizeof(__half);
         bool bad = false;
         for (auto &L : m->layers) {
             if (cudaMalloc(&L.k_cache, kv_bytes) != cudaSuccess || cudaMalloc(&L.v_cache, kv_bytes) != cudaSuccess ||
@@ -381,18 +444,18 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
         }
         if (bad) break;
         m->stats.kv_bytes = 2 * kv_bytes * c.layers;
-        m->attn_nsplit = attn_pick_nsplit(c.kv_heads, o.max_seq, m->sm_count);
+        m->attn_nsplit = attn_pick_nsplit(lc.kv_heads, o.max_seq, m->sm_count);
         if (cudaMalloc(&m->x, sizeof(float) * c.hidden) != cudaSuccess) break;
         if (cudaMalloc(&m->qkv, sizeof(float) * (qd + 2 * kvd)) != cudaSuccess) break;
         if (cudaMalloc(&m->q_rot, sizeof(float) * qd) != cudaSuccess) break;
-        if (cudaMalloc(&m->logits, sizeof(float) * c.vocab) != cudaSuccess) break;
-        if (cudaMalloc(&m->act, sizeof(float) * c.inter) != cudaSuccess) break;
-        if (cudaMalloc(&m->gate_buf, sizeof(float) * c.inter) != cudaSuccess) break;
-        if (cudaMalloc(&m->up_buf, sizeof(float) * c.inter) != cudaSuccess) break;
-        if (cudaMalloc(&m->attn_part, sizeof(float) * (size_t)m->attn_nsplit * c.heads * (c.head_dim + 2)) !=
+        if (cudaMalloc(&m->logits, sizeof(float) * lc.vocab) != cudaSuccess) break;
+        if (cudaMalloc(&m->act, sizeof(float) * lc.inter) != cudaSuccess) break;
+        if (cudaMalloc(&m->gate_buf, sizeof(float) * lc.inter) != cudaSuccess) break;
+        if (cudaMalloc(&m->up_buf, sizeof(float) * lc.inter) != cudaSuccess) break;
+        if (cudaMalloc(&m->attn_part, sizeof(float) * (size_t)m->attn_nsplit * lc.heads * (c.head_dim + 2)) !=
             cudaSuccess)
             break;
-        size_t xh = xq_halves(c.hidden), xa = xq_halves(qd), xi = xq_halves(c.inter);
+        size_t xh = xq_halves(c.hidden), xa = xq_halves(qd), xi = xq_halves(lc.inter);
         if (cudaMalloc(&m->xq_h, sizeof(__half) * xh) != cudaSuccess) break;
         if (cudaMalloc(&m->xq_attn, sizeof(__half) * xa) != cudaSuccess) break;
         if (cudaMalloc(&m->xq_act, sizeof(__half) * xi) != cudaSuccess) break;
@@ -405,9 +468,9 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
         if (cudaMalloc(&m->rope_cs, sizeof(float) * cs.size()) != cudaSuccess) break;
         if (cudaMemcpy(m->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice) != cudaSuccess) break;
         if (cudaMalloc(&m->done, sizeof(unsigned int)) != cudaSuccess) break;
-        if (cudaMalloc(&m->tickets, sizeof(unsigned int) * c.kv_heads) != cudaSuccess) break;
+        if (cudaMalloc(&m->tickets, sizeof(unsigned int) * lc.kv_heads) != cudaSuccess) break;
         cudaMemset(m->done, 0, sizeof(unsigned int));
-        cudaMemset(m->tickets, 0, sizeof(unsigned int) * c.kv_heads);
+        cudaMemset(m->tickets, 0, sizeof(unsigned int) * lc.kv_heads);
         if (cudaMalloc(&m->state, sizeof(StepState)) != cudaSuccess) break;
         cudaMemset(m->state, 0, sizeof(StepState));
         if (cudaMallocHost(&m->state_host, sizeof(StepState)) != cudaSuccess) break;
@@ -420,15 +483,38 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
             if (cudaMalloc(&m->pf_x, sizeof(float) * C * c.hidden) != cudaSuccess) break;
             if (cudaMalloc(&m->pf_qkv, sizeof(float) * C * (qd + 2 * kvd)) != cudaSuccess) break;
             if (cudaMalloc(&m->pf_q, sizeof(float) * C * qd) != cudaSuccess) break;
-            if (cudaMalloc(&m->pf_g, sizeof(float) * C * c.inter) != cudaSuccess) break;
-            if (cudaMalloc(&m->pf_u, sizeof(float) * C * c.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_g, sizeof(float) * C * lc.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_u, sizeof(float) * C * lc.inter) != cudaSuccess) break;
             if (cudaMalloc(&m->pf_h, sizeof(__half) * C * wide) != cudaSuccess) break;
             if (cudaMalloc(&m->pf_l, sizeof(__half) * C * wide) != cudaSuccess) break;
-            if (cudaMalloc(&m->pf_ah, sizeof(__half) * C * c.inter) != cudaSuccess) break;
-            if (cudaMalloc(&m->pf_al, sizeof(__half) * C * c.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_ah, sizeof(__half) * C * lc.inter) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_al, sizeof(__half) * C * lc.inter) != cudaSuccess) break;
             if (cudaMalloc(&m->pf_ids, sizeof(uint32_t) * C) != cudaSuccess) break;
             if (cudaMalloc(&m->gemm_err, sizeof(int)) != cudaSuccess) break;
             cudaMemset(m->gemm_err, 0, sizeof(int));
+        }
+        if (o.tp_size > 1) {
+            // communication buffer: 2 phase regions of [tp][max_chunk * hidden]
+            // fp32 slots, [tp] argmax keys, 4 counters (plain cudaMalloc: IPC-exportable)
+            const size_t slot = (size_t)o.max_chunk * c.hidden;
+            TpComm &t = m->tpc;
+            t.rank = o.tp_rank;
+            t.size = o.tp_size;
+            t.slot_floats = slot;
+            t.off_phase[0] = 0;
+            t.off_phase[1] = round256(sizeof(float) * slot * o.tp_size);
+            t.off_am = t.off_phase[1] + round256(sizeof(float) * slot * o.tp_size);
+            t.off_ctr = t.off_am + 256;
+            m->tp_bytes = t.off_ctr + 256;
+            if (cudaMalloc(&m->tp_buf, m->tp_bytes) != cudaSuccess) break;
+            if (cudaMemset(m->tp_buf, 0, m->tp_bytes) != cudaSuccess) break;
+            if (cudaMalloc(&m->tp_err, sizeof(int)) != cudaSuccess) break;
+            if (cudaMalloc(&m->tp_done, sizeof(unsigned int)) != cudaSuccess) break;
+            if (cudaMalloc(&m->pf_part, sizeof(float) * slot) != cudaSuccess) break;
+            cudaMemset(m->tp_err, 0, sizeof(int));
+            cudaMemset(m->tp_done, 0, sizeof(unsigned int));
+            t.err = m->tp_err;
+            t.peer[t.rank] = m->tp_buf;
         }
         if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess) break;
         ok = true;
@@ -479,6 +565,38 @@ int cuq_upload_tensor(cuq_model *m, int layer, int role, int ggml_type, const vo
         set_error("InvalidTensorShape: %zu bytes for %u x %u of type %d", nbytes, rows, cols, ggml_type);
         return CUQ_EINVAL;
     }
+    // tensor parallelism: keep this rank's shard only (rows for column-parallel
+    // projections and the lm_head, whole-block columns for o and down)
+    std::vector<uint8_t> shard;
+    if (m->opt.tp_size > 1 && role != CUQ_ROLE_EMBED) {
+        const cuq_config &lc = m->lc;
+        const uint32_t rank = (uint32_t)m->opt.tp_rank, lqd = q_dim(lc), lkvd = kv_dim(lc);
+        uint32_t r0 = 0, r1 = rows, c0 = 0, c1 = cols;
+        switch (role) {
+        case CUQ_ROLE_Q: r0 = rank * lqd; r1 = r0 + lqd; break;
+        case CUQ_ROLE_K: case CUQ_ROLE_V: r0 = rank * lkvd; r1 = r0 + lkvd; break;
+        case CUQ_ROLE_GATE: case CUQ_ROLE_UP: r0 = rank * lc.inter; r1 = r0 + lc.inter; break;
+        case CUQ_ROLE_OUTPUT: r0 = m->vocab_base; r1 = r0 + lc.vocab; break;
+        case CUQ_ROLE_O: c0 = rank * lqd; c1 = c0 + lqd; break;
+        case CUQ_ROLE_DOWN: c0 = rank * lc.inter; c1 = c0 + lc.inter; break;
+        default: break;
+        }
+        const size_t row_bytes = (size_t)(cols / epb) * bpb;
+        if (c0 % epb || c1 % epb) {
+            set_error("tensor parallel: columns [%u, %u) of role %d are not whole blocks of %d", c0, c1, role, epb);
+            return CUQ_EINVAL;
+        }
+        const size_t lrow_bytes = (size_t)((c1 - c0) / epb) * bpb;
+        shard.resize((size_t)(r1 - r0) * lrow_bytes);
+        const uint8_t *src = static_cast<const uint8_t *>(raw_host);
+        for (uint32_t r = r0; r < r1; r++)
+            memcpy(shard.data() + (size_t)(r - r0) * lrow_bytes, src + (size_t)r * row_bytes + (size_t)(c0 / epb) * bpb,
+                   lrow_bytes);
+        raw_host = shard.data();
+        nbytes = shard.size();
+        rows = r1 - r0;
+        cols = c1 - c0;
+    }
     PendingTensor *t;
     if (role == CUQ_ROLE_EMBED)
         t = &m->pend_embed;
@@ -503,6 +621,30 @@ int cuq_upload_f32(cuq_model *m, int layer, int role, const float *v, size_t n) 
     CUQ_CHECK_ARG(m && v, "cuq_upload_f32: null argument");
     const cuq_config &c = m->cfg;
     uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    // tensor parallelism: q/k/v biases follow their projection's row shard
+    const uint32_t lqd = q_dim(m->lc), lkvd = kv_dim(m->lc), rank = (uint32_t)m->opt.tp_rank;
+    if (m->opt.tp_size > 1 && (role == CUQ_ROLE_Q_BIAS || role == CUQ_ROLE_K_BIAS || role == CUQ_ROLE_V_BIAS)) {
+        const size_t want_full = role == CUQ_ROLE_Q_BIAS ? qd : kvd;
+        if (n != want_full) {
+            set_error("DimensionMismatch: role %d has %zu values, expected %zu", role, n, want_full);
+            return CUQ_EINVAL;
+        }
+        CUQ_CHECK_ARG(layer >= 0 && (uint32_t)layer < c.layers, "cuq_upload_f32: layer %d out of range", layer);
+        float **slot = &m->layers[layer].qkv_bias;
+        const size_t total = lqd + 2 * lkvd;
+        size_t off = 0, len = lqd, src = (size_t)rank * lqd;
+        if (role != CUQ_ROLE_Q_BIAS) {
+            off = role == CUQ_ROLE_K_BIAS ? lqd : lqd + lkvd;
+            len = lkvd;
+            src = (size_t)rank * lkvd;
+        }
+        if (!*slot) {
+            CUQ_CUDA_TRY(cudaMalloc(slot, sizeof(float) * total));
+            CUQ_CUDA_TRY(cudaMemset(*slot, 0, sizeof(float) * total));
+        }
+        CUQ_CUDA_TRY(cudaMemcpy(*slot + off, v + src, sizeof(float) * len, cudaMemcpyHostToDevice));
+        return CUQ_OK;
+    }
     float **slot = nullptr;
     size_t want = 0, off = 0, total = 0;
     if (role == CUQ_ROLE_FINAL_NORM) {
@@ -537,9 +679,13 @@ int cuq_model_finalize(cuq_model *m) {
     CUQ_CHECK_ARG(m, "cuq_model_finalize: null model");
     if (m->finalized) return CUQ_OK;
     const cuq_config &c = m->cfg;
-    const uint32_t qd = q_dim(c), kvd = kv_dim(c);
+    const uint32_t qd = q_dim(m->lc), kvd = kv_dim(m->lc);
     cudaStream_t s = m->stream;
     int rc;
+    if (m->opt.tp_size > 1 && !m->tp_connected) {
+        set_error("cuq_model_finalize: tensor-parallel model not connected (cuq_tp_connect first)");
+        return CUQ_ENOTREADY;
+    }
     if (!m->pend_embed.raw) {
         set_error("MissingTensor: token_embd.weight");
         return CUQ_EINVAL;
@@ -611,15 +757,23 @@ int cuq_model_finalize(cuq_model *m) {
         account(L.down.p, 0);
         for (int r = 0; r < 7; r++) free_pending(L.pend[r]);
     }
+    if (c.tie_embeddings && m->opt.tp_size > 1) {
+        // tied lm_head under tensor parallelism: this rank's vocab rows of the
+        // embedding table become its own head weight
+        PendingTensor view = m->pend_embed;
+        const size_t row_bytes = view.nbytes / view.rows;
+        view.raw += (size_t)m->vocab_base * row_bytes;
+        view.rows = m->lc.vocab;
+        view.nbytes = (size_t)m->lc.vocab * row_bytes;
+        if ((rc = build_proj(m->output, {&view}, s))) return rc;
+    }
     if ((rc = build_proj(m->embed, {&m->pend_embed}, s))) return rc;
     free_pending(m->pend_embed);
     if (!c.tie_embeddings) {
         if ((rc = build_proj(m->output, {&m->pend_output}, s))) return rc;
         free_pending(m->pend_output);
-        account(m->output.p, 0);
-    } else {
-        account(m->embed.p, 0);
     }
+    account(head_proj(m).p, 0);
     m->ws_floats = ws_need;
     m->n_counters = ctr_need + 1;
     if (ws_need) CUQ_CUDA_TRY(cudaMalloc(&m->ws, sizeof(float) * ws_need));
@@ -648,6 +802,47 @@ int cuq_model_finalize(cuq_model *m) {
     return CUQ_OK;
 }
 
+int cuq_tp_comm_handle(cuq_model *m, void *handle_out) {
+    CUQ_CHECK_ARG(m && handle_out, "cuq_tp_comm_handle: null argument");
+    if (m->opt.tp_size < 2) {
+        set_error("cuq_tp_comm_handle: model is not tensor parallel");
+        return CUQ_EINVAL;
+    }
+    cudaIpcMemHandle_t h;
+    CUQ_CUDA_TRY(cudaIpcGetMemHandle(&h, m->tp_buf));
+    static_assert(sizeof(h) == CUQ_TP_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle_out, &h, sizeof(h));
+    return CUQ_OK;
+}
+
+int cuq_tp_connect(cuq_model *m, const void *handles) {
+    CUQ_CHECK_ARG(m && handles, "cuq_tp_connect: null argument");
+    if (m->opt.tp_size < 2 || m->tp_connected) {
+        set_error("cuq_tp_connect: model is not tensor parallel or already connected");
+        return CUQ_EINVAL;
+    }
+    const uint8_t *hb = static_cast<const uint8_t *>(handles);
+    for (int r = 0; r < m->tpc.size; r++) {
+        if (r == m->tpc.rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, hb + (size_t)r * CUQ_TP_HANDLE_BYTES, sizeof(h));
+        void *p = nullptr;
+        cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+        if (e != cudaSuccess) {
+            for (int q = 0; q < r; q++)
+                if (q != m->tpc.rank && m->tpc.peer[q]) {
+                    cudaIpcCloseMemHandle(m->tpc.peer[q]);
+                    m->tpc.peer[q] = nullptr;
+                }
+            set_error("cuq_tp_connect: rank %d buffer: %s", r, cudaGetErrorString(e));
+            return CUQ_ECUDA;
+        }
+        m->tpc.peer[r] = static_cast<uint8_t *>(p);
+    }
+    m->tp_connected = true;
+    return CUQ_OK;
+}
+
 int cuq_model_get_config(const cuq_model *m, cuq_config *out) {
     CUQ_CHECK_ARG(m && out, "cuq_model_get_config: null argument");
     *out = m->cfg;
@@ -657,7 +852,7 @@ int cuq_model_get_config(const cuq_model *m, cuq_config *out) {
 static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint32_t *argmax_out, double *ms_out) {
     CUQ_CUDA_TRY(cudaEventRecord(m->ev1, m->stream));
     if (logits_host)
-        CUQ_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * m->cfg.vocab, cudaMemcpyDeviceToHost,
+        CUQ_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * m->lc.vocab, cudaMemcpyDeviceToHost,
                                      m->stream));
     if (n_steps)
         CUQ_CUDA_TRY(cudaMemcpyAsync(m->out_host, m->out_tokens, sizeof(uint32_t) * n_steps, cudaMemcpyDeviceToHost,
@@ -667,6 +862,15 @@ static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint3
     cudaEventElapsedTime(&ms, m->ev0, m->ev1);
     if (ms_out) *ms_out += ms;
     if (argmax_out && n_steps) *argmax_out = m->out_host[n_steps - 1];
+    if (m->tp_err) {
+        int herr = 0;
+        CUQ_CUDA_TRY(cudaMemcpy(&herr, m->tp_err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (herr) {
+            cudaMemset(m->tp_err, 0, sizeof(int));
+            set_error("tensor parallel: a peer did not arrive within the wait limit");
+            return CUQ_ETIMEOUT;
+        }
+    }
     return CUQ_OK;
 }
 
@@ -785,7 +989,7 @@ int cuq_reset(cuq_model *m) {
     CUQ_CHECK_ARG(m, "cuq_reset: null model");
     // Engine.reset (engine.zig:1479): the cache is simply overwritten from position 0
     // by the next prefill; clearing it keeps stale rows from ever being read.
-    size_t kv_bytes = (size_t)m->cfg.kv_heads * m->opt.max_seq * m->cfg.head_dim * sizeof(__half);
+    size_t kv_bytes = (size_t)m->lc.kv_heads * m->opt.max_seq * m->cfg.head_dim * sizeof(__half);
     for (auto &L : m->layers) {
         CUQ_CUDA_TRY(cudaMemsetAsync(L.k_cache, 0, kv_bytes, m->stream));
         CUQ_CUDA_TRY(cudaMemsetAsync(L.v_cache, 0, kv_bytes, m->stream));
@@ -829,9 +1033,12 @@ void cuq_model_free(cuq_model *m) {
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
                     m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets,
                     m->pf_x,       m->pf_qkv, m->pf_q, m->pf_g, m->pf_u, m->pf_h, m->pf_l, m->pf_ah, m->pf_al,
-                    m->pf_ids,     m->gemm_err};
+                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part};
     for (void *b : bufs)
         if (b) cudaFree(b);
+    for (int r = 0; r < m->tpc.size && m->tp_connected; r++)
+        if (r != m->tpc.rank && m->tpc.peer[r]) cudaIpcCloseMemHandle(m->tpc.peer[r]);
+    if (m->tp_buf) cudaFree(m->tp_buf);
     if (m->state_host) cudaFreeHost(m->state_host);
     if (m->out_host) cudaFreeHost(m->out_host);
     if (m->ev0) cudaEventDestroy(m->ev0);

@@ -34,6 +34,8 @@ struct Layer {
 
 struct cuq_model {
     cuq_config cfg{};
+    cuq_config lc{};             // this rank's geometry: heads, kv_heads, inter, vocab divided by tp_size
+    uint32_t vocab_base = 0;     // first lm_head row (global token id) held by this rank
     cuq_options opt{};
     bool finalized = false;
     int sm_count = 148;
@@ -64,6 +66,15 @@ struct cuq_model {
     __half *pf_h = nullptr, *pf_l = nullptr, *pf_ah = nullptr, *pf_al = nullptr;
     uint32_t *pf_ids = nullptr;
     int *gemm_err = nullptr;
+
+    // tensor parallelism (opt.tp_size > 1)
+    uint8_t *tp_buf = nullptr;                   // this rank's communication buffer (IPC-exported)
+    size_t tp_bytes = 0;
+    cuq::TpComm tpc;                             // peers mapped by cuq_tp_connect
+    bool tp_connected = false;
+    int *tp_err = nullptr;                       // wait time-outs (device)
+    unsigned int *tp_done = nullptr;             // grid completion of the prefill reduce kernel
+    float *pf_part = nullptr;                    // [max_chunk][hidden] partial of o / down
 
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;

@@ -23,9 +23,13 @@ def _ptr(a):
 class Engine:
     """A model resident on one GPU, built from a GGUF file or uploaded tensors."""
 
-    def __init__(self, handle, cfg):
+    def __init__(self, handle, cfg, tp_rank=0, tp_size=1):
         self._h = handle
         self.cfg = cfg  # CuqConfig
+        self._tp = (tp_rank, tp_size)
+        # logits returned by forward/prefill: this rank's vocab slice
+        self.local_vocab = cfg.vocab // tp_size
+        self.vocab_base = self.local_vocab * tp_rank
 
     @classmethod
     def from_gguf(cls, path, max_seq=2048, use_graphs=True, device=0, max_chunk=512):
@@ -40,8 +44,14 @@ class Engine:
         return cls(h, cfg)
 
     @classmethod
-    def from_synth(cls, model, max_seq=None, use_graphs=True, device=0, max_chunk=512):
-        """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads)."""
+    def from_synth(cls, model, max_seq=None, use_graphs=True, device=0, max_chunk=512, tp_rank=0, tp_size=1,
+                   exchange=None):
+        """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads).
+
+        Tensor parallel (tp_size > 1, one process per GPU): every rank uploads
+        the full tensors and keeps its shard; `exchange(handle_bytes)` must
+        return the list of every rank's handle in rank order (an all-gather
+        over the caller's process group)."""
         L = rt.load()
         rt.init(device)
         c = model.cfg
@@ -49,11 +59,11 @@ class Engine:
                            head_dim=c.head_dim, inter=c.inter, vocab=c.vocab, eps=c.eps, rope_theta=c.rope_theta,
                            rope_adjacent=int(c.rope_adjacent), tie_embeddings=int(c.tie_embeddings))
         opts = rt.CuqOptions(max_seq=max_seq or c.max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs),
-                             tp_rank=0, tp_size=1)
+                             tp_rank=tp_rank, tp_size=tp_size)
         h = L.cuq_model_create(ctypes.byref(cfg), ctypes.byref(opts))
         if not h:
             raise rt.CuqError(rt.EINVAL, rt.last_error())
-        eng = cls(h, cfg)
+        eng = cls(h, cfg, tp_rank, tp_size)
         try:
             for t in model.tensors():
                 buf = np.frombuffer(t.data, dtype=np.uint8)
@@ -63,11 +73,27 @@ class Engine:
                 else:
                     rt.check(L.cuq_upload_tensor(h, t.layer, rt.ROLE[t.role], t.ggml_type, _ptr(buf), buf.size,
                                                  t.rows, t.cols))
+            if tp_size > 1:
+                eng.tp_connect(exchange)
             rt.check(L.cuq_model_finalize(h))
         except Exception:
             eng.close()
             raise
         return eng
+
+    def tp_connect(self, exchange):
+        """Publish this rank's communication buffer and map every peer's."""
+        L = rt.load()
+        mine = ctypes.create_string_buffer(rt.TP_HANDLE_BYTES)
+        rt.check(L.cuq_tp_comm_handle(self._h, mine))
+        handles = exchange(mine.raw)
+        blob = ctypes.create_string_buffer(b"".join(handles), rt.TP_HANDLE_BYTES * len(handles))
+        rt.check(L.cuq_tp_connect(self._h, blob))
+
+    @property
+    def tp_size(self):
+        o = getattr(self, "_tp", (0, 1))
+        return o[1]
 
     def close(self):
         if getattr(self, "_h", None):
@@ -79,7 +105,7 @@ class Engine:
 
     def forward(self, token, pos, want_logits=True):
         """Engine.forward: one decode step; returns (logits or None, argmax)."""
-        logits = np.empty(self.cfg.vocab, dtype=np.float32) if want_logits else None
+        logits = np.empty(self.local_vocab, dtype=np.float32) if want_logits else None
         am = ctypes.c_uint32(0)
         rt.check(rt.load().cuq_forward(self._h, token, pos, _ptr(logits) if want_logits else None,
                                        ctypes.byref(am)))
@@ -88,7 +114,7 @@ class Engine:
     def prefill(self, ids, start_pos=0, want_logits=True):
         """Engine.prefill: logits (and argmax) of the last prompt token."""
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
-        logits = np.empty(self.cfg.vocab, dtype=np.float32) if want_logits else None
+        logits = np.empty(self.local_vocab, dtype=np.float32) if want_logits else None
         am = ctypes.c_uint32(0)
         rt.check(rt.load().cuq_prefill(self._h, _ptr(ids), ids.size, start_pos,
                                        _ptr(logits) if want_logits else None, ctypes.byref(am)))

@@ -12,6 +12,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libcuq.so")
 
 OK, EINVAL, ENOMEM, ECUDA, ECONTEXT, EUNSUPPORTED, ETIMEOUT, EFORMAT, ENOTREADY = 0, -1, -2, -3, -4, -5, -6, -7, -8
+TP_HANDLE_BYTES = 64
 
 ROLE = {"q": 0, "k": 1, "v": 2, "o": 3, "gate": 4, "up": 5, "down": 6, "attn_norm": 7, "ffn_norm": 8,
         "q_bias": 9, "k_bias": 10, "v_bias": 11, "o_bias": 12, "embed": 13, "output": 14, "final_norm": 15}
@@ -50,6 +51,10 @@ SIGNATURES = [
     ("cuq_model_finalize", I32, [P]),
     ("cuq_model_load_gguf", P, [ctypes.c_char_p, P]),
     ("cuq_model_get_config", I32, [P, P]),
+    ("cuq_tp_comm_handle", I32, [P, P]),
+    ("cuq_tp_connect", I32, [P, P]),
+    ("cuq_shard_rows", I32, [I32, U32, U32, U32, U32, P, P]),
+    ("cuq_shard_cols", I32, [I32, U32, U32, U32, U32, P, P]),
     ("cuq_forward", I32, [P, U32, U32, P, P]),
     ("cuq_prefill", I32, [P, P, U32, U32, P, P]),
     ("cuq_generate", I32, [P, P, U32, U32, P]),

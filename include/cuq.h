@@ -164,7 +164,8 @@ typedef struct {
     uint32_t max_seq;        /* KV-cache positions (engine.zig:447-458); default 2048 */
     uint32_t max_chunk;      /* largest prefill chunk; default 512 */
     int32_t use_graphs;      /* capture the decode step in a CUDA graph (default 1) */
-    int32_t tp_rank, tp_size;/* tensor parallel slot (tp_size 1 = single GPU) */
+    int32_t tp_rank, tp_size;/* tensor parallel slot (tp_size 1 = single GPU; up to 8, one
+                              * process per GPU; see cuq_tp_connect) */
 } cuq_options;
 
 /* Tensor roles for cuq_upload_*. */
@@ -212,8 +213,34 @@ int cuq_upload_f32(cuq_model *m, int layer, int role, const float *v_host, size_
 /* Check every tensor is present and build the device-resident step. */
 int cuq_model_finalize(cuq_model *m);
 /* Parse a GGUF v2/v3 file (gguf.zig:328-656), read its config (load_gguf.loadConfig,
- * load_gguf.zig:96-302) and upload every tensor raw.  Returns a finalized model. */
+ * load_gguf.zig:96-302) and upload every tensor raw.  Returns a finalized model,
+ * except with opts->tp_size > 1: then the caller runs cuq_tp_connect and
+ * cuq_model_finalize. */
 cuq_model *cuq_model_load_gguf(const char *path, const cuq_options *opts);
+
+/* Tensor parallelism (Megatron split of BASELINE config 5; the reference engine
+ * is single-device, so these have no counterpart there).  One process per GPU,
+ * each creating its model with the same config and tp_size and its own tp_rank,
+ * uploading the FULL tensors (each rank keeps its shard: q/k/v/gate/up and the
+ * lm_head by rows, o/down by whole-block columns; embeddings and norms are
+ * replicated).  Before cuq_model_finalize every rank publishes its
+ * communication buffer's handle (CUQ_TP_HANDLE_BYTES opaque bytes) and passes
+ * all ranks' handles, in rank order, to cuq_tp_connect.  The ranks then exchange
+ * partial sums over NVLink inside the step's kernels (no library collective);
+ * every rank must make the same calls with the same arguments, in the same
+ * order.  cuq_forward/cuq_prefill return this rank's slice of the logits
+ * (vocab / tp_size values starting at token id tp_rank * vocab / tp_size); the
+ * argmax and generated tokens are global.  A peer that does not arrive within
+ * 10 s ends the call with CUQ_ETIMEOUT. */
+#define CUQ_TP_HANDLE_BYTES 64
+int cuq_tp_comm_handle(cuq_model *m, void *handle_out);
+int cuq_tp_connect(cuq_model *m, const void *handles);
+/* Host-only helpers (no GPU needed): copy rows [r0, r1), or whole-block columns
+ * [c0, c1) of every row, of a raw [rows][cols] GGUF tensor into out. */
+int cuq_shard_rows(int ggml_type, uint32_t rows, uint32_t cols, uint32_t r0, uint32_t r1,
+                   const void *raw, void *out);
+int cuq_shard_cols(int ggml_type, uint32_t rows, uint32_t cols, uint32_t c0, uint32_t c1,
+                   const void *raw, void *out);
 int cuq_model_get_config(const cuq_model *m, cuq_config *out);
 
 /* Engine.forward (engine.zig:547-819): one decode step for `token` at `pos`.
