@@ -584,25 +584,37 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
+    extern __shared__ float4 rn_stage[];  // n floats when the launch gave them (fast path)
+    const bool fast = p.post.n % 16 == 0 && p.post.n <= RN_MAX;
     if (p.post.op == POST_TP_REDUCE) {
         // every rank's CTAs pushed once: x += sum over ranks (+ bias), then the RMSNorm
         const TpComm &tp = p.post.tp;
         __shared__ int ok;
         if (t == 0) ok = tp_wait(tp, p.post.tp_phase, (unsigned)tp.size * gridDim.x);
         __syncthreads();
-        if (ok) {
-            for (uint32_t i = t; i < p.post.n; i += blockDim.x) {
-                float sum = tp_sum(tp, p.post.tp_phase, i);
-                if (p.post.bias) sum = sum + p.post.bias[i];
-                p.post.xr[i] = __ldcg(p.post.xr + i) + sum;
+        if (fast) {
+            reduce_norm_xq_block(p.post.xr, ok ? &tp : nullptr, p.post.tp_phase, p.post.bias, p.post.w, p.post.n,
+                                 p.post.eps, p.post.xq, xq_pad(p.post.n), rn_stage);
+        } else {
+            if (ok) {
+                for (uint32_t i = t; i < p.post.n; i += blockDim.x) {
+                    float sum = tp_sum(tp, p.post.tp_phase, i);
+                    if (p.post.bias) sum = sum + p.post.bias[i];
+                    p.post.xr[i] = __ldcg(p.post.xr + i) + sum;
+                }
             }
+            __threadfence();
+            __syncthreads();
+            rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
         }
-        __threadfence();
         __syncthreads();
         if (t == 0) tp_reset(tp, p.post.tp_phase);
-        rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
     } else if (p.post.op == POST_RMSNORM) {
-        rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
+        if (fast)
+            reduce_norm_xq_block(const_cast<float *>(p.post.x), nullptr, 0, nullptr, p.post.w, p.post.n, p.post.eps,
+                                 p.post.xq, xq_pad(p.post.n), rn_stage);
+        else
+            rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
     } else if (p.post.op == POST_FINISH) {
         if (t == 0) finish_step(p.post.state, p.post.forced, p.post.out_tokens);
     } else if (p.post.op == POST_TP_FINISH) {
@@ -633,7 +645,10 @@ cudaError_t launch_kw(const GemvArgs &a, const KArgs &k, cudaStream_t s) {
     constexpr int D = EPI == EPI_SILU_XQ ? 1 : TT::DEPTH;
     constexpr int TPC = 4 / KW;
     dim3 grid((a.w->rows / 16 + TPC - 1) / TPC, k.ksplit);
-    return launch_maybe_pdl(gemv_kernel<TT, EPI, KW, D>, grid, dim3(128), 0, s, a.pdl, k);
+    // the RMSNorm post-ops stage x in dynamic shared memory (reduce_norm_xq_block)
+    const bool norm = a.post.op == POST_RMSNORM || a.post.op == POST_TP_REDUCE;
+    const size_t smem = norm && a.post.n % 16 == 0 && a.post.n <= RN_MAX ? sizeof(float) * a.post.n : 0;
+    return launch_maybe_pdl(gemv_kernel<TT, EPI, KW, D>, grid, dim3(128), smem, s, a.pdl, k);
 }
 
 template <class TT, int EPI>

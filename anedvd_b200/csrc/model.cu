@@ -200,6 +200,9 @@ static int enqueue_step(cuq_model *m) {
         TRY(launch_gemv(a, EPI_ARGMAX, s));
     }
     m->stats.kernels_per_step = nk;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(s, &cap);
+    if (cap == cudaStreamCaptureStatusNone) m->stats.kernel_launches += nk;
 #undef TRY
     return CUQ_OK;
 }
@@ -209,6 +212,7 @@ static int run_steps(cuq_model *m, uint32_t n) {
         if (m->graph_exec) {
             CUQ_CUDA_TRY(cudaGraphLaunch(m->graph_exec, m->stream));
             m->stats.graph_replays++;
+            m->stats.kernel_launches += m->stats.kernels_per_step;
         } else {
             int rc = enqueue_step(m);
             if (rc) return rc;
@@ -268,6 +272,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
     do {                             \
         rc = (x);                    \
         if (rc != CUQ_OK) return rc; \
+        m->stats.kernel_launches++;  \
     } while (0)
     PTRY(launch_embed_rows(m->embed.p, ids_dev, n, m->pf_x, s));
     for (uint32_t l = 0; l < c.layers; l++) {
@@ -300,7 +305,10 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             g.bias = tp ? nullptr : L.o_bias;
             g.err = m->gemm_err;
             PTRY(launch_qgemm(g, tp ? EPI_STORE : EPI_ADD, s));
-            if (tp) PTRY(prefill_allreduce(m, n, L.o_bias, 0));
+            if (tp) {
+                PTRY(prefill_allreduce(m, n, L.o_bias, 0));
+                m->stats.kernel_launches++;  // push + reduce
+            }
         }
         PTRY(launch_rmsnorm_hilo(m->pf_x, L.ffn_norm, c.hidden, n, c.eps, m->pf_h, m->pf_l, s));
         if (L.gate_up_dual) {
@@ -338,10 +346,16 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             g.ldy = c.hidden;
             g.err = m->gemm_err;
             PTRY(launch_qgemm(g, tp ? EPI_STORE : EPI_ADD, s));
-            if (tp) PTRY(prefill_allreduce(m, n, nullptr, 1));
+            if (tp) {
+                PTRY(prefill_allreduce(m, n, nullptr, 1));
+                m->stats.kernel_launches++;  // push + reduce
+            }
         }
     }
-    if (last) PTRY(enqueue_head(m, m->pf_x + (size_t)(n - 1) * c.hidden, false));
+    if (last) {
+        PTRY(enqueue_head(m, m->pf_x + (size_t)(n - 1) * c.hidden, false));
+        m->stats.kernel_launches++;  // final norm + lm_head
+    }
 #undef PTRY
     return CUQ_OK;
 }

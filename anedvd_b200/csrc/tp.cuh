@@ -78,6 +78,114 @@ __device__ __forceinline__ float tp_sum(const TpComm &t, int ph, size_t i) {
     return s;
 }
 
+// Residual update + RMSNorm -> xq for the GEMV post-ops (one CTA, n % 16 == 0,
+// n <= RN_MAX): x += (sum over ranks of the phase-ph partials + bias) when tp
+// is set, then cpu.rmsnorm (cpu.zig:11-18) of x split into xq hi/lo with per-16
+// sums.  x goes through `stage` (n floats of dynamic shared memory) so it is
+// read from global memory once; loads are issued four float4 at a time per
+// thread, so the post-op costs a few memory round trips, not one per element.
+constexpr uint32_t RN_MAX = 8192;
+__device__ __forceinline__ void reduce_norm_xq_block(float *x, const TpComm *tp, int ph, const float *bias,
+                                                     const float *w, uint32_t n, float eps, __half *xq,
+                                                     uint32_t kpad, float4 *stage) {
+    constexpr int U = 4;
+    const int t = threadIdx.x, B = blockDim.x;
+    const uint32_t n4 = n / 4;
+    float ss = 0.f;
+    for (uint32_t base = 0; base < n4; base += U * B) {
+        float4 v[U];
+#pragma unroll
+        for (int k = 0; k < U; k++) {
+            const uint32_t i4 = base + t + k * B;
+            v[k] = i4 < n4 ? __ldcg(reinterpret_cast<const float4 *>(x) + i4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (tp) {
+            float4 sm[U];
+#pragma unroll
+            for (int k = 0; k < U; k++) sm[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int r = 0; r < tp->size; r++) {  // rank order: identical sums on every rank
+                const float4 *src = reinterpret_cast<const float4 *>(tp_slot(*tp, tp->rank, ph, r));
+#pragma unroll
+                for (int k = 0; k < U; k++) {
+                    const uint32_t i4 = base + t + k * B;
+                    if (i4 < n4) {
+                        const float4 q = __ldcv(src + i4);
+                        sm[k].x += q.x;
+                        sm[k].y += q.y;
+                        sm[k].z += q.z;
+                        sm[k].w += q.w;
+                    }
+                }
+            }
+#pragma unroll
+            for (int k = 0; k < U; k++) {
+                const uint32_t i4 = base + t + k * B;
+                if (i4 < n4) {
+                    if (bias) {
+                        const float4 b = reinterpret_cast<const float4 *>(bias)[i4];
+                        sm[k].x = sm[k].x + b.x;
+                        sm[k].y = sm[k].y + b.y;
+                        sm[k].z = sm[k].z + b.z;
+                        sm[k].w = sm[k].w + b.w;
+                    }
+                    v[k].x = v[k].x + sm[k].x;
+                    v[k].y = v[k].y + sm[k].y;
+                    v[k].z = v[k].z + sm[k].z;
+                    v[k].w = v[k].w + sm[k].w;
+                    reinterpret_cast<float4 *>(x)[i4] = v[k];
+                }
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; k++) {
+            const uint32_t i4 = base + t + k * B;
+            if (i4 < n4) stage[i4] = v[k];
+            ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
+        }
+    }
+    __shared__ float part[32];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    __syncthreads();
+    if ((t & 31) == 0) part[t >> 5] = ss;
+    __syncthreads();
+    if (t < 32) {
+        float a = t < (B >> 5) ? part[t] : 0.f;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+        if (t == 0) part[0] = a;
+    }
+    __syncthreads();
+    const float inv = 1.0f / sqrtf(part[0] / (float)n + eps);
+    float *sums = xq_sums(xq, kpad);
+    for (uint32_t base = 0; base < n4; base += B) {  // uniform trip count: shuffles below
+        const uint32_t i4 = base + t;
+        float grp = 0.f;
+        if (i4 < n4) {
+            const float4 v = stage[i4];
+            const float4 wv = reinterpret_cast<const float4 *>(w)[i4];
+            const float f[4] = {(v.x * inv) * wv.x, (v.y * inv) * wv.y, (v.z * inv) * wv.z, (v.w * inv) * wv.w};
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const uint32_t i = 4 * i4 + e;
+                const __half hi = __float2half_rn(f[e]);
+                xq[xq_pos(i)] = hi;
+                xq[kpad + xq_pos(i)] = __float2half_rn(f[e] - __half2float(hi));
+            }
+            grp = (f[0] + f[1]) + (f[2] + f[3]);
+        }
+        // 16 consecutive columns = the float4s of 4 consecutive threads
+        grp += __shfl_xor_sync(0xffffffffu, grp, 1);
+        grp += __shfl_xor_sync(0xffffffffu, grp, 2);
+        if (i4 < n4 && (i4 & 3u) == 0) sums[i4 >> 2] = grp;
+    }
+    for (uint32_t i = n + t; i < kpad; i += B) {  // zero tail (and its sums)
+        xq[xq_pos(i)] = __float2half_rn(0.f);
+        xq[kpad + xq_pos(i)] = __float2half_rn(0.f);
+        if ((i & 15u) == 0) sums[i >> 4] = 0.f;
+    }
+}
+
 // Prefill all-reduce: push a [count] fp32 partial to every rank (phase ph), then
 // x[i] += sum + bias[i % hidden] once every rank's push has arrived.
 int launch_tp_push(const TpComm &t, int ph, const float *src, size_t count, int *grid_out, cudaStream_t s);

@@ -80,7 +80,8 @@ class CuqOptions(ctypes.Structure):
 class CuqStats(ctypes.Structure):
     _fields_ = [("tokens", U64), ("prefill_tokens", U64), ("decode_ms", ctypes.c_double),
                 ("prefill_ms", ctypes.c_double), ("weight_bytes", U64), ("kv_bytes", U64),
-                ("graph_replays", U64), ("kernels_per_step", U64)]
+                ("graph_replays", U64), ("kernels_per_step", U64),
+                ("kernel_launches", U64)]
 
 
 class CuqError(RuntimeError):

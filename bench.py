@@ -1,25 +1,33 @@
 #!/usr/bin/env python3
-"""Benchmark: batch-1 greedy decode of the SmolLM2-135M-shaped Q8_0 model
-(30 layers, hidden 576, vocab 49152, 16-token prompt, 128
-greedy tokens) on the device-resident CUDA engine, one JSON line on rank 0.
+"""Benchmark of the quantized-weight decode/prefill path, one JSON line on rank 0.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config c2|c3|c4|c5] [--profile gemv]
 
-A step is one generation: prefill the 16-token prompt, then 128 decode steps.
-`value` is decode tokens/s over the timed steps (device time from CUDA events
-on the engine's stream; the GPU holds all weights, so no host copies).  `e2e`
-is the same workload through the C ABI's cuq_generate with host prompt ids in
-and host tokens out, timed by the host clock.  `roofline` measures the
-dominant kernel (the Q8_0 quant-GEMV, here the 49152 x 576 lm_head, the
-largest single launch) on its own with CUDA events, rotating weight copies
-larger than L2.  The weights (142.9 MB) exceed the 126 MB L2, and L2 is also
-flushed between timed steps.
+Workloads are BASELINE.json's configs (random-init synthetic models of the
+named architectures, seeded random prompt ids):
+  c2  SmolLM2-135M-arch, Q8_0, 16-token prompt + 128 greedy tokens  (default at N=1)
+  c3  Qwen2.5-0.5B-arch, Q8_0, 203 + 256
+  c4  Qwen2.5-1.5B-arch, Q4_K_M mix, 2048 + 256
+  c5  Llama-3-8B-arch, Q4_K_M mix, 4096 + 512  (default at N>1: tensor parallel over the N ranks)
 
-N > 1 (torchrun): the path does not shard at this config, so each rank runs an
-independent replica (weak scaling); value = all ranks' tokens / max rank time.
-`--impl reference`: the reference CPU path (the C oracle restating
-src/cpu.zig + main.zig refForward; the Zig reference cannot be built here) on
-all host cores, rank 0 only.
+A step is one generation: prefill the prompt, then the decode tokens.  `value`
+is decode tokens/s over the timed steps (device time from CUDA events on the
+engine's stream, max over ranks); `prefill` reports the prompt pass the same
+way.  `e2e` is the same workload through the public API (cuq_generate: host
+prompt ids in, host tokens out) timed by the host clock, prefill included.
+`roofline` measures the config's largest GEMV (the lm_head, this rank's shard
+under tensor parallelism) alone: CUDA events around back-to-back launches over
+rotating weight copies larger than L2.  L2 (126 MB) is flushed between timed
+steps.
+
+N > 1 (torchrun): c5 runs tensor-parallel (one sequence, strong scaling: value
+is that sequence's tokens/s); c2-c4 do not shard and run one replica per rank
+(weak scaling: value = all ranks' tokens / max rank time).
+`--impl reference`: the reference CPU path (the C oracle restating src/cpu.zig
++ main.zig refForward; the Zig reference cannot be built here) on all host
+cores, rank 0 only, on a bounded sample of the same workload.
+`--profile gemv`: 6 launches of the roofline GEMV only (for an ncu capture).
 """
 import argparse
 import ctypes
@@ -35,8 +43,27 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
-CONFIG = "smollm2-135m"
-N_PROMPT, N_DECODE = 16, 128
+CONFIGS = {
+    "c2": dict(model="smollm2-135m", prompt=16, decode=128, payload="quantized", head="token_embd.weight",
+               ref_sample=(4, 4), cpu_sample=(16, 48), cpu_threads=1,
+               desc="c2: SmolLM2-135M-arch Q8_0 (30 layers, hidden 576, vocab 49152), batch-1 greedy decode of 128 "
+                    "tokens after a 16-token prompt"),
+    "c3": dict(model="qwen2.5-0.5b", prompt=203, decode=256, payload="tiled", head="token_embd.weight",
+               ref_sample=(2, 2), cpu_sample=(2, 6), cpu_threads=1,
+               desc="c3: Qwen2.5-0.5B-arch Q8_0 (24 layers, hidden 896, vocab 151936), 203-token prompt + 256 "
+                    "greedy tokens"),
+    "c4": dict(model="qwen2.5-1.5b", prompt=2048, decode=256, payload="tiled", head="token_embd.weight",
+               ref_sample=(1, 2), cpu_sample=(1, 4), cpu_threads=0,
+               desc="c4: Qwen2.5-1.5B-arch Q4_K_M mix (28 layers, hidden 1536, vocab 151936), 2048-token prompt + "
+                    "256 greedy tokens"),
+    "c5": dict(model="llama3-8b", prompt=4096, decode=512, payload="tiled", head="output.weight",
+               ref_sample=(1, 1), cpu_sample=(1, 2), cpu_threads=0,
+               desc="c5: Llama-3-8B-arch Q4_K_M mix (32 layers, hidden 4096, vocab 128256 untied), 4096-token "
+                    "prompt + 512 greedy tokens"),
+}
+DATA = {"quantized": "synthetic: seeded N(0,0.02) weights quantized per tensor, seeded random prompt ids",
+        "tiled": "synthetic: every block is one of 256 real quantized blocks of seeded N(0,0.02) weights per tensor "
+                 "(valid blocks, same statistics; throughput does not depend on values), seeded random prompt ids"}
 
 
 def parse():
@@ -45,6 +72,7 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default=None, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile", choices=["gemv"], default=None,
                     help="run only the roofline kernel (a few launches) for an ncu capture, print nothing")
@@ -124,16 +152,17 @@ def barrier(world):
         dist.barrier()
 
 
-def prompt_ids(vocab, seed=0):
-    return np.random.default_rng(seed).integers(0, vocab, size=N_PROMPT).astype(np.uint32)
+def prompt_ids(vocab, n, seed=0):
+    return np.random.default_rng(seed).integers(0, vocab, size=n).astype(np.uint32)
 
 
 def cpu_baseline(model, threads, n_prompt, n_decode):
-    """The oracle (CPU restatement of the reference path) on a bounded sample."""
+    """The oracle (CPU restatement of the reference path) on a bounded sample:
+    decode tokens/s after an n_prompt-token prompt."""
     from oracle import oracle as orc
     ref = orc.Model(model.cfg, threads=threads, max_seq=n_prompt + n_decode + 1)
     ref.load(model)
-    ids = prompt_ids(model.cfg.vocab)[:n_prompt]
+    ids = prompt_ids(model.cfg.vocab, n_prompt)
     for p, t in enumerate(ids):
         lg = ref.forward(int(t), p)
     tok = orc.argmax(lg)
@@ -145,13 +174,19 @@ def cpu_baseline(model, threads, n_prompt, n_decode):
     return n_decode / dt
 
 
+def pick_config(args, world):
+    return args.config or ("c2" if world == 1 else "c5")
+
+
 def run_reference(args, world, rank):
     if rank != 0:
         return
     from anedvd_b200 import synth
-    model = synth.model(CONFIG)
+    name = pick_config(args, world)
+    C = CONFIGS[name]
+    model = synth.model(C["model"], payload=C["payload"], cache=False)
     threads = os.cpu_count() or 1
-    n_prompt, n_decode = 4, 4   # a bounded sample of the workload per step
+    n_prompt, n_decode = C["ref_sample"]
     vals = []
     for i in range(args.warmup + args.steps):
         v = cpu_baseline(model, threads, n_prompt, n_decode)
@@ -160,107 +195,127 @@ def run_reference(args, world, rank):
     value = float(np.mean(vals))
     print(json.dumps({
         "impl": "reference", "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded random-init weights, random prompt ids)",
-        "config": {"workload": "c2: SmolLM2-135M-arch Q8_0, batch-1 greedy decode", "model": CONFIG,
-                   "prompt": N_PROMPT, "decode": N_DECODE},
+        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "scaling": "strong" if (world > 1 and name == "c5") else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": DATA[C["payload"]],
+        "config": {"workload": C["desc"], "model": C["model"], "prompt": C["prompt"], "decode": C["decode"]},
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": "per step: %d-token prompt then %d greedy decode tokens, oracle refForward "
+                         "sample": "per step: %d-token prompt then %d greedy decode tokens timed, oracle refForward "
                                    "(rows split across %d threads, reference per-row order)"
                                    % (n_prompt, n_decode, threads)},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
-def gemv_roofline(model, stream_ptr, pk, reps=64):
-    """Time the lm_head quant-GEMV alone: CUDA events around `reps` back-to-back
-    launches on the engine's stream over 8 rotating weight copies (240 MB > L2),
-    so every launch streams from HBM; the mean launch duration includes the
-    short gap between consecutive launches."""
+def head_shard(model, C, rank, world):
+    """The config's lm_head weight (this rank's vocab rows under tensor parallelism)."""
+    t = model.tensor(C["head"])
+    raw = np.frombuffer(t.data, dtype=np.uint8)
+    rows = t.rows // world
+    row_bytes = raw.size // t.rows
+    return t.ggml_type, np.ascontiguousarray(raw[rank * rows * row_bytes:(rank + 1) * rows * row_bytes]), rows, t.cols
+
+
+def gemv_roofline(ttype, raw, rows, cols, stream_ptr, pk, label, reps=64):
+    """Time one quant-GEMV alone: CUDA events around `reps` back-to-back launches
+    on the engine's stream over rotating weight copies (> 2 x L2 in total), so
+    every launch streams from HBM; the mean launch duration includes the short
+    gap between consecutive launches."""
     import torch
+    from anedvd_b200 import gguf
     from anedvd_b200 import runtime as rt
     L = rt.load()
-    t = model.tensor("token_embd.weight")
-    raw = np.frombuffer(t.data, dtype=np.uint8)
-    copies = [L.cuq_weight_create(t.ggml_type, raw.ctypes.data_as(ctypes.c_void_p), raw.size, t.rows, t.cols)
-              for _ in range(8)]
+    ncopy = int(min(16, max(2, np.ceil(260e6 / raw.size))))
+    copies = [L.cuq_weight_create(ttype, raw.ctypes.data_as(ctypes.c_void_p), raw.size, rows, cols)
+              for _ in range(ncopy)]
     assert all(copies), rt.last_error()
-    x = torch.randn(t.cols, device="cuda", dtype=torch.float32)
-    xq = torch.empty(L.cuq_xq_halves(t.cols), dtype=torch.int16, device="cuda")
-    y = torch.empty(t.rows, device="cuda", dtype=torch.float32)
+    x = torch.randn(cols, device="cuda", dtype=torch.float32)
+    xq = torch.empty(L.cuq_xq_halves(cols), dtype=torch.int16, device="cuda")
+    y = torch.empty(rows, device="cuda", dtype=torch.float32)
     stream = torch.cuda.ExternalStream(stream_ptr)
-    rt.check(L.cuq_prepare_x(ctypes.c_void_p(x.data_ptr()), t.cols, ctypes.c_void_p(xq.data_ptr()),
+    args = lambda i: (copies[i % ncopy], ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(y.data_ptr()),
+                      ctypes.c_void_p(stream_ptr))
+    rt.check(L.cuq_prepare_x(ctypes.c_void_p(x.data_ptr()), cols, ctypes.c_void_p(xq.data_ptr()),
                              ctypes.c_void_p(stream_ptr)))
     for i in range(8 if reps > 0 else 6):  # warm-up (profile mode: these are the only launches)
-        rt.check(L.cuq_gemv_prepared(copies[i % 8], ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(y.data_ptr()),
-                                     ctypes.c_void_p(stream_ptr)))
+        rt.check(L.cuq_gemv_prepared(*args(i)))
     if reps <= 0:
         torch.cuda.synchronize()
         for c in copies:
             L.cuq_weight_free(c)
         return None
-    # back-to-back launches on the engine's stream; a spin kernel first lets the
-    # host queue them all, so the events time the GPU, not the launch calls
+    # a spin kernel first lets the host queue every launch, so the events time the GPU
     with torch.cuda.stream(stream):
         torch.cuda._sleep(4_000_000)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for i in range(reps):
-        L.cuq_gemv_prepared(copies[i % 8], ctypes.c_void_p(xq.data_ptr()), ctypes.c_void_p(y.data_ptr()),
-                            ctypes.c_void_p(stream_ptr))
+        L.cuq_gemv_prepared(*args(i))
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / reps
     for c in copies:
         L.cuq_weight_free(c)
-    alg = t.rows * t.cols * 34 // 32 + 4 * t.cols + 4 * t.rows   # N*K*bpw + 4K + 4N (Q8_0 bpw 34/32)
+    alg = gguf.tensor_nbytes(ttype, rows * cols) + 4 * cols + 4 * rows   # N*K*bpw + 4K + 4N
     achieved = alg / (ms * 1e-3) / 1e9
     traffic = None
     try:
-        prof = json.load(open(os.path.join(ROOT, "profiles", "gemv_q8_0_lm_head_traffic.json")))
-        traffic = prof.get("dram_bytes_per_launch")
+        prof = json.load(open(os.path.join(ROOT, "profiles", "roofline_traffic.json")))
+        traffic = prof.get(label, {}).get("dram_bytes_per_launch")
     except (OSError, ValueError):
         pass
-    return {"kernel": "gemv_kernel<TQ8_0> (lm_head 49152x576 Q8_0)", "bound": "hbm", "achieved": achieved,
-            "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"], "traffic": traffic,
-            "algorithmic_bytes": alg, "launch_us": ms * 1e3}
+    tname = {8: "TQ8_0", 12: "TQ4K", 14: "TQ6K"}.get(ttype, str(ttype))
+    return {"kernel": "gemv_kernel<%s> (%s %dx%d)" % (tname, label, rows, cols), "bound": "hbm",
+            "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+            "traffic": traffic, "algorithmic_bytes": alg, "launch_us": ms * 1e3}
 
 
 def run_ours(args, world, rank, local):
     import torch
     from anedvd_b200 import engine as E
-    from anedvd_b200 import runtime as rt
     from anedvd_b200 import synth
 
+    name = pick_config(args, world)
+    C = CONFIGS[name]
+    tp = world > 1 and name == "c5"
     torch.cuda.set_device(local)
     pk, pk_kind = peaks()
-    model = synth.model(CONFIG)
-    max_seq = N_PROMPT + N_DECODE + 8
-    eng = E.Engine.from_synth(model, max_seq=max_seq, device=local)
+    model = synth.model(C["model"], payload=C["payload"], cache=False)
+    n_prompt, n_decode = C["prompt"], C["decode"]
+    max_seq = n_prompt + n_decode + 8
+
+    def exchange(h):
+        import torch.distributed as dist
+        out = [None] * world
+        dist.all_gather_object(out, h)
+        return out
+
+    eng = E.Engine.from_synth(model, max_seq=max_seq, device=local, max_chunk=512,
+                              tp_rank=rank if tp else 0, tp_size=world if tp else 1, exchange=exchange)
     stream_ptr = eng.stream
     stream = torch.cuda.ExternalStream(stream_ptr)
-    ids = prompt_ids(model.cfg.vocab)
+    ids = prompt_ids(model.cfg.vocab, n_prompt)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device="cuda")
 
-    def one_step():
-        _, first = eng.prefill(ids, 0, want_logits=False)
-        return eng.decode_greedy(first, N_PROMPT, N_DECODE)
-
     for _ in range(args.warmup):
-        one_step()
+        barrier(world)
+        _, first = eng.prefill(ids, 0, want_logits=False)
+        eng.decode_greedy(first, n_prompt, n_decode)
     torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     clocks = Clocks(local)
+    launches0 = eng.stats.kernel_launches
     dec_ms, pre_ms = 0.0, 0.0
     for _ in range(args.steps):
         flush.zero_()
         torch.cuda.synchronize()
+        barrier(world)
         e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
         e0.record(stream)
         _, first = eng.prefill(ids, 0, want_logits=False)
         e1.record(stream)
-        eng.decode_greedy(first, N_PROMPT, N_DECODE)
+        eng.decode_greedy(first, n_prompt, n_decode)
         e2.record(stream)
         torch.cuda.synchronize()
         pre_ms += e0.elapsed_time(e1)
@@ -268,68 +323,81 @@ def run_ours(args, world, rank, local):
     torch.cuda.synchronize()
     barrier(world)
     clk = clocks.stop()
+    launches = eng.stats.kernel_launches - launches0
     dec_ms_max = max_over_ranks(dec_ms, world)
     pre_ms_max = max_over_ranks(pre_ms, world)
-    tokens = N_DECODE * args.steps * world
-    value = tokens / (dec_ms_max * 1e-3)
-    prefill_tps = N_PROMPT * args.steps * world / (pre_ms_max * 1e-3)
+    seqs = 1 if tp else world   # tensor parallel: the ranks share one sequence
+    value = n_decode * args.steps * seqs / (dec_ms_max * 1e-3)
+    prefill_tps = n_prompt * args.steps * seqs / (pre_ms_max * 1e-3)
     kps = eng.stats.kernels_per_step
 
-    # end to end through the C ABI: host prompt ids in, host tokens out (cuq_generate)
+    # end to end through the public API: host prompt ids in, host tokens out (cuq_generate)
     sess = E.Session(eng, max_seq)
-    sess.generate(ids, N_DECODE)
+    barrier(world)
+    sess.generate(ids, n_decode)
     barrier(world)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        sess.generate(ids, N_DECODE)
+        sess.generate(ids, n_decode)
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
-    e2e = N_DECODE * args.steps * world / e2e_s
+    e2e = n_decode * args.steps * seqs / e2e_s
 
-    roof = gemv_roofline(model, stream_ptr, pk) if rank == 0 else None
+    ttype, raw, rows, cols = head_shard(model, C, rank if tp else 0, world if tp else 1)
+    roof = gemv_roofline(ttype, raw, rows, cols, stream_ptr, pk, "%s lm_head" % name) if rank == 0 else None
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        n_p, n_d = 16, 48
-        cpu = {"value": cpu_baseline(model, 1, n_p, n_d), "unit": "tok/s", "cores": 1, "kind": "port",
-               "sample": "%d-token prompt, then %d greedy decode tokens timed; single thread (the reference "
-                         "engine is single-threaded), oracle refForward in the reference's scalar order" % (n_p, n_d)}
+        n_p, n_d = C["cpu_sample"]
+        threads = C["cpu_threads"] or (os.cpu_count() or 1)
+        cpu = {"value": cpu_baseline(model, threads, n_p, n_d), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": "%d-token prompt, then %d greedy decode tokens timed; %s, oracle refForward in the "
+                         "reference's per-row order" % (n_p, n_d, "single thread (the reference engine is "
+                                                                   "single-threaded)" if threads == 1 else
+                                                        "rows split across %d threads" % threads)}
+    wbytes = model.weight_bytes_per_token()
     if rank == 0:
+        parallelism = ("tensor parallel x%d" % world) if tp else ("replicas x%d" % world if world > 1 else
+                                                                  "single GPU")
         line = {
             "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": (dec_ms_max + pre_ms_max) / args.steps,
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "q8_0 weights, fp16 tensor-core "
-            "MMA with fp32 accumulate, fp32 activations",
-            "data": "synthetic (seeded random-init weights, random prompt ids)",
-            "config": {"workload": "c2: SmolLM2-135M-arch Q8_0 (30 layers, hidden 576, vocab 49152), batch-1 "
-                                   "greedy decode of 128 tokens after a 16-token prompt",
-                       "model": CONFIG, "prompt": N_PROMPT, "decode": N_DECODE,
-                       "parallelism": "replicas" if world > 1 else "single GPU",
-                       "l2": "flushed between steps; weights 142.9 MB > 126 MB L2"},
-            "prefill_tok_per_s": prefill_tps,
-            "weight_bytes_per_token": model.weight_bytes_per_token(),
-            "weight_stream_gbs": model.weight_bytes_per_token() * value / world / 1e9,
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * N_PROMPT + 4,
-                    "d2h_bytes_per_step": 4 * N_DECODE},
+            "higher_is_better": True, "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "dtype": "%s weights dequantized exactly to fp16, fp16 tensor-core MMA with fp32 accumulate, fp32 "
+                     "activations (split hi+lo fp16)" % ("q8_0" if name in ("c2", "c3") else "q4_k/q6_k"),
+            "data": DATA[C["payload"]],
+            "config": {"workload": C["desc"], "model": C["model"], "prompt": n_prompt, "decode": n_decode,
+                       "parallelism": parallelism,
+                       "l2": "flushed between steps (256 MB write); weights %.1f MB" % (wbytes / 1e6)},
+            "prefill": {"tok_per_s": prefill_tps, "ms": pre_ms_max / args.steps},
+            "weight_bytes_per_token": wbytes,
+            "weight_stream_gbs": wbytes * value / seqs / 1e9,
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt + 4 * 1,
+                    "d2h_bytes_per_step": 4 * n_decode},
             "roofline": roof, "peak_kind": pk_kind, "cpu_baseline": cpu,
-            "gpu_launches": int(kps * (N_PROMPT + N_DECODE) * args.steps),
+            "gpu_launches": int(launches),
             "kernels_per_token": int(kps),
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)
+    barrier(world)
     eng.close()
 
 
 def profile_case(args):
-    """A handful of launches of the roofline kernel alone (3 warm-up + 3), for
-    `ncu -k regex:gemv_kernel -s 3 -c 3`; nothing printed."""
+    """A handful of launches of the roofline kernel alone (6 launches), for
+    `ncu -k regex:gemv_kernel -s 3 -c 1`; nothing printed."""
     import torch
     from anedvd_b200 import runtime as rt
     from anedvd_b200 import synth
     rt.load()
     rt.init(0)
     torch.cuda.set_device(0)
+    name = args.config or "c2"
+    C = CONFIGS[name]
+    model = synth.model(C["model"], payload=C["payload"], cache=False)
     if args.profile == "gemv":
         s = torch.cuda.Stream()
-        gemv_roofline(synth.model(CONFIG), s.cuda_stream, peaks()[0], reps=0)  # 6 launches
+        ttype, raw, rows, cols = head_shard(model, C, 0, 1)
+        gemv_roofline(ttype, raw, rows, cols, s.cuda_stream, peaks()[0], name, reps=0)
     torch.cuda.synchronize()
 
 

@@ -198,6 +198,7 @@ typedef struct {
     uint64_t kv_bytes;         /* KV-cache bytes */
     uint64_t graph_replays;
     uint64_t kernels_per_step; /* kernel launches in one decode step */
+    uint64_t kernel_launches;  /* all kernels this model has launched (graph nodes counted) */
 } cuq_stats;
 
 /* Engine.init (engine.zig:320-521) without weights: allocates the KV cache and
