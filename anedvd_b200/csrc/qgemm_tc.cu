@@ -14,6 +14,8 @@
 // += into the residual, or SiLU*mul for a gate|up pair) to global memory.
 // Every mbarrier wait is bounded: on timeout the CTA records an error, stops
 // issuing, releases its tensor memory and returns.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "qgemm.cuh"
 
@@ -25,7 +27,6 @@ constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;        // 16 KB
 constexpr int B_BYTES = 2 * BN * BK * 2;    // 32 KB (hi + lo)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /* align */ + 256 /* barriers */;
 constexpr uint32_t TMEM_COLS = 256;
 constexpr uint32_t WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (seconds)
 
@@ -106,144 +107,324 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
     for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// ----------------------------------------------------- weight dequant ----
-// 64 consecutive weights of one row, as the reference's fp16 values
-// (RN16 of the fp32 dequant, gguf.zig:751-1071).  Arithmetic rounds where the
-// reference rounds (explicit _rn intrinsics: no FMA contraction).
+// ----------------------------------------------------- weight planes ----
 
 struct WPlanes {
     const uint8_t *q, *q2, *s, *s2;
     uint32_t rows, cols;
 };
 
-__device__ __forceinline__ float f16bits(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+// Raw bytes of one 64-column K step, staged per weight row in shared memory by
+// cp.async (prefetched RAWD-1 steps ahead), then dequantised from there.
+//   RAW_ROW: quant bytes per row (padded to a power of two for the swizzle);
+//   SIDE:    per-step side data (scales, 5th bits) for the tile's 128 rows.
+template <int T>
+struct RawGeom;
+template <> struct RawGeom<CUQ_Q8_0> { static constexpr int RAW_ROW = 64, SIDE = 2 * 256; };
+template <> struct RawGeom<CUQ_Q4_0> { static constexpr int RAW_ROW = 32, SIDE = 2 * 256; };
+template <> struct RawGeom<CUQ_Q4_1> { static constexpr int RAW_ROW = 32, SIDE = 2 * 512; };
+template <> struct RawGeom<CUQ_Q5_0> { static constexpr int RAW_ROW = 32, SIDE = 2 * 256 + 2 * 512; };
+template <> struct RawGeom<CUQ_Q5_1> { static constexpr int RAW_ROW = 32, SIDE = 2 * 512 + 2 * 512; };
+template <> struct RawGeom<CUQ_Q4_K> { static constexpr int RAW_ROW = 32, SIDE = 128 * 16; };
+template <> struct RawGeom<CUQ_Q6_K> { static constexpr int RAW_ROW = 96, SIDE = 128 * 16 + 256; };
+template <> struct RawGeom<CUQ_F16> { static constexpr int RAW_ROW = 128, SIDE = 0; };
+template <> struct RawGeom<CUQ_BF16> { static constexpr int RAW_ROW = 128, SIDE = 0; };
 
-__device__ __forceinline__ void scale_min_k4(int j, const uint8_t *q, int &d, int &m) {
-    if (j < 4) {
-        d = q[j] & 63;
-        m = q[j + 4] & 63;
-    } else {
-        d = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
-        m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+template <int T>
+struct Geo {
+    static constexpr int RAW_ROW = RawGeom<T>::RAW_ROW, SIDE = RawGeom<T>::SIDE;
+    static constexpr int CH = RAW_ROW / 16;                        // 16-byte chunks per row
+    static constexpr int SLOT = BM * RAW_ROW + SIDE;               // bytes per raw slot
+    static constexpr int RAWD = SLOT > 12288 ? 2 : 3;              // raw ring depth (fits 227 KB)
+    static constexpr int SMEM = STAGES * STAGE_BYTES + RAWD * SLOT + 1024 + 256;
+};
+
+// physical 16-byte chunk of logical chunk c in row r (conflict-free 16-byte reads
+// by consecutive rows: 8 consecutive rows cover the 8 bank groups)
+template <int CH>
+__device__ __forceinline__ int raw_chunk(int r, int c) {
+    if (CH & (CH - 1)) return c;  // not a power of two (Q6_K, 6 chunks): plain rows, 2-way conflicts
+    return CH >= 8 ? (c ^ (r & 7)) : c ^ ((r / (8 / CH)) & (CH - 1));
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Issue the copies of K step kb into `slot` (thread t of the 128 producers).
+template <int T>
+__device__ __forceinline__ void raw_issue(const WPlanes &w, const WPlanes &w2, bool dual, uint32_t row0, uint32_t kb,
+                                          uint8_t *slot, int t) {
+    using G = Geo<T>;
+    const uint32_t sb = kb / 4;
+    // quant bytes of row t (gate rows then up rows in a dual tile)
+    const WPlanes &wp = (dual && t >= 64) ? w2 : w;
+    const uint32_t r = dual ? row0 + (t & 63) : row0 + t;
+    const uint32_t rr = r < wp.rows ? r : wp.rows - 1;  // rows past the end: any valid row (results unused)
+    const uint8_t *src;
+    if (T == CUQ_Q8_0)
+        src = wp.q + (size_t)rr * wp.cols + kb * 64;
+    else if (T == CUQ_F16 || T == CUQ_BF16)
+        src = wp.q + ((size_t)rr * wp.cols + kb * 64) * 2;
+    else if (T == CUQ_Q6_K)
+        src = wp.q + (size_t)rr * (wp.cols / 2) + (size_t)sb * 128 + 64 * ((kb % 4) / 2);
+    else
+        src = wp.q + (size_t)rr * (wp.cols / 2) + (size_t)kb * 32;
+    const uint32_t base = smem_u32(slot) + t * G::RAW_ROW;
+    const int nq = T == CUQ_Q6_K ? 4 : G::CH;  // Q6_K: ql 64 B here, qh 32 B below
+#pragma unroll
+    for (int c = 0; c < nq; c++) cp_async16(base + raw_chunk<G::CH>(t, c) * 16, src + 16 * c);
+    if (T == CUQ_Q6_K) {
+        const uint8_t *qh = wp.q2 + (size_t)rr * (wp.cols / 4) + (size_t)sb * 64 + 32 * ((kb % 4) / 2);
+        cp_async16(base + raw_chunk<G::CH>(t, 4) * 16, qh);
+        cp_async16(base + raw_chunk<G::CH>(t, 5) * 16, qh + 16);
+    }
+    // side data: block-major planes, so the tile's rows are contiguous; chunks
+    // of rows past the matrix end are skipped (their results are never stored)
+    const uint32_t sside = smem_u32(slot + BM * G::RAW_ROW);
+    if (T == CUQ_Q4_K || T == CUQ_Q6_K) {
+        // 16 bytes of scales per row of superblock sb (Q4_K: d, dmin, 12 scale bytes)
+        const uint32_t ra = row0 + (dual ? (t & 63) : t);
+        if (ra < wp.rows) cp_async16(sside + 16 * t, wp.s + ((size_t)sb * wp.rows + ra) * 16);
+        if (T == CUQ_Q6_K && t < 16) {
+            // d: one fp16 per row = 8 rows per chunk (dual: 8 chunks of gate rows, 8 of up rows)
+            const bool upc = dual && t >= 8;
+            const WPlanes &a = upc ? w2 : w;
+            const uint32_t first = row0 + 8 * (dual ? (t & 7) : t);
+            if (first < a.rows)
+                cp_async16(sside + 2048 + 16 * t, a.s2 + ((size_t)sb * a.rows + first) * 2);
+        }
+    } else if (T != CUQ_F16 && T != CUQ_BF16) {
+        // two 32-blocks per step; per block: d (2 B) or d|m (4 B) per row; Q5: qh 4 B per row
+        constexpr int SE = (T == CUQ_Q4_1 || T == CUQ_Q5_1) ? 4 : 2;
+        constexpr int SB = 128 * SE;     // side bytes per block
+        constexpr int PER = SB / 16;     // chunks per block
+        constexpr int RPC = 16 / SE;     // rows per chunk
+        for (int c = t; c < 2 * PER; c += 128) {
+            const int blk = c / PER, cc = c % PER;
+            const bool upc = dual && cc >= PER / 2;
+            const WPlanes &a = upc ? w2 : w;
+            const uint32_t first = row0 + RPC * (dual ? (cc % (PER / 2)) : cc);
+            if (first < a.rows)
+                cp_async16(sside + blk * SB + 16 * cc, a.s + ((size_t)(kb * 2 + blk) * a.rows + first) * SE);
+        }
+        if (T == CUQ_Q5_0 || T == CUQ_Q5_1) {
+            for (int c = t; c < 2 * 32; c += 128) {  // qh: 4 rows per chunk, 32 chunks per block
+                const int blk = c / 32, cc = c % 32;
+                const bool upc = dual && cc >= 16;
+                const WPlanes &a = upc ? w2 : w;
+                const uint32_t first = row0 + 4 * (dual ? (cc % 16) : cc);
+                if (first < a.rows)
+                    cp_async16(sside + 2 * SB + blk * 512 + 16 * cc,
+                               a.q2 + ((size_t)(kb * 2 + blk) * a.rows + first) * 4);
+            }
+        }
     }
 }
 
+// -------------------------------------------------------- packed helpers --
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+typedef unsigned long long u64;
+__device__ __forceinline__ u64 f2pack(float a, float b) {
+    return (u64)__float_as_uint(a) | ((u64)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ u64 ffma2(u64 a, u64 b, u64 c) {
+    u64 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ u64 fmul2(u64 a, u64 b) {
+    u64 d;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+__device__ __forceinline__ u64 fsub2(u64 a, u64 b) {
+    u64 d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// RN16 of both fp32 lanes -> half2 (lane 0 low)
+__device__ __forceinline__ uint32_t cvt_h2(u64 v) {
+    return h2u(__floats2half2_rn(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32))));
+}
+// bytes b0, b1 of w (small unsigned ints) as exact floats 2^23 + b (magic), packed
+__device__ __forceinline__ u64 bytes01_magic(uint32_t w, uint32_t sel0, uint32_t sel1) {
+    return (u64)__byte_perm(w, 0x4B000000u, sel0) | ((u64)__byte_perm(w, 0x4B000000u, sel1) << 32);
+}
+#define MAGIC23 8388608.0f
+
+// ------------------------------------------------- dequant from shared ----
+// Row t's 64 weights of step kb, as the reference's fp16 values (RN16 of the
+// fp32 dequant, gguf.zig:751-1071 / load_gguf.zig:371), in natural k order:
+// out[c] = weights 8c .. 8c+7.  Arithmetic rounds where the reference rounds.
 template <int T>
-__device__ void dequant64(const WPlanes &w, uint32_t row, uint32_t kb, __half (&o)[64]) {
-    const uint32_t k0 = kb * 64;
-    if (T == CUQ_Q8_0) {  // gguf.zig:827-840: d * q
-        const int8_t *qs = reinterpret_cast<const int8_t *>(w.q) + (size_t)row * w.cols + k0;
-        const __half *dp = reinterpret_cast<const __half *>(w.s);
-        uint4 v[4];
+__device__ __forceinline__ void dequant_smem(const uint8_t *slot, int t, uint32_t kb, bool dual, uint4 (&out)[8]) {
+    using G = Geo<T>;
+    const uint8_t *row = slot + t * G::RAW_ROW;
+    const uint8_t *side = slot + BM * G::RAW_ROW;
+    auto chunk = [&](int c) { return *reinterpret_cast<const uint4 *>(row + raw_chunk<G::CH>(t, c) * 16); };
+    const int srow = t;  // side index of this row (dual tiles stack gate rows then up rows)
+    if (T == CUQ_Q8_0) {  // gguf.zig:827-840: RN16(d * q), the product is exact
+        const __half2 off = __float2half2_rn(1152.f);
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = reinterpret_cast<const uint4 *>(qs)[i];
-        const int8_t *b = reinterpret_cast<const int8_t *>(v);
+        for (int c4 = 0; c4 < 4; c4++) {
+            const uint4 v = chunk(c4);
+            const __half2 d = __half2half2(reinterpret_cast<const __half *>(side)[(c4 / 2) * 128 + srow]);
+            const uint32_t wv[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
+            uint32_t o[8];
 #pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-            float d = __half2float(dp[(size_t)(k0 / 32 + blk) * w.rows + row]);
-#pragma unroll
-            for (int j = 0; j < 32; j++) o[blk * 32 + j] = __float2half_rn(__fmul_rn(d, (float)b[blk * 32 + j]));
-        }
-    } else if (T == CUQ_Q4_0 || T == CUQ_Q4_1 || T == CUQ_Q5_0 || T == CUQ_Q5_1) {
-        const uint8_t *qs = w.q + (size_t)row * (w.cols / 2) + k0 / 2;
-        uint4 v[2];
-        v[0] = reinterpret_cast<const uint4 *>(qs)[0];
-        v[1] = reinterpret_cast<const uint4 *>(qs)[1];
-        const uint8_t *b = reinterpret_cast<const uint8_t *>(v);
-#pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-            const size_t bi = (size_t)(k0 / 32 + blk) * w.rows + row;
-            float d, m = 0.f;
-            if (T == CUQ_Q4_0 || T == CUQ_Q5_0) {
-                d = __half2float(reinterpret_cast<const __half *>(w.s)[bi]);
-            } else {
-                __half2 dm = reinterpret_cast<const __half2 *>(w.s)[bi];
-                d = __low2float(dm);
-                m = __high2float(dm);
+            for (int i = 0; i < 4; i++) {
+                o[2 * i] = h2u(__hmul2(__hsub2(u2h(__byte_perm(wv[i], 0x64646464u, 0x4140u)), off), d));
+                o[2 * i + 1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(wv[i], 0x64646464u, 0x4342u)), off), d));
             }
-            uint32_t qh = (T == CUQ_Q5_0 || T == CUQ_Q5_1) ? reinterpret_cast<const uint32_t *>(w.q2)[bi] : 0u;
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                int byte = b[blk * 16 + (j & 15)];
-                int nib = j < 16 ? (byte & 0xF) : (byte >> 4);
-                float val;
-                if (T == CUQ_Q4_0) {
-                    val = __fmul_rn((float)(nib - 8), d);  // gguf.zig:763-776
-                } else if (T == CUQ_Q4_1) {
-                    val = __fadd_rn(__fmul_rn((float)nib, d), m);  // gguf.zig:778-792
-                } else {
-                    int hb = j < 16 ? (int)(((qh >> j) << 4) & 0x10u) : (int)((qh >> (j - 16 + 12)) & 0x10u);
-                    float x = (float)((nib | hb) - (T == CUQ_Q5_0 ? 16 : 0));
-                    val = __fadd_rn(__fmul_rn(x, d), m);  // gguf.zig:795-825
-                }
-                o[blk * 32 + j] = __float2half_rn(val);
-            }
+            out[2 * c4] = make_uint4(o[0], o[1], o[2], o[3]);
+            out[2 * c4 + 1] = make_uint4(o[4], o[5], o[6], o[7]);
         }
-    } else if (T == CUQ_Q4_K) {  // gguf.zig:962-996: (d*sc)*q - dmin*m
-        const uint32_t sb = kb / 4, c = kb % 4;
-        const uint8_t *qs = w.q + (size_t)row * (w.cols / 2) + (size_t)sb * 128 + 32 * c;
-        uint4 v[2];
-        v[0] = reinterpret_cast<const uint4 *>(qs)[0];
-        v[1] = reinterpret_cast<const uint4 *>(qs)[1];
-        uint4 meta = *reinterpret_cast<const uint4 *>(w.s + ((size_t)sb * w.rows + row) * 16);
-        const uint8_t *mb = reinterpret_cast<const uint8_t *>(&meta);
-        const uint8_t *b = reinterpret_cast<const uint8_t *>(v);
-        float d = f16bits((uint16_t)(meta.x & 0xFFFF)), dmin = f16bits((uint16_t)(meta.x >> 16));
+    } else if (T == CUQ_Q4_K) {  // gguf.zig:962-996: fp32 (d*sc)*q - dmin*m, then RN16
+        const uint32_t c = kb % 4;
+        const uint4 meta = reinterpret_cast<const uint4 *>(side)[srow];
+        const float d = __half2float(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
+        const float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
+        u64 d1[2], nm1[2];
 #pragma unroll
         for (int part = 0; part < 2; part++) {
-            int sc, mm;
-            scale_min_k4(2 * c + part, mb + 4, sc, mm);
-            float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)mm);
+            const int j = 2 * c + part, sh = 8 * (j & 3);
+            const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
+            const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
+            const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
+            const float a = __fmul_rn(d, (float)sc), m = __fmul_rn(dmin, (float)mm);
+            d1[part] = f2pack(a, a);
+            // fold the magic: d1*(2^23+q) - (d1*2^23 + m1) is not exact, so subtract 2^23 first
+            nm1[part] = f2pack(-m, -m);
+        }
+        const u64 mg = f2pack(MAGIC23, MAGIC23);
+        const uint4 q0 = chunk(0), q1 = chunk(1);
+        const uint32_t wv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-            for (int l = 0; l < 32; l++) {
-                float q = (float)(part ? (b[l] >> 4) : (b[l] & 0xF));
-                o[part * 32 + l] = __float2half_rn(__fsub_rn(__fmul_rn(d1, q), m1));
+        for (int part = 0; part < 2; part++) {
+#pragma unroll
+            for (int i = 0; i < 8; i++) {  // 4 weights (one word) per i
+                const uint32_t nib = part ? ((wv[i] >> 4) & 0x0F0F0F0Fu) : (wv[i] & 0x0F0F0F0Fu);
+                const u64 a01 = fsub2(bytes01_magic(nib, 0x7440u, 0x7441u), mg);
+                const u64 a23 = fsub2(bytes01_magic(nib, 0x7442u, 0x7443u), mg);
+                const uint32_t h01 = cvt_h2(ffma2(d1[part], a01, nm1[part]));
+                const uint32_t h23 = cvt_h2(ffma2(d1[part], a23, nm1[part]));
+                uint32_t *o = reinterpret_cast<uint32_t *>(&out[part * 4 + i / 2]);
+                o[(i & 1) * 2] = h01;
+                o[(i & 1) * 2 + 1] = h23;
             }
         }
-    } else if (T == CUQ_Q6_K) {  // gguf.zig:1036-1059: (d*sc)*(q-32)
-        const uint32_t sb = kb / 4, qtr = kb % 4, h = qtr / 2, t0 = 2 * (qtr % 2);
-        const uint8_t *ql = w.q + (size_t)row * (w.cols / 2) + (size_t)sb * 128 + 64 * h;
-        const uint8_t *qh = w.q2 + (size_t)row * (w.cols / 4) + (size_t)sb * 64 + 32 * h;
-        uint4 scv = *reinterpret_cast<const uint4 *>(w.s + ((size_t)sb * w.rows + row) * 16);
-        const int8_t *sc = reinterpret_cast<const int8_t *>(&scv);
-        float d = __half2float(reinterpret_cast<const __half *>(w.s2)[(size_t)sb * w.rows + row]);
-        uint4 lv[4], hv[2];
-#pragma unroll
-        for (int i = 0; i < 4; i++) lv[i] = reinterpret_cast<const uint4 *>(ql)[i];
-        hv[0] = reinterpret_cast<const uint4 *>(qh)[0];
-        hv[1] = reinterpret_cast<const uint4 *>(qh)[1];
-        const uint8_t *L = reinterpret_cast<const uint8_t *>(lv), *H = reinterpret_cast<const uint8_t *>(hv);
+    } else if (T == CUQ_Q6_K) {  // gguf.zig:1036-1059: fp32 (d*sc) * (q-32), then RN16
+        const uint32_t qtr = kb % 4, h = qtr / 2, t0 = 2 * (qtr % 2);
+        const uint4 scv = reinterpret_cast<const uint4 *>(side)[srow];
+        const float d = __half2float(reinterpret_cast<const __half *>(side + 2048)[srow]);
+        const uint4 L0 = chunk(0), L1 = chunk(1), L2 = chunk(2), L3 = chunk(3), H0 = chunk(4), H1 = chunk(5);
+        const uint32_t Lw[16] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w,
+                                 L2.x, L2.y, L2.z, L2.w, L3.x, L3.y, L3.z, L3.w};
+        const uint32_t Hw[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
+        const u64 mg = f2pack(MAGIC23 + 32.f, MAGIC23 + 32.f);
 #pragma unroll
         for (int tt = 0; tt < 2; tt++) {
-            const int t = t0 + tt;
+            const uint32_t tq = t0 + tt;  // which 32 of the half: ql lo/hi and qh bit pair
 #pragma unroll
-            for (int l = 0; l < 32; l++) {
-                int lo = (t & 1) ? L[32 + l] : L[l];
-                int q = ((t >= 2) ? (lo >> 4) : (lo & 0xF)) | (((H[l] >> (2 * t)) & 3) << 4);
-                float s = __fmul_rn(d, (float)sc[8 * h + 2 * t + (l >> 4)]);
-                o[tt * 32 + l] = __float2half_rn(__fmul_rn(s, (float)(q - 32)));
+            for (int sub = 0; sub < 2; sub++) {  // l in [16 sub, 16 sub + 16): one int8 scale
+                const int si = 8 * h + 2 * tq + sub;
+                const uint32_t sw = si < 4 ? scv.x : si < 8 ? scv.y : si < 12 ? scv.z : scv.w;
+                const float scale = __fmul_rn(d, (float)(int)(int8_t)((sw >> (8 * (si & 3))) & 0xFFu));
+                const u64 s2 = f2pack(scale, scale);
+#pragma unroll
+                for (int i = 0; i < 4; i++) {  // 4 words of 4 weights
+                    const int l4 = sub * 4 + i;  // word index of l in 0..7
+                    const uint32_t L = (tq & 1) ? Lw[8 + l4] : Lw[l4];
+                    const uint32_t lo = (tq >= 2) ? ((L >> 4) & 0x0F0F0F0Fu) : (L & 0x0F0F0F0Fu);
+                    const uint32_t q = lo | (((Hw[l4] >> (2 * tq)) & 0x03030303u) << 4);
+                    const u64 a01 = fsub2(bytes01_magic(q, 0x7440u, 0x7441u), mg);
+                    const u64 a23 = fsub2(bytes01_magic(q, 0x7442u, 0x7443u), mg);
+                    uint32_t *o = reinterpret_cast<uint32_t *>(&out[tt * 4 + l4 / 2]);
+                    o[(l4 & 1) * 2] = cvt_h2(fmul2(s2, a01));
+                    o[(l4 & 1) * 2 + 1] = cvt_h2(fmul2(s2, a23));
+                }
             }
         }
     } else if (T == CUQ_F16) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(w.q + ((size_t)row * w.cols + k0) * 2);
 #pragma unroll
-        for (int i = 0; i < 8; i++) reinterpret_cast<uint4 *>(o)[i] = src[i];
+        for (int c = 0; c < 8; c++) out[c] = chunk(c);
     } else if (T == CUQ_BF16) {  // Gguf.readF16 of a bf16 tensor: RN16(f32(bf16))
-        const uint16_t *src = reinterpret_cast<const uint16_t *>(w.q + ((size_t)row * w.cols + k0) * 2);
-        uint4 v[8];
 #pragma unroll
-        for (int i = 0; i < 8; i++) v[i] = reinterpret_cast<const uint4 *>(src)[i];
-        const uint16_t *bb = reinterpret_cast<const uint16_t *>(v);
+        for (int c = 0; c < 8; c++) {
+            const uint4 v = chunk(c);
+            const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+            uint32_t o[4];
 #pragma unroll
-        for (int j = 0; j < 64; j++) o[j] = __float2half_rn(__uint_as_float((uint32_t)bb[j] << 16));
+            for (int i = 0; i < 4; i++)
+                o[i] = h2u(__floats2half2_rn(__uint_as_float(wv[i] << 16), __uint_as_float(wv[i] & 0xFFFF0000u)));
+            out[c] = make_uint4(o[0], o[1], o[2], o[3]);
+        }
+    } else {  // legacy 32-blocks (gguf.zig:763-825), scalar fp32 as the reference
+        constexpr int SE = (T == CUQ_Q4_1 || T == CUQ_Q5_1) ? 4 : 2;
+        const uint4 q0 = chunk(0), q1 = chunk(1);
+        const uint8_t *b = reinterpret_cast<const uint8_t *>(&q0);
+        const uint8_t *b1 = reinterpret_cast<const uint8_t *>(&q1);
+        __half vals[64];
+#pragma unroll
+        for (int blk = 0; blk < 2; blk++) {
+            const uint8_t *bb = blk ? b1 : b;
+            float dd, m = 0.f;
+            if (SE == 2) {
+                dd = __half2float(reinterpret_cast<const __half *>(side)[blk * 128 + srow]);
+            } else {
+                const __half2 dm = reinterpret_cast<const __half2 *>(side)[blk * 128 + srow];
+                dd = __low2float(dm);
+                m = __high2float(dm);
+            }
+            const uint32_t qh = (T == CUQ_Q5_0 || T == CUQ_Q5_1)
+                                    ? reinterpret_cast<const uint32_t *>(side + 2 * 128 * SE + blk * 512)[srow]
+                                    : 0u;
+#pragma unroll
+            for (int j = 0; j < 32; j++) {
+                const int byte = bb[j & 15];
+                const int nib = j < 16 ? (byte & 0xF) : (byte >> 4);
+                float val;
+                if (T == CUQ_Q4_0) {
+                    val = __fmul_rn((float)(nib - 8), dd);
+                } else if (T == CUQ_Q4_1) {
+                    val = __fadd_rn(__fmul_rn((float)nib, dd), m);
+                } else {
+                    const int hb = j < 16 ? (int)(((qh >> j) << 4) & 0x10u) : (int)((qh >> (j - 16 + 12)) & 0x10u);
+                    const float x = (float)((nib | hb) - (T == CUQ_Q5_0 ? 16 : 0));
+                    val = __fadd_rn(__fmul_rn(x, dd), m);
+                }
+                vals[blk * 32 + j] = __float2half_rn(val);
+            }
+        }
+#pragma unroll
+        for (int c = 0; c < 8; c++) out[c] = reinterpret_cast<const uint4 *>(vals)[c];
     }
+    (void)dual;
+}
+
+// ---------------------------------------------------------------- TMA ----
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
 }
 
 // ------------------------------------------------------------- kernel ----
 
-struct QgArgs {
+struct __align__(64) QgArgs {
+    CUtensorMap mh, ml;        // x hi / lo [n][cols] fp16, box 64 x 128, 128-byte swizzle
     WPlanes w, w2;             // w2: the up matrix of a gate|up pair
-    const __half *xh, *xl;     // [n][cols] activation hi / lo
     uint32_t n;
     float *y;                  // [n][ldy] fp32 output (STORE / ADD)
     uint32_t ldy;
@@ -252,32 +433,39 @@ struct QgArgs {
     int *err;                  // set to 1 when a wait timed out
 };
 
+// Warps 0-3: weight producers (raw prefetch + dequant into the A stage), then
+// the epilogue; warp 4: TMEM allocation and the MMA issuer (lane 0); warp 5
+// lane 0: TMA loads of the x hi / lo tiles into the B stage.
 template <int T, int EPI>
-__global__ void __launch_bounds__(160, 1) qgemm_tc_kernel(const QgArgs p) {
+__global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const __grid_constant__ QgArgs p) {
+    using G = Geo<T>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint8_t *raw = smem + STAGES * STAGE_BYTES;
+    uint64_t *full = reinterpret_cast<uint64_t *>(raw + G::RAWD * G::SLOT);
     uint64_t *empty = full + STAGES;
     uint64_t *done = empty + STAGES;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    __shared__ float xchg[64][33];  // SILU: up values handed to the gate rows
+    volatile int *stop = abort_flag + 1;  // [2] producers' per-step snapshot of abort_flag
+    // SILU epilogue: up values handed to the gate rows, in stage 0 (free once every MMA completed)
+    float(*xchg)[33] = reinterpret_cast<float(*)[33]>(smem);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
     const uint32_t rows = p.w.rows, cols = p.w.cols;
     const uint32_t nkb = cols / BK;
-    // DUAL: the tile is 64 gate rows followed by the same 64 up rows
     const uint32_t row0 = blockIdx.x * (DUAL ? BM / 2 : BM);
     const uint32_t tok0 = blockIdx.y * BN;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 128);
+            mbar_init(&full[s], 129);  // 128 producer arrivals + the TMA thread's expect_tx
             mbar_init(&empty[s], 1);
         }
         mbar_init(done, 1);
         *abort_flag = 0;
+        stop[0] = stop[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     if (warp == 4) {  // tensor memory for the 128 x 256 fp32 accumulator
@@ -293,46 +481,33 @@ __global__ void __launch_bounds__(160, 1) qgemm_tc_kernel(const QgArgs p) {
 
     if (warp < 4) {
         // ---------------------------------------------------- producers
-        const uint32_t t = threadIdx.x;  // A row within the tile
+        const int t = threadIdx.x;
+        for (uint32_t i = 0; i + 1 < (uint32_t)G::RAWD && i < nkb; i++) {
+            raw_issue<T>(p.w, p.w2, DUAL, row0, i, raw + i * G::SLOT, t);
+            cp_async_commit();
+        }
+        for (uint32_t i = nkb; i + 1 < (uint32_t)G::RAWD; i++) cp_async_commit();  // keep the group count uniform
         for (uint32_t kb = 0; kb < nkb; kb++) {
             const int s = kb % STAGES;
-            if (kb >= (uint32_t)STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag)) break;
-            uint8_t *A = smem + s * STAGE_BYTES, *B = A + A_BYTES;
-            // A: one weight row per thread, 64 fp16 = 8 chunks of 16 B, swizzled
-            {
-                __half vals[64];
-                uint32_t r;
-                const WPlanes *wp = &p.w;
-                if (DUAL) {
-                    r = row0 + (t & 63);
-                    wp = t < 64 ? &p.w : &p.w2;
-                } else {
-                    r = row0 + t;
-                }
-                if (r < rows)
-                    dequant64<T>(*wp, r, kb, vals);
-                else
-#pragma unroll
-                    for (int j = 0; j < 64; j++) vals[j] = __float2half_rn(0.f);
-#pragma unroll
-                for (int c = 0; c < 8; c++)
-                    *reinterpret_cast<uint4 *>(A + t * 128 + ((c ^ (t & 7)) * 16)) = reinterpret_cast<uint4 *>(vals)[c];
+            if (t == 0) {
+                if (kb >= (uint32_t)STAGES) mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag);
+                stop[kb & 1] = *abort_flag;
             }
-            // B: 256 rows (128 hi tokens, 128 lo tokens) x 8 chunks, 16 per thread
-#pragma unroll 4
-            for (int j = 0; j < 16; j++) {
-                const uint32_t q = t + 128 * j, b = q >> 3, c = q & 7;
-                const uint32_t tok = tok0 + (b & 127);
-                uint4 v = make_uint4(0u, 0u, 0u, 0u);
-                if (tok < p.n) {
-                    const __half *src = (b < 128 ? p.xh : p.xl) + (size_t)tok * cols + kb * BK + c * 8;
-                    v = *reinterpret_cast<const uint4 *>(src);
-                }
-                *reinterpret_cast<uint4 *>(B + b * 128 + ((c ^ (b & 7)) * 16)) = v;
-            }
+            cp_async_wait<G::RAWD - 2>();
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // raw step kb landed; slot of kb-1 is free
+            if (stop[kb & 1]) break;
+            if (kb + G::RAWD - 1 < nkb)
+                raw_issue<T>(p.w, p.w2, DUAL, row0, kb + G::RAWD - 1, raw + ((kb + G::RAWD - 1) % G::RAWD) * G::SLOT, t);
+            cp_async_commit();
+            uint4 vals[8];
+            dequant_smem<T>(raw + (kb % G::RAWD) * G::SLOT, t, kb, DUAL, vals);
+            uint8_t *A = smem + s * STAGE_BYTES;
+#pragma unroll
+            for (int c = 0; c < 8; c++) *reinterpret_cast<uint4 *>(A + t * 128 + ((c ^ (t & 7)) * 16)) = vals[c];
             fence_async_smem();
             mbar_arrive(&full[s]);
         }
+        cp_async_wait<0>();
         // ---------------------------------------------------- epilogue
         mbar_wait(done, 0, abort_flag);
         asm volatile("bar.sync 1, 128;" ::: "memory");  // all producers past the wait: abort_flag is final
@@ -354,7 +529,7 @@ __global__ void __launch_bounds__(160, 1) qgemm_tc_kernel(const QgArgs p) {
                     asm volatile("bar.sync 1, 128;" ::: "memory");
                     if (trow < 64) {
                         const uint32_t r = row0 + trow;
-#pragma unroll 4
+#pragma unroll
                         for (int i = 0; i < 32; i++) {
                             const uint32_t tok = tok0 + ch * 32 + i;
                             if (tok >= p.n || r >= rows) continue;
@@ -371,10 +546,10 @@ __global__ void __launch_bounds__(160, 1) qgemm_tc_kernel(const QgArgs p) {
                     const uint32_t r = row0 + trow;
                     if (r < rows) {
                         const float b = p.bias ? p.bias[r] : 0.f;
-#pragma unroll 4
+#pragma unroll
                         for (int i = 0; i < 32; i++) {
                             const uint32_t tok = tok0 + ch * 32 + i;
-                            if (tok >= p.n) break;
+                            if (tok >= p.n) continue;
                             float v = hi[i] + lo[i];
                             if (p.bias) v = v + b;
                             float *dst = p.y + (size_t)tok * p.ldy + r;
@@ -387,24 +562,36 @@ __global__ void __launch_bounds__(160, 1) qgemm_tc_kernel(const QgArgs p) {
                 }
             }
         }
+    } else if (warp == 4) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            bool ok = true;
+            for (uint32_t kb = 0; kb < nkb; kb++) {
+                const int s = kb % STAGES;
+                if (!mbar_wait(&full[s], (kb / STAGES) & 1, abort_flag)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
+#pragma unroll
+                for (int k = 0; k < BK / 16; k++)
+                    umma_f16(tmem, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) ? 1u : 0u);
+                umma_commit(&empty[s]);  // frees the stage when these MMAs complete
+            }
+            if (ok) umma_commit(done);
+            else mbar_arrive(done);      // let the epilogue stop waiting
+        }
     } else if (lane == 0) {
-        // ---------------------------------------------------- MMA issuer
-        bool ok = true;
+        // ---------------------------------------------------- TMA: x hi / lo
         for (uint32_t kb = 0; kb < nkb; kb++) {
             const int s = kb % STAGES;
-            if (!mbar_wait(&full[s], (kb / STAGES) & 1, abort_flag)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
-#pragma unroll
-            for (int k = 0; k < BK / 16; k++)
-                umma_f16(tmem, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) ? 1u : 0u);
-            umma_commit(&empty[s]);  // frees the stage when these MMAs complete
+            if (kb >= (uint32_t)STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag)) break;
+            const uint32_t b = smem_u32(smem + s * STAGE_BYTES + A_BYTES);
+            mbar_expect_tx(&full[s], B_BYTES);
+            tma_load_2d(b, &p.mh, (int)(kb * BK), (int)tok0, &full[s]);
+            tma_load_2d(b + B_BYTES / 2, &p.ml, (int)(kb * BK), (int)tok0, &full[s]);
         }
-        if (ok) umma_commit(done);
-        else mbar_arrive(done);      // let the epilogue stop waiting
     }
     tc_fence_before();
     __syncthreads();
@@ -420,7 +607,7 @@ int launch_tq(const QgArgs &a, uint32_t rows, uint32_t n, cudaStream_t s) {
     auto kern = qgemm_tc_kernel<T, EPI>;
     static bool attr_set = false;  // per instantiation
     if (!attr_set) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Geo<T>::SMEM);
         if (e != cudaSuccess) {
             set_error("qgemm: shared memory opt-in failed: %s", cudaGetErrorString(e));
             return CUQ_ECUDA;
@@ -429,7 +616,7 @@ int launch_tq(const QgArgs &a, uint32_t rows, uint32_t n, cudaStream_t s) {
     }
     const uint32_t rows_per_cta = EPI == EPI_SILU_XQ ? BM / 2 : BM;
     dim3 grid((rows + rows_per_cta - 1) / rows_per_cta, (n + BN - 1) / BN);
-    kern<<<grid, 160, SMEM_BYTES, s>>>(a);
+    kern<<<grid, 192, Geo<T>::SMEM, s>>>(a);
     CUQ_CUDA_TRY(cudaGetLastError());
     return CUQ_OK;
 }
@@ -449,6 +636,29 @@ int dispatch(int type, const QgArgs &a, uint32_t rows, uint32_t n, cudaStream_t 
     }
     set_error("UnsupportedType: no tensor-core GEMM for ggml type %d", type);
     return CUQ_EUNSUPPORTED;
+}
+
+// Tensor map of an x part [n][cols] fp16 (row stride cols*2 bytes): boxes of
+// 64 columns x 128 tokens in the 128-byte swizzle the MMA descriptors expect;
+// tokens past n read as zero.
+int make_x_map(CUtensorMap *m, const __half *base, uint32_t n, uint32_t cols) {
+    if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16) {
+        set_error("qgemm: activation must be 16-byte aligned with 16-byte rows");
+        return CUQ_EINVAL;
+    }
+    cuuint64_t dims[2] = {cols, n};
+    cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+    cuuint32_t box[2] = {BK, BN};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = cuTensorMapEncodeTiled(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims,
+                                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        set_error("qgemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
+        return CUQ_ECUDA;
+    }
+    return CUQ_OK;
 }
 
 WPlanes wplanes(const Planes &p) {
@@ -480,10 +690,11 @@ int launch_qgemm(const QgemmArgs &g, int epi, cudaStream_t s) {
     }
     if (g.n == 0) return CUQ_OK;
     QgArgs a;
+    int rc = make_x_map(&a.mh, g.xh, g.n, w.cols);
+    if (rc == CUQ_OK) rc = make_x_map(&a.ml, g.xl, g.n, w.cols);
+    if (rc) return rc;
     a.w = wplanes(w);
     if (g.w2) a.w2 = wplanes(*g.w2);
-    a.xh = g.xh;
-    a.xl = g.xl;
     a.n = g.n;
     a.y = g.y;
     a.ldy = g.ldy ? g.ldy : w.rows;
