@@ -502,123 +502,6 @@ __global__ void rmsnorm_hilo_kernel(const float *__restrict__ x, const float *__
     }
 }
 
-// Causal attention for a chunk of prompt positions (cpu.attentionPrefill,
-// cpu.zig:165-217, semantically attentionDecode per position): CTA (kv head,
-// query) walks cache positions [0, pos] with the online softmax of
-// attn_decode_kernel and writes the normalised result as fp16 hi + lo.
-template <int HD, int G>
-__global__ void __launch_bounds__(128) attn_prefill_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
-                                                            const __half *__restrict__ vc, uint32_t cache_stride,
-                                                            uint32_t pos0, uint32_t heads, __half *__restrict__ oh,
-                                                            __half *__restrict__ ol) {
-    constexpr int E = 8, LPP = HD / E, PPW = 32 / LPP;
-    const uint32_t kvh = blockIdx.x, qi = blockIdx.y;
-    const uint32_t n = pos0 + qi + 1;  // positions this query sees
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int lp = lane % LPP, pg = lane / LPP;
-    const float scale = 1.0f / sqrtf((float)HD);
-    const uint32_t qd = heads * HD;
-    float qr[G][E];
-#pragma unroll
-    for (int g = 0; g < G; g++)
-#pragma unroll
-        for (int e = 0; e < E; e++) qr[g][e] = q[(size_t)qi * qd + (size_t)(kvh * G + g) * HD + lp * E + e];
-    float m[G], l[G], o[G][E];
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-        m[g] = -INFINITY;
-        l[g] = 0.f;
-#pragma unroll
-        for (int e = 0; e < E; e++) o[g][e] = 0.f;
-    }
-    const __half *kh = kc + (size_t)kvh * cache_stride * HD;
-    const __half *vh = vc + (size_t)kvh * cache_stride * HD;
-    for (uint32_t pb = warp * PPW; pb < n; pb += 4 * PPW) {  // warp-uniform bound
-        const uint32_t pp = pb + pg;
-        const bool valid = pp < n;
-        float kf[E], vf[E];
-        uint4 ku = make_uint4(0u, 0u, 0u, 0u), vu = make_uint4(0u, 0u, 0u, 0u);
-        if (valid) {
-            ku = *reinterpret_cast<const uint4 *>(kh + (size_t)pp * HD + lp * E);
-            vu = *reinterpret_cast<const uint4 *>(vh + (size_t)pp * HD + lp * E);
-        }
-        const __half2 *k2 = reinterpret_cast<const __half2 *>(&ku);
-        const __half2 *v2 = reinterpret_cast<const __half2 *>(&vu);
-#pragma unroll
-        for (int j = 0; j < 4; j++) {
-            float2 kk = __half22float2(k2[j]), vv = __half22float2(v2[j]);
-            kf[2 * j] = kk.x;
-            kf[2 * j + 1] = kk.y;
-            vf[2 * j] = vv.x;
-            vf[2 * j + 1] = vv.y;
-        }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float d = 0.f;
-#pragma unroll
-            for (int e = 0; e < E; e++) d = fmaf(qr[g][e], kf[e], d);
-#pragma unroll
-            for (int sh = 1; sh < LPP; sh <<= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
-            if (valid) {
-                float s = d * scale;
-                float mn = fmaxf(m[g], s);
-                float corr = expf(m[g] - mn);
-                float pe = expf(s - mn);
-                l[g] = l[g] * corr + pe;
-#pragma unroll
-                for (int e = 0; e < E; e++) o[g][e] = o[g][e] * corr + pe * vf[e];
-                m[g] = mn;
-            }
-        }
-    }
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-#pragma unroll
-        for (int sh = LPP; sh < 32; sh <<= 1) {
-            float mo = __shfl_xor_sync(0xffffffffu, m[g], sh);
-            float lo = __shfl_xor_sync(0xffffffffu, l[g], sh);
-            float mn = fmaxf(m[g], mo);
-            float ca = mn == -INFINITY ? 0.f : expf(m[g] - mn);
-            float cb = mn == -INFINITY ? 0.f : expf(mo - mn);
-            l[g] = l[g] * ca + lo * cb;
-#pragma unroll
-            for (int e = 0; e < E; e++) {
-                float oo = __shfl_xor_sync(0xffffffffu, o[g][e], sh);
-                o[g][e] = o[g][e] * ca + oo * cb;
-            }
-            m[g] = mn;
-        }
-    }
-    __shared__ float sm_m[4][G], sm_l[4][G], sm_o[4][G][HD];
-    if (pg == 0) {
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            if (lp == 0) {
-                sm_m[warp][g] = m[g];
-                sm_l[warp][g] = l[g];
-            }
-#pragma unroll
-            for (int e = 0; e < E; e++) sm_o[warp][g][lp * E + e] = o[g][e];
-        }
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
-        int g = t / HD, dd = t % HD;
-        float mm = fmaxf(fmaxf(sm_m[0][g], sm_m[1][g]), fmaxf(sm_m[2][g], sm_m[3][g]));
-        float acc = 0.f, ll = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; w++) {
-            float c = mm == -INFINITY ? 0.f : expf(sm_m[w][g] - mm);
-            acc += sm_o[w][g][dd] * c;
-            ll += sm_l[w][g] * c;
-        }
-        float r = acc / ll;
-        size_t i = (size_t)qi * qd + (size_t)(kvh * G + g) * HD + dd;
-        __half h = __float2half_rn(r);
-        oh[i] = h;
-        ol[i] = __float2half_rn(r - __half2float(h));
-    }
-}
 
 // siluMul (cpu.zig:65-70) of separate gate / up GEMM outputs, as hi + lo.
 __global__ void silu_hilo_kernel(const float *__restrict__ g, const float *__restrict__ u, size_t count,
@@ -783,28 +666,6 @@ int launch_rmsnorm_hilo(const float *x, const float *w, uint32_t n, uint32_t n_r
     return CUQ_OK;
 }
 
-int launch_attention_prefill(const float *q, const __half *k_cache, const __half *v_cache, uint32_t cache_stride,
-                             uint32_t pos0, uint32_t n_q, uint32_t heads, uint32_t kv_heads, uint32_t hd,
-                             __half *oh, __half *ol, cudaStream_t s) {
-    if (kv_heads == 0 || heads % kv_heads) {
-        set_error("attention: heads (%u) must be a multiple of kv_heads (%u)", heads, kv_heads);
-        return CUQ_EINVAL;
-    }
-    if (n_q == 0) return CUQ_OK;
-    uint32_t G = heads / kv_heads;
-    dim3 grid(kv_heads, n_q);
-#define CUQ_ATP(HDV, GV) \
-    if (hd == HDV && G == GV) attn_prefill_kernel<HDV, GV><<<grid, 128, 0, s>>>(q, k_cache, v_cache, cache_stride, pos0, heads, oh, ol); else
-    CUQ_ATP(64, 1) CUQ_ATP(64, 2) CUQ_ATP(64, 3) CUQ_ATP(64, 4) CUQ_ATP(64, 6) CUQ_ATP(64, 7) CUQ_ATP(64, 8)
-    CUQ_ATP(128, 1) CUQ_ATP(128, 2) CUQ_ATP(128, 3) CUQ_ATP(128, 4) CUQ_ATP(128, 6) CUQ_ATP(128, 7)
-    CUQ_ATP(128, 8) {
-        set_error("attention: unsupported head_dim %u / group %u (head_dim 64 or 128, group 1-8)", hd, G);
-        return CUQ_EUNSUPPORTED;
-    }
-#undef CUQ_ATP
-    CUQ_CUDA_TRY(cudaGetLastError());
-    return CUQ_OK;
-}
 
 int launch_silu_hilo(const float *g, const float *u, size_t count, __half *hi, __half *lo, cudaStream_t s) {
     size_t grid = (count + 255) / 256;

@@ -28,7 +28,8 @@ constexpr int A_BYTES = BM * BK * 2;        // 16 KB
 constexpr int B_BYTES = 2 * BN * BK * 2;    // 32 KB (hi + lo)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 256;
-constexpr uint32_t WAIT_LIMIT = 1u << 24;   // try_wait polls before giving up (seconds)
+constexpr unsigned long long WAIT_NS = 2000000000ull;  // a stage wait gives up after 2 s
+constexpr uint32_t SUSPEND_NS = 20000;                   // try_wait sleeps up to 20 us per poll
 
 __device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
 
@@ -38,23 +39,34 @@ __device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// try_wait with a suspend-time hint: the thread sleeps until the phase
+// completes (or the hint expires) instead of spinning, so waiting warps take
+// no issue slots from the producers sharing their SM sub-partition.
 __device__ __forceinline__ uint32_t mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(SUSPEND_NS)
         : "memory");
     return ok;
 }
-// Bounded wait for the phase with `parity`; false on timeout or when another
-// thread of the CTA has already given up.
+__device__ __forceinline__ unsigned long long now_ns() {
+    unsigned long long v;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(v));
+    return v;
+}
+// Bounded wait for the phase with `parity`; false on timeout (WAIT_NS) or when
+// another thread of the CTA has already given up.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    for (uint32_t i = 0; i < WAIT_LIMIT; i++) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const unsigned long long t0 = now_ns();
+    while (true) {
         if (mbar_try_wait(bar, parity)) return true;
         if (*abort_flag) return false;
+        if (now_ns() - t0 > WAIT_NS) break;
     }
     *abort_flag = 1;
     return false;

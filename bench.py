@@ -27,7 +27,8 @@ is that sequence's tokens/s); c2-c4 do not shard and run one replica per rank
 `--impl reference`: the reference CPU path (the C oracle restating src/cpu.zig
 + main.zig refForward; the Zig reference cannot be built here) on all host
 cores, rank 0 only, on a bounded sample of the same workload.
-`--profile gemv`: 6 launches of the roofline GEMV only (for an ncu capture).
+`--profile gemv`: 6 launches of the roofline GEMV only; `--profile qgemm`: 4
+prefill GEMMs of the config's first ffn_gate on 512 tokens (for ncu captures).
 """
 import argparse
 import ctypes
@@ -74,7 +75,7 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default=None, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--profile", choices=["gemv"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "qgemm"], default=None,
                     help="run only the roofline kernel (a few launches) for an ncu capture, print nothing")
     return ap.parse_args()
 
@@ -398,6 +399,18 @@ def profile_case(args):
         s = torch.cuda.Stream()
         ttype, raw, rows, cols = head_shard(model, C, 0, 1)
         gemv_roofline(ttype, raw, rows, cols, s.cuda_stream, peaks()[0], name, reps=0)
+    elif args.profile == "qgemm":
+        # the prefill GEMM of the config's first ffn_gate on a 512-token chunk, 4 launches
+        L = rt.load()
+        t = model.tensor("blk.0.ffn_gate.weight")
+        raw = np.frombuffer(t.data, dtype=np.uint8)
+        h = L.cuq_weight_create(t.ggml_type, raw.ctypes.data_as(ctypes.c_void_p), raw.size, t.rows, t.cols)
+        assert h, rt.last_error()
+        x = torch.randn(512, t.cols, device="cuda")
+        y = torch.empty(512, t.rows, device="cuda")
+        for _ in range(4):
+            rt.check(L.cuq_gemm(h, ctypes.c_void_p(x.data_ptr()), 512, ctypes.c_void_p(y.data_ptr()), None))
+        L.cuq_weight_free(h)
     torch.cuda.synchronize()
 
 
