@@ -75,6 +75,8 @@ struct TQ8_0 {
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
     struct Raw { uint4 q[2]; __half2 d[2]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         uint32_t k = it * SPAN + tig * 16;
         if (k < w.cols) {
@@ -89,7 +91,7 @@ struct TQ8_0 {
         }
     }
     __device__ static uint32_t word(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
-    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
         const __half2 off = __float2half2_rn(1152.f);
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
@@ -111,6 +113,8 @@ struct TQ4L {
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
     struct Raw { uint4 q[2]; __half2 d[2], m[2]; uint32_t qh[2]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         uint32_t k = it * SPAN + tig * 32;
         if (k < w.cols) {
@@ -144,7 +148,7 @@ struct TQ4L {
         }
     }
     // k-step s: word i = s >> 1 of the block, low nibbles (s even) or high (s odd).
-    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
         const int i = s >> 1;
         const bool hi = s & 1;
         constexpr bool five = (T == CUQ_Q5_0 || T == CUQ_Q5_1);
@@ -192,7 +196,10 @@ struct TQ4L {
 struct TQ4K {
     static constexpr int SPAN = 256, KSTEPS = 16, DEPTH = 1;
     static constexpr bool HAS_CORR = true;
-    struct Raw { uint4 q[2][2]; __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
+    // prefetched: the quant bytes and the 16-byte scale record of rows r0, r0+8
+    struct Raw { uint4 q[2][2]; uint4 meta[2]; };
+    // derived at compute time (keeps the prefetch ring small)
+    struct Prep { __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
@@ -200,9 +207,15 @@ struct TQ4K {
             const uint8_t *qp = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + tig * 32;
             R.q[rr][0] = ldg_stream(qp);
             R.q[rr][1] = ldg_stream(qp + 16);
-            uint4 meta = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
-            R.d[rr] = __half2half2(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
-            float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
+            R.meta[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
+        }
+    }
+    __device__ static void prep(const Raw &R, int tig, Prep &P) {
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const uint4 meta = R.meta[rr];
+            P.d[rr] = __half2half2(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
+            const float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
 #pragma unroll
             for (int part = 0; part < 2; part++) {
                 // get_scale_min_k4 (gguf.zig:960-973) for sub-block j = 2*tig + part,
@@ -212,34 +225,34 @@ struct TQ4K {
                 const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
                 const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
                 const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
-                R.sc[rr][part] = __float2half2_rn((float)sc);
-                R.csc[rr][part] = __float2half2_rn(-1024.f * (float)sc);  // exact: |1024*63| < 65504
-                float m1 = dmin * (float)mm;                                // exact in fp32
-                __half m1h = __float2half_rn(m1);
-                R.nm1[rr][part] = __half2half2(__hneg(m1h));
-                R.m1[rr][part] = m1 - __half2float(m1h);                    // remainder, exact
+                P.sc[rr][part] = __float2half2_rn((float)sc);
+                P.csc[rr][part] = __float2half2_rn(-1024.f * (float)sc);  // exact: |1024*63| < 65504
+                const float m1 = dmin * (float)mm;                         // exact in fp32
+                const __half m1h = __float2half_rn(m1);
+                P.nm1[rr][part] = __half2half2(__hneg(m1h));
+                P.m1[rr][part] = m1 - __half2float(m1h);                   // remainder, exact
             }
         }
     }
     // k-step s: word i = s & 7 of the group, part = s >> 3 (low nibbles, then high).
-    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
         const int i = s & 7, part = s >> 3;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             uint32_t u = TQ8_0::word(R.q[rr][i >> 2], i & 3);
             uint32_t v02 = part ? (u >> 4) : u, v13 = part ? (u >> 12) : (u >> 8);
-            __half2 q02 = __hfma2(u2h(magic(v02, 0x000F000Fu)), R.sc[rr][part], R.csc[rr][part]);  // q*sc
-            __half2 q13 = __hfma2(u2h(magic(v13, 0x000F000Fu)), R.sc[rr][part], R.csc[rr][part]);
-            a[rr] = h2u(__hfma2(q02, R.d[rr], R.nm1[rr][part]));  // RN16(d1*q - m1h)
-            a[rr + 2] = h2u(__hfma2(q13, R.d[rr], R.nm1[rr][part]));
+            __half2 q02 = __hfma2(u2h(magic(v02, 0x000F000Fu)), P.sc[rr][part], P.csc[rr][part]);  // q*sc
+            __half2 q13 = __hfma2(u2h(magic(v13, 0x000F000Fu)), P.sc[rr][part], P.csc[rr][part]);
+            a[rr] = h2u(__hfma2(q02, P.d[rr], P.nm1[rr][part]));  // RN16(d1*q - m1h)
+            a[rr + 2] = h2u(__hfma2(q13, P.d[rr], P.nm1[rr][part]));
         }
     }
     // sum over this lane's two sub-blocks of (m1 - m1h) * sum(x), for rows r0 and r0+8
-    __device__ static void correct(const Raw &R, const float *xsum, int it, int tig, float &c0, float &c1) {
+    __device__ static void correct(const Prep &P, const float *xsum, int it, int tig, float &c0, float &c1) {
         float4 X = *reinterpret_cast<const float4 *>(xsum + 16 * it + 4 * tig);
         float xl = X.x + X.y, xh = X.z + X.w;
-        c0 += R.m1[0][0] * xl + R.m1[0][1] * xh;
-        c1 += R.m1[1][0] * xl + R.m1[1][1] * xh;
+        c0 += P.m1[0][0] * xl + P.m1[0][1] * xh;
+        c1 += P.m1[1][0] * xl + P.m1[1][1] * xh;
     }
     __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 64 + (s >> 3) * 32 + (s & 7) * 4; }
 };
@@ -255,7 +268,10 @@ struct TQ6K {
     static constexpr bool HAS_CORR = false;
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
-    struct Raw { uint4 a[2], b[2], h[2]; __half2 s[2][4], sl[2][4]; };
+    // prefetched: ql/qh bytes, the 16 int8 scales and d of rows r0, r0+8
+    struct Raw { uint4 a[2], b[2], h[2], scv[2]; __half d[2]; };
+    // derived at compute time: d*sc as an fp16 hi + lo pair per quarter
+    struct Prep { __half2 s[2][4], sl[2][4]; };
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         const int hh = tig >> 1, lh = (tig & 1) * 16;
 #pragma unroll
@@ -265,23 +281,31 @@ struct TQ6K {
             R.a[rr] = ldg_stream(ql);
             R.b[rr] = ldg_stream(ql + 32);
             R.h[rr] = ldg_stream(w.q2 + (size_t)r * (w.cols / 4) + (size_t)it * 64 + hh * 32 + lh);
-            uint4 scv = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
-            float d = __half2float(reinterpret_cast<const __half *>(w.s2)[(size_t)it * w.rows + r]);
+            R.scv[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
+            R.d[rr] = reinterpret_cast<const __half *>(w.s2)[(size_t)it * w.rows + r];
+        }
+    }
+    __device__ static void prep(const Raw &R, int tig, Prep &P) {
+        const int hh = tig >> 1;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const float d = __half2float(R.d[rr]);
+            const uint4 scv = R.scv[rr];
 #pragma unroll
             for (int t = 0; t < 4; t++) {
                 // int8 scale hh*8 + 2t + (tig&1), picked with a select and a runtime
                 // shift (no local-memory indexing)
                 const uint32_t wd = t < 2 ? (hh ? scv.z : scv.x) : (hh ? scv.w : scv.y);
                 const int sc = (int)(int8_t)((wd >> (8 * (2 * (t & 1) + (tig & 1)))) & 0xFFu);
-                float scale = d * (float)sc;  // exact
-                __half hi = __float2half_rn(scale);
-                R.s[rr][t] = __half2half2(hi);
-                R.sl[rr][t] = __float2half2_rn(scale - __half2float(hi));
+                const float scale = d * (float)sc;  // exact
+                const __half hi = __float2half_rn(scale);
+                P.s[rr][t] = __half2half2(hi);
+                P.sl[rr][t] = __float2half2_rn(scale - __half2float(hi));
             }
         }
     }
     // k-step s: t = s >> 2 (which quarter), word i = s & 3.
-    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
         const int t = s >> 2, i = s & 3;
         const __half2 off = __float2half2_rn(1056.f);  // 1024 + 32
 #pragma unroll
@@ -307,8 +331,8 @@ struct TQ6K {
                 break;
             }
             __half2 x02 = __hsub2(u2h(p02 | 0x64006400u), off), x13 = __hsub2(u2h(p13 | 0x64006400u), off);
-            a[rr] = h2u(__hfma2(x02, R.s[rr][t], __hmul2(x02, R.sl[rr][t])));  // ~RN16((q-32) * scale)
-            a[rr + 2] = h2u(__hfma2(x13, R.s[rr][t], __hmul2(x13, R.sl[rr][t])));
+            a[rr] = h2u(__hfma2(x02, P.s[rr][t], __hmul2(x02, P.sl[rr][t])));  // ~RN16((q-32) * scale)
+            a[rr + 2] = h2u(__hfma2(x13, P.s[rr][t], __hmul2(x13, P.sl[rr][t])));
         }
     }
     __device__ static uint32_t koff(int it, int tig, int s) {
@@ -324,6 +348,8 @@ struct T16 {
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
     struct Raw { uint4 q[2][2]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         uint32_t k = it * SPAN + tig * 16;
 #pragma unroll
@@ -342,7 +368,7 @@ struct T16 {
         float a = __uint_as_float(lo16src << 16), b = __uint_as_float(hi16src << 16);
         return h2u(__floats2half2_rn(a, b));
     }
-    __device__ static void frag(const Raw &R, int s, uint32_t (&a)[4]) {
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             const uint4 &v = R.q[rr][s >> 1];
@@ -449,21 +475,24 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
                 TT::load(ring[j], p.w, r0, itn, tig);
                 if (DUAL) TT::load(ring2[j], p.w2, r0, itn, tig);
             }
+            typename TT::Prep P, P2;
+            TT::prep(R, tig, P);
+            if (DUAL) TT::prep(R2, tig, P2);
 #pragma unroll
             for (int s = 0; s < TT::KSTEPS; s++) {
                 uint2 b = make_uint2(0u, 0u);
                 if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
                 uint32_t a[4];
-                TT::frag(R, s, a);
+                TT::frag(R, P, s, a);
                 mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
                 if (DUAL) {
-                    TT::frag(R2, s, a);
+                    TT::frag(R2, P2, s, a);
                     mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
                 }
             }
             if (TT::HAS_CORR) {
-                TT::correct(R, p.xsum, it, tig, k0, k1);
-                if (DUAL) TT::correct(R2, p.xsum, it, tig, k20, k21);
+                TT::correct(P, p.xsum, it, tig, k0, k1);
+                if (DUAL) TT::correct(P2, p.xsum, it, tig, k20, k21);
             }
         }
     }
