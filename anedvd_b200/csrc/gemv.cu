@@ -429,14 +429,18 @@ __device__ void finish_step(StepState *st, const uint32_t *forced, uint32_t *out
 // keeps D iterations of loads in flight ahead of the one it computes.
 template <class TT, int EPI, int KW, int D>
 __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
+    // Dual (gate|up): one tile per CTA, warps 0-1 stream the gate rows and
+    // warps 2-3 the same rows of up (KW = 2 per matrix), so no warp holds both.
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
-    constexpr int TPC = 4 / KW;           // tiles per CTA
-    constexpr int NV = DUAL ? 32 : 16;    // values per tile (gate rows then up rows)
-    __shared__ float red[4][NV];
+    constexpr int TPC = DUAL ? 1 : 4 / KW;  // tiles per CTA
+    constexpr int KWE = DUAL ? 2 : KW;      // warps per tile and matrix
+    constexpr int NV = DUAL ? 32 : 16;      // values per tile (gate rows then up rows)
+    __shared__ float red[4][16];
     __shared__ int is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
-    const int lt = warp / KW, kw = warp % KW;
+    const int lt = DUAL ? 0 : warp / KW, kw = warp % KWE;
+    const W &wm = (DUAL && warp >= 2) ? p.w2 : p.w;
     const uint32_t ntiles = p.w.rows / 16;
     const uint32_t tile = blockIdx.x * TPC + lt;
     const bool active = tile < ntiles;
@@ -447,14 +451,11 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
 
     // The weights do not depend on the previous kernel: start streaming the
     // warp's first D iterations before waiting for the activation.
-    typename TT::Raw ring[D], ring2[D];
+    typename TT::Raw ring[D];
 #pragma unroll
     for (int j = 0; j < D; j++) {
-        const int itj = it0 + kw + KW * j;
-        if (itj < it1) {
-            TT::load(ring[j], p.w, r0, itj, tig);
-            if (DUAL) TT::load(ring2[j], p.w2, r0, itj, tig);
-        }
+        const int itj = it0 + kw + KWE * j;
+        if (itj < it1) TT::load(ring[j], wm, r0, itj, tig);
     }
     griddep_wait();
     griddep_launch();
@@ -462,22 +463,18 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     const __half *xb = p.xq + (g == 1 ? p.kpad : 0);  // B fragments: L1-cached, shared by the SM's CTAs
     const bool bl = g < 2;
 
-    float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
-    float k0 = 0.f, k1 = 0.f, k20 = 0.f, k21 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
-    for (int base = it0 + kw; base < it1; base += KW * D) {
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    float k0 = 0.f, k1 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
+    for (int base = it0 + kw; base < it1; base += KWE * D) {
 #pragma unroll
         for (int j = 0; j < D; j++) {
-            const int it = base + KW * j;
+            const int it = base + KWE * j;
             if (it >= it1) break;  // uniform across the warp
-            typename TT::Raw R = ring[j], R2 = ring2[j];
-            const int itn = it + KW * D;
-            if (itn < it1) {  // refill this slot while the iteration computes
-                TT::load(ring[j], p.w, r0, itn, tig);
-                if (DUAL) TT::load(ring2[j], p.w2, r0, itn, tig);
-            }
-            typename TT::Prep P, P2;
+            typename TT::Raw R = ring[j];
+            const int itn = it + KWE * D;
+            if (itn < it1) TT::load(ring[j], wm, r0, itn, tig);  // refill this slot while the iteration computes
+            typename TT::Prep P;
             TT::prep(R, tig, P);
-            if (DUAL) TT::prep(R2, tig, P2);
 #pragma unroll
             for (int s = 0; s < TT::KSTEPS; s++) {
                 uint2 b = make_uint2(0u, 0u);
@@ -485,15 +482,8 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
                 uint32_t a[4];
                 TT::frag(R, P, s, a);
                 mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
-                if (DUAL) {
-                    TT::frag(R2, P2, s, a);
-                    mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
-                }
             }
-            if (TT::HAS_CORR) {
-                TT::correct(P, p.xsum, it, tig, k0, k1);
-                if (DUAL) TT::correct(P2, p.xsum, it, tig, k20, k21);
-            }
+            if (TT::HAS_CORR) TT::correct(P, p.xsum, it, tig, k0, k1);
         }
     }
     if (TT::HAS_CORR) {  // the four lanes of a row hold different sub-blocks: sum them
@@ -501,28 +491,23 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
         for (int sh = 1; sh <= 2; sh <<= 1) {
             k0 += __shfl_xor_sync(0xffffffffu, k0, sh);
             k1 += __shfl_xor_sync(0xffffffffu, k1, sh);
-            k20 += __shfl_xor_sync(0xffffffffu, k20, sh);
-            k21 += __shfl_xor_sync(0xffffffffu, k21, sh);
         }
     }
     if (tig == 0) {
         red[warp][g] = (c[0] + c[1]) - k0;
         red[warp][g + 8] = (c[2] + c[3]) - k1;
-        if (DUAL) {
-            red[warp][16 + g] = (c2[0] + c2[1]) - k20;
-            red[warp][16 + g + 8] = (c2[2] + c2[3]) - k21;
-        }
     }
     __syncthreads();
-    // thread t < TPC * NV owns value vi of local tile tl
+    // thread t < TPC * NV owns value vi of local tile tl (dual: vi < 16 gate, >= 16 up)
     const int t = threadIdx.x;
     const int tl = t / NV, vi = t % NV;
     const bool own = t < TPC * NV && blockIdx.x * TPC + tl < ntiles;
     const uint32_t row = (blockIdx.x * TPC + tl) * 16 + (vi & 15);
     float v = 0.f;
     if (own) {
+        const int w0 = DUAL ? 2 * (vi >> 4) : tl * KW;
 #pragma unroll
-        for (int w = 0; w < KW; w++) v += red[tl * KW + w][vi];
+        for (int w = 0; w < KWE; w++) v += red[w0 + w][vi & 15];
     }
     const uint32_t rows = p.w.rows;
     if (p.ksplit > 1) {
@@ -671,8 +656,8 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
 
 template <class TT, int EPI, int KW>
 cudaError_t launch_kw(const GemvArgs &a, const KArgs &k, cudaStream_t s) {
-    constexpr int D = EPI == EPI_SILU_XQ ? 1 : TT::DEPTH;
-    constexpr int TPC = 4 / KW;
+    constexpr int D = TT::DEPTH;
+    constexpr int TPC = EPI == EPI_SILU_XQ ? 1 : 4 / KW;
     dim3 grid((a.w->rows / 16 + TPC - 1) / TPC, k.ksplit);
     // the RMSNorm post-ops stage x in dynamic shared memory (reduce_norm_xq_block)
     const bool norm = a.post.op == POST_RMSNORM || a.post.op == POST_TP_REDUCE;
@@ -682,6 +667,7 @@ cudaError_t launch_kw(const GemvArgs &a, const KArgs &k, cudaStream_t s) {
 
 template <class TT, int EPI>
 cudaError_t launch_epi(const GemvArgs &a, const KArgs &k, int kw, cudaStream_t s) {
+    if (EPI == EPI_SILU_XQ) return launch_kw<TT, EPI, 2>(a, k, s);  // dual: 2 warps per matrix, one tile per CTA
     switch (kw) {
     case 1: return launch_kw<TT, EPI, 1>(a, k, s);
     case 2: return launch_kw<TT, EPI, 2>(a, k, s);
