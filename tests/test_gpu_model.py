@@ -72,6 +72,21 @@ def test_smollm2_full_size_matches_reference():
     assert e < LOGIT_TOL, e
 
 
+# BASELINE configs 3-5 at their full depth and vocabulary (config 5 with 8 of
+# its 32 layers, to keep the CPU oracle within a few GB of host memory).  The
+# weights are "tiled" payloads: every block a real quantised block, the same
+# bytes for the GPU and the oracle.
+FULL = [("qwen2.5-0.5b", {}), ("qwen2.5-1.5b", {}), ("llama3-8b", dict(layers=8))]
+
+
+@pytest.mark.parametrize("name,kw", FULL, ids=[f[0] for f in FULL])
+def test_full_size_configs_match_reference(name, kw):
+    import os
+    m = synth.model(name, payload="tiled", **kw)
+    e = _compare(m, n_prompt=12, n_decode=4, threads=os.cpu_count() or 8)
+    assert e < LOGIT_TOL, e
+
+
 @pytest.mark.parametrize("chunk", [1, 4, 7])
 def test_chunked_prefill_matches_reference(chunk):
     """The prompt split into several tensor-core chunks (the last one ragged)."""
