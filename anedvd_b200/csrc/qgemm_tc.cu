@@ -21,6 +21,8 @@
 
 namespace cuq {
 
+int sm_count_current();
+
 namespace {
 
 constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
@@ -148,7 +150,7 @@ struct Geo {
     static constexpr int CH = RAW_ROW / 16;                        // 16-byte chunks per row
     static constexpr int SLOT = BM * RAW_ROW + SIDE;               // bytes per raw slot
     static constexpr int RAWD = SLOT > 12288 ? 2 : 3;              // raw ring depth (fits 227 KB)
-    static constexpr int SMEM = STAGES * STAGE_BYTES + RAWD * SLOT + 1024 + 256;
+    static constexpr int SMEM = STAGES * STAGE_BYTES + RAWD * SLOT + 1024 + 256;  // + barriers
 };
 
 // physical 16-byte chunk of logical chunk c in row r (conflict-free 16-byte reads
@@ -166,72 +168,87 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// Issue the copies of K step kb into `slot` (thread t of the 128 producers).
+// Issue the copies of K step kb into `slot` for the 16 A rows of producer warp
+// pw (lane = 2 * row + half): every warp loads, and later reads, only its own
+// rows' bytes, so the 8 producer warps never wait for one another.
+// A row ar of a dual tile interleaves gate and up: matrix ar & 1, row ar >> 1.
+// Side records (scales, 5th bits) are indexed by side row sr: ar for a plain
+// tile, (ar & 1) * 64 + (ar >> 1) for a dual one, so 8 or 16 consecutive
+// matrix rows stay contiguous and copy as 16-byte chunks.
 template <int T>
 __device__ __forceinline__ void raw_issue(const WPlanes &w, const WPlanes &w2, bool dual, uint32_t row0, uint32_t kb,
-                                          uint8_t *slot, int t) {
+                                          uint8_t *slot, int pw, int lane) {
     using G = Geo<T>;
     const uint32_t sb = kb / 4;
-    // quant bytes of row t (gate rows then up rows in a dual tile)
-    const WPlanes &wp = (dual && t >= 64) ? w2 : w;
-    const uint32_t r = dual ? row0 + (t & 63) : row0 + t;
-    const uint32_t rr = r < wp.rows ? r : wp.rows - 1;  // rows past the end: any valid row (results unused)
+    const int ar = 16 * pw + (lane >> 1), half = lane & 1;
+    const WPlanes &wq = (dual && (ar & 1)) ? w2 : w;
+    const uint32_t rq = dual ? row0 + (ar >> 1) : row0 + ar;
+    const uint32_t rr = rq < wq.rows ? rq : wq.rows - 1;  // rows past the end: any valid row (results unused)
     const uint8_t *src;
     if (T == CUQ_Q8_0)
-        src = wp.q + (size_t)rr * wp.cols + kb * 64;
+        src = wq.q + (size_t)rr * wq.cols + kb * 64;
     else if (T == CUQ_F16 || T == CUQ_BF16)
-        src = wp.q + ((size_t)rr * wp.cols + kb * 64) * 2;
+        src = wq.q + ((size_t)rr * wq.cols + kb * 64) * 2;
     else if (T == CUQ_Q6_K)
-        src = wp.q + (size_t)rr * (wp.cols / 2) + (size_t)sb * 128 + 64 * ((kb % 4) / 2);
+        src = wq.q + (size_t)rr * (wq.cols / 2) + (size_t)sb * 128 + 64 * ((kb % 4) / 2);
     else
-        src = wp.q + (size_t)rr * (wp.cols / 2) + (size_t)kb * 32;
-    const uint32_t base = smem_u32(slot) + t * G::RAW_ROW;
-    const int nq = T == CUQ_Q6_K ? 4 : G::CH;  // Q6_K: ql 64 B here, qh 32 B below
+        src = wq.q + (size_t)rr * (wq.cols / 2) + (size_t)kb * 32;
+    const uint32_t base = smem_u32(slot) + ar * G::RAW_ROW;
+    if (T == CUQ_Q6_K) {  // ql 64 B = chunks 0-3, qh 32 B = chunks 4-5; three per thread
+        const uint8_t *qh = wq.q2 + (size_t)rr * (wq.cols / 4) + (size_t)sb * 64 + 32 * ((kb % 4) / 2);
 #pragma unroll
-    for (int c = 0; c < nq; c++) cp_async16(base + raw_chunk<G::CH>(t, c) * 16, src + 16 * c);
-    if (T == CUQ_Q6_K) {
-        const uint8_t *qh = wp.q2 + (size_t)rr * (wp.cols / 4) + (size_t)sb * 64 + 32 * ((kb % 4) / 2);
-        cp_async16(base + raw_chunk<G::CH>(t, 4) * 16, qh);
-        cp_async16(base + raw_chunk<G::CH>(t, 5) * 16, qh + 16);
+        for (int i = 0; i < 3; i++) {
+            const int c = 3 * half + i;
+            cp_async16(base + raw_chunk<G::CH>(ar, c) * 16, c < 4 ? src + 16 * c : qh + 16 * (c - 4));
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < G::CH / 2; i++) {
+            const int c = half * (G::CH / 2) + i;
+            cp_async16(base + raw_chunk<G::CH>(ar, c) * 16, src + 16 * c);
+        }
     }
-    // side data: block-major planes, so the tile's rows are contiguous; chunks
-    // of rows past the matrix end are skipped (their results are never stored)
     const uint32_t sside = smem_u32(slot + BM * G::RAW_ROW);
+    // the warp's side rows: one run of 16 (plain) or two runs of 8 (dual: gate, up)
+    const int nrun = dual ? 2 : 1, run_rows = dual ? 8 : 16;
     if (T == CUQ_Q4_K || T == CUQ_Q6_K) {
-        // 16 bytes of scales per row of superblock sb (Q4_K: d, dmin, 12 scale bytes)
-        const uint32_t ra = row0 + (dual ? (t & 63) : t);
-        if (ra < wp.rows) cp_async16(sside + 16 * t, wp.s + ((size_t)sb * wp.rows + ra) * 16);
-        if (T == CUQ_Q6_K && t < 16) {
-            // d: one fp16 per row = 8 rows per chunk (dual: 8 chunks of gate rows, 8 of up rows)
-            const bool upc = dual && t >= 8;
-            const WPlanes &a = upc ? w2 : w;
-            const uint32_t first = row0 + 8 * (dual ? (t & 7) : t);
+        // 16 bytes of scales per row of superblock sb: one chunk per side row
+        if (half == 0) {
+            const int sr = dual ? (ar & 1) * 64 + (ar >> 1) : ar;
+            const WPlanes &a = (dual && sr >= 64) ? w2 : w;
+            const uint32_t ra = row0 + (dual ? (sr & 63) : sr);
+            if (ra < a.rows) cp_async16(sside + 16 * sr, a.s + ((size_t)sb * a.rows + ra) * 16);
+        }
+        if (T == CUQ_Q6_K && lane < nrun * run_rows * 2 / 16) {  // d: fp16 per row, 8 rows per chunk
+            const int run = dual ? lane : 0, cir = dual ? 0 : lane;
+            const WPlanes &a = run ? w2 : w;
+            const int sr0 = dual ? run * 64 + 8 * pw : 16 * pw;
+            const uint32_t first = row0 + (dual ? 8 * pw : 16 * pw) + 8 * cir;
             if (first < a.rows)
-                cp_async16(sside + 2048 + 16 * t, a.s2 + ((size_t)sb * a.rows + first) * 2);
+                cp_async16(sside + 2048 + 2 * (sr0 + 8 * cir), a.s2 + ((size_t)sb * a.rows + first) * 2);
         }
     } else if (T != CUQ_F16 && T != CUQ_BF16) {
         // two 32-blocks per step; per block: d (2 B) or d|m (4 B) per row; Q5: qh 4 B per row
         constexpr int SE = (T == CUQ_Q4_1 || T == CUQ_Q5_1) ? 4 : 2;
-        constexpr int SB = 128 * SE;     // side bytes per block
-        constexpr int PER = SB / 16;     // chunks per block
-        constexpr int RPC = 16 / SE;     // rows per chunk
-        for (int c = t; c < 2 * PER; c += 128) {
-            const int blk = c / PER, cc = c % PER;
-            const bool upc = dual && cc >= PER / 2;
-            const WPlanes &a = upc ? w2 : w;
-            const uint32_t first = row0 + RPC * (dual ? (cc % (PER / 2)) : cc);
-            if (first < a.rows)
-                cp_async16(sside + blk * SB + 16 * cc, a.s + ((size_t)(kb * 2 + blk) * a.rows + first) * SE);
-        }
-        if (T == CUQ_Q5_0 || T == CUQ_Q5_1) {
-            for (int c = t; c < 2 * 32; c += 128) {  // qh: 4 rows per chunk, 32 chunks per block
-                const int blk = c / 32, cc = c % 32;
-                const bool upc = dual && cc >= 16;
-                const WPlanes &a = upc ? w2 : w;
-                const uint32_t first = row0 + 4 * (dual ? (cc % 16) : cc);
-                if (first < a.rows)
-                    cp_async16(sside + 2 * SB + blk * 512 + 16 * cc,
-                               a.q2 + ((size_t)(kb * 2 + blk) * a.rows + first) * 4);
+        constexpr int SB = 128 * SE;  // side bytes per block
+        constexpr bool Q5 = (T == CUQ_Q5_0 || T == CUQ_Q5_1);
+        const int cpr = run_rows * SE / 16;      // chunks per run of scale records
+        const int cq5 = run_rows * 4 / 16;       // chunks per run of qh words
+        const int per_blk = nrun * (cpr + (Q5 ? cq5 : 0));
+        for (int c = lane; c < 2 * per_blk; c += 32) {
+            const int blk = c / per_blk, rem = c % per_blk;
+            const bool isq = rem >= nrun * cpr;
+            const int r2 = isq ? rem - nrun * cpr : rem;
+            const int per = isq ? cq5 : cpr, esz = isq ? 4 : SE;
+            const int run = r2 / per, cc = r2 % per;
+            const WPlanes &a = run ? w2 : w;
+            const int sr0 = (dual ? run * 64 + 8 * pw : 16 * pw) + cc * (16 / esz);
+            const uint32_t first = row0 + (dual ? 8 * pw : 16 * pw) + cc * (16 / esz);
+            if (first < a.rows) {
+                if (isq)
+                    cp_async16(sside + 2 * SB + blk * 512 + 4 * sr0, a.q2 + ((size_t)(kb * 2 + blk) * a.rows + first) * 4);
+                else
+                    cp_async16(sside + blk * SB + esz * sr0, a.s + ((size_t)(kb * 2 + blk) * a.rows + first) * esz);
             }
         }
     }
@@ -270,22 +287,24 @@ __device__ __forceinline__ u64 bytes01_magic(uint32_t w, uint32_t sel0, uint32_t
 #define MAGIC23 8388608.0f
 
 // ------------------------------------------------- dequant from shared ----
-// Row t's 64 weights of step kb, as the reference's fp16 values (RN16 of the
-// fp32 dequant, gguf.zig:751-1071 / load_gguf.zig:371), in natural k order:
-// out[c] = weights 8c .. 8c+7.  Arithmetic rounds where the reference rounds.
+// Half `half` (32 weights) of A row ar's 64 weights of step kb, as the
+// reference's fp16 values (RN16 of the fp32 dequant, gguf.zig:751-1071 /
+// load_gguf.zig:371), in natural k order: out[i] = weights 32 half + 8i .. +7.
+// Arithmetic rounds where the reference rounds.
 template <int T>
-__device__ __forceinline__ void dequant_smem(const uint8_t *slot, int t, uint32_t kb, bool dual, uint4 (&out)[8]) {
+__device__ __forceinline__ void dequant_half(const uint8_t *slot, int ar, int half, uint32_t kb, bool dual,
+                                             uint4 (&out)[4]) {
     using G = Geo<T>;
-    const uint8_t *row = slot + t * G::RAW_ROW;
+    const uint8_t *row = slot + ar * G::RAW_ROW;
     const uint8_t *side = slot + BM * G::RAW_ROW;
-    auto chunk = [&](int c) { return *reinterpret_cast<const uint4 *>(row + raw_chunk<G::CH>(t, c) * 16); };
-    const int srow = t;  // side index of this row (dual tiles stack gate rows then up rows)
+    auto chunk = [&](int c) { return *reinterpret_cast<const uint4 *>(row + raw_chunk<G::CH>(ar, c) * 16); };
+    const int srow = dual ? (ar & 1) * 64 + (ar >> 1) : ar;  // side index of this row
     if (T == CUQ_Q8_0) {  // gguf.zig:827-840: RN16(d * q), the product is exact
         const __half2 off = __float2half2_rn(1152.f);
+        const __half2 d = __half2half2(reinterpret_cast<const __half *>(side)[half * 128 + srow]);
 #pragma unroll
-        for (int c4 = 0; c4 < 4; c4++) {
-            const uint4 v = chunk(c4);
-            const __half2 d = __half2half2(reinterpret_cast<const __half *>(side)[(c4 / 2) * 128 + srow]);
+        for (int c2 = 0; c2 < 2; c2++) {
+            const uint4 v = chunk(2 * half + c2);
             const uint32_t wv[4] = {v.x ^ 0x80808080u, v.y ^ 0x80808080u, v.z ^ 0x80808080u, v.w ^ 0x80808080u};
             uint32_t o[8];
 #pragma unroll
@@ -293,82 +312,66 @@ __device__ __forceinline__ void dequant_smem(const uint8_t *slot, int t, uint32_
                 o[2 * i] = h2u(__hmul2(__hsub2(u2h(__byte_perm(wv[i], 0x64646464u, 0x4140u)), off), d));
                 o[2 * i + 1] = h2u(__hmul2(__hsub2(u2h(__byte_perm(wv[i], 0x64646464u, 0x4342u)), off), d));
             }
-            out[2 * c4] = make_uint4(o[0], o[1], o[2], o[3]);
-            out[2 * c4 + 1] = make_uint4(o[4], o[5], o[6], o[7]);
+            out[2 * c2] = make_uint4(o[0], o[1], o[2], o[3]);
+            out[2 * c2 + 1] = make_uint4(o[4], o[5], o[6], o[7]);
         }
     } else if (T == CUQ_Q4_K) {  // gguf.zig:962-996: fp32 (d*sc)*q - dmin*m, then RN16
         const uint32_t c = kb % 4;
         const uint4 meta = reinterpret_cast<const uint4 *>(side)[srow];
         const float d = __half2float(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
         const float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
-        u64 d1[2], nm1[2];
-#pragma unroll
-        for (int part = 0; part < 2; part++) {
-            const int j = 2 * c + part, sh = 8 * (j & 3);
-            const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
-            const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
-            const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
-            const float a = __fmul_rn(d, (float)sc), m = __fmul_rn(dmin, (float)mm);
-            d1[part] = f2pack(a, a);
-            // fold the magic: d1*(2^23+q) - (d1*2^23 + m1) is not exact, so subtract 2^23 first
-            nm1[part] = f2pack(-m, -m);
-        }
-        const u64 mg = f2pack(MAGIC23, MAGIC23);
+        // sub-block 2c (low nibbles, half 0) or 2c+1 (high nibbles, half 1)
+        const int j = 2 * c + half, sh = 8 * (j & 3);
+        const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
+        const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
+        const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
+        const float a = __fmul_rn(d, (float)sc), m = __fmul_rn(dmin, (float)mm);
+        const u64 d1 = f2pack(a, a), nm1 = f2pack(-m, -m), mg = f2pack(MAGIC23, MAGIC23);
         const uint4 q0 = chunk(0), q1 = chunk(1);
         const uint32_t wv[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
-        for (int part = 0; part < 2; part++) {
-#pragma unroll
-            for (int i = 0; i < 8; i++) {  // 4 weights (one word) per i
-                const uint32_t nib = part ? ((wv[i] >> 4) & 0x0F0F0F0Fu) : (wv[i] & 0x0F0F0F0Fu);
-                const u64 a01 = fsub2(bytes01_magic(nib, 0x7440u, 0x7441u), mg);
-                const u64 a23 = fsub2(bytes01_magic(nib, 0x7442u, 0x7443u), mg);
-                const uint32_t h01 = cvt_h2(ffma2(d1[part], a01, nm1[part]));
-                const uint32_t h23 = cvt_h2(ffma2(d1[part], a23, nm1[part]));
-                uint32_t *o = reinterpret_cast<uint32_t *>(&out[part * 4 + i / 2]);
-                o[(i & 1) * 2] = h01;
-                o[(i & 1) * 2 + 1] = h23;
-            }
+        for (int i = 0; i < 8; i++) {  // 4 weights (one word) per i
+            const uint32_t nib = half ? ((wv[i] >> 4) & 0x0F0F0F0Fu) : (wv[i] & 0x0F0F0F0Fu);
+            const u64 a01 = fsub2(bytes01_magic(nib, 0x7440u, 0x7441u), mg);
+            const u64 a23 = fsub2(bytes01_magic(nib, 0x7442u, 0x7443u), mg);
+            uint32_t *o = reinterpret_cast<uint32_t *>(&out[i / 2]);
+            o[(i & 1) * 2] = cvt_h2(ffma2(d1, a01, nm1));
+            o[(i & 1) * 2 + 1] = cvt_h2(ffma2(d1, a23, nm1));
         }
     } else if (T == CUQ_Q6_K) {  // gguf.zig:1036-1059: fp32 (d*sc) * (q-32), then RN16
-        const uint32_t qtr = kb % 4, h = qtr / 2, t0 = 2 * (qtr % 2);
+        const uint32_t qtr = kb % 4, h = qtr / 2, tq = 2 * (qtr % 2) + half;
         const uint4 scv = reinterpret_cast<const uint4 *>(side)[srow];
         const float d = __half2float(reinterpret_cast<const __half *>(side + 2048)[srow]);
-        const uint4 L0 = chunk(0), L1 = chunk(1), L2 = chunk(2), L3 = chunk(3), H0 = chunk(4), H1 = chunk(5);
-        const uint32_t Lw[16] = {L0.x, L0.y, L0.z, L0.w, L1.x, L1.y, L1.z, L1.w,
-                                 L2.x, L2.y, L2.z, L2.w, L3.x, L3.y, L3.z, L3.w};
+        const uint4 La = chunk((tq & 1) ? 2 : 0), Lb = chunk((tq & 1) ? 3 : 1), H0 = chunk(4), H1 = chunk(5);
+        const uint32_t Lw[8] = {La.x, La.y, La.z, La.w, Lb.x, Lb.y, Lb.z, Lb.w};
         const uint32_t Hw[8] = {H0.x, H0.y, H0.z, H0.w, H1.x, H1.y, H1.z, H1.w};
         const u64 mg = f2pack(MAGIC23 + 32.f, MAGIC23 + 32.f);
 #pragma unroll
-        for (int tt = 0; tt < 2; tt++) {
-            const uint32_t tq = t0 + tt;  // which 32 of the half: ql lo/hi and qh bit pair
+        for (int sub = 0; sub < 2; sub++) {  // l in [16 sub, 16 sub + 16): one int8 scale
+            const int si = 8 * h + 2 * tq + sub;
+            const uint32_t sw = si < 4 ? scv.x : si < 8 ? scv.y : si < 12 ? scv.z : scv.w;
+            const float scale = __fmul_rn(d, (float)(int)(int8_t)((sw >> (8 * (si & 3))) & 0xFFu));
+            const u64 s2 = f2pack(scale, scale);
 #pragma unroll
-            for (int sub = 0; sub < 2; sub++) {  // l in [16 sub, 16 sub + 16): one int8 scale
-                const int si = 8 * h + 2 * tq + sub;
-                const uint32_t sw = si < 4 ? scv.x : si < 8 ? scv.y : si < 12 ? scv.z : scv.w;
-                const float scale = __fmul_rn(d, (float)(int)(int8_t)((sw >> (8 * (si & 3))) & 0xFFu));
-                const u64 s2 = f2pack(scale, scale);
-#pragma unroll
-                for (int i = 0; i < 4; i++) {  // 4 words of 4 weights
-                    const int l4 = sub * 4 + i;  // word index of l in 0..7
-                    const uint32_t L = (tq & 1) ? Lw[8 + l4] : Lw[l4];
-                    const uint32_t lo = (tq >= 2) ? ((L >> 4) & 0x0F0F0F0Fu) : (L & 0x0F0F0F0Fu);
-                    const uint32_t q = lo | (((Hw[l4] >> (2 * tq)) & 0x03030303u) << 4);
-                    const u64 a01 = fsub2(bytes01_magic(q, 0x7440u, 0x7441u), mg);
-                    const u64 a23 = fsub2(bytes01_magic(q, 0x7442u, 0x7443u), mg);
-                    uint32_t *o = reinterpret_cast<uint32_t *>(&out[tt * 4 + l4 / 2]);
-                    o[(l4 & 1) * 2] = cvt_h2(fmul2(s2, a01));
-                    o[(l4 & 1) * 2 + 1] = cvt_h2(fmul2(s2, a23));
-                }
+            for (int i = 0; i < 4; i++) {  // 4 words of 4 weights
+                const int l4 = sub * 4 + i;
+                const uint32_t L = Lw[l4];
+                const uint32_t lo = (tq >= 2) ? ((L >> 4) & 0x0F0F0F0Fu) : (L & 0x0F0F0F0Fu);
+                const uint32_t q = lo | (((Hw[l4] >> (2 * tq)) & 0x03030303u) << 4);
+                const u64 a01 = fsub2(bytes01_magic(q, 0x7440u, 0x7441u), mg);
+                const u64 a23 = fsub2(bytes01_magic(q, 0x7442u, 0x7443u), mg);
+                uint32_t *o = reinterpret_cast<uint32_t *>(&out[l4 / 2]);
+                o[(l4 & 1) * 2] = cvt_h2(fmul2(s2, a01));
+                o[(l4 & 1) * 2 + 1] = cvt_h2(fmul2(s2, a23));
             }
         }
     } else if (T == CUQ_F16) {
 #pragma unroll
-        for (int c = 0; c < 8; c++) out[c] = chunk(c);
+        for (int c = 0; c < 4; c++) out[c] = chunk(4 * half + c);
     } else if (T == CUQ_BF16) {  // Gguf.readF16 of a bf16 tensor: RN16(f32(bf16))
 #pragma unroll
-        for (int c = 0; c < 8; c++) {
-            const uint4 v = chunk(c);
+        for (int c = 0; c < 4; c++) {
+            const uint4 v = chunk(4 * half + c);
             const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
             uint32_t o[4];
 #pragma unroll
@@ -376,47 +379,41 @@ __device__ __forceinline__ void dequant_smem(const uint8_t *slot, int t, uint32_
                 o[i] = h2u(__floats2half2_rn(__uint_as_float(wv[i] << 16), __uint_as_float(wv[i] & 0xFFFF0000u)));
             out[c] = make_uint4(o[0], o[1], o[2], o[3]);
         }
-    } else {  // legacy 32-blocks (gguf.zig:763-825), scalar fp32 as the reference
+    } else {  // legacy 32-blocks (gguf.zig:763-825), scalar fp32 as the reference; block = half
         constexpr int SE = (T == CUQ_Q4_1 || T == CUQ_Q5_1) ? 4 : 2;
-        const uint4 q0 = chunk(0), q1 = chunk(1);
-        const uint8_t *b = reinterpret_cast<const uint8_t *>(&q0);
-        const uint8_t *b1 = reinterpret_cast<const uint8_t *>(&q1);
-        __half vals[64];
+        const uint4 qv = chunk(half);
+        const uint8_t *bb = reinterpret_cast<const uint8_t *>(&qv);
+        float dd, m = 0.f;
+        if (SE == 2) {
+            dd = __half2float(reinterpret_cast<const __half *>(side)[half * 128 + srow]);
+        } else {
+            const __half2 dm = reinterpret_cast<const __half2 *>(side)[half * 128 + srow];
+            dd = __low2float(dm);
+            m = __high2float(dm);
+        }
+        const uint32_t qh = (T == CUQ_Q5_0 || T == CUQ_Q5_1)
+                                ? reinterpret_cast<const uint32_t *>(side + 2 * 128 * SE + half * 512)[srow]
+                                : 0u;
+        __half vals[32];
 #pragma unroll
-        for (int blk = 0; blk < 2; blk++) {
-            const uint8_t *bb = blk ? b1 : b;
-            float dd, m = 0.f;
-            if (SE == 2) {
-                dd = __half2float(reinterpret_cast<const __half *>(side)[blk * 128 + srow]);
+        for (int j = 0; j < 32; j++) {
+            const int byte = bb[j & 15];
+            const int nib = j < 16 ? (byte & 0xF) : (byte >> 4);
+            float val;
+            if (T == CUQ_Q4_0) {
+                val = __fmul_rn((float)(nib - 8), dd);
+            } else if (T == CUQ_Q4_1) {
+                val = __fadd_rn(__fmul_rn((float)nib, dd), m);
             } else {
-                const __half2 dm = reinterpret_cast<const __half2 *>(side)[blk * 128 + srow];
-                dd = __low2float(dm);
-                m = __high2float(dm);
+                const int hb = j < 16 ? (int)(((qh >> j) << 4) & 0x10u) : (int)((qh >> (j - 16 + 12)) & 0x10u);
+                const float x = (float)((nib | hb) - (T == CUQ_Q5_0 ? 16 : 0));
+                val = __fadd_rn(__fmul_rn(x, dd), m);
             }
-            const uint32_t qh = (T == CUQ_Q5_0 || T == CUQ_Q5_1)
-                                    ? reinterpret_cast<const uint32_t *>(side + 2 * 128 * SE + blk * 512)[srow]
-                                    : 0u;
-#pragma unroll
-            for (int j = 0; j < 32; j++) {
-                const int byte = bb[j & 15];
-                const int nib = j < 16 ? (byte & 0xF) : (byte >> 4);
-                float val;
-                if (T == CUQ_Q4_0) {
-                    val = __fmul_rn((float)(nib - 8), dd);
-                } else if (T == CUQ_Q4_1) {
-                    val = __fadd_rn(__fmul_rn((float)nib, dd), m);
-                } else {
-                    const int hb = j < 16 ? (int)(((qh >> j) << 4) & 0x10u) : (int)((qh >> (j - 16 + 12)) & 0x10u);
-                    const float x = (float)((nib | hb) - (T == CUQ_Q5_0 ? 16 : 0));
-                    val = __fadd_rn(__fmul_rn(x, dd), m);
-                }
-                vals[blk * 32 + j] = __float2half_rn(val);
-            }
+            vals[j] = __float2half_rn(val);
         }
 #pragma unroll
-        for (int c = 0; c < 8; c++) out[c] = reinterpret_cast<const uint4 *>(vals)[c];
+        for (int c = 0; c < 4; c++) out[c] = reinterpret_cast<const uint4 *>(vals)[c];
     }
-    (void)dual;
 }
 
 // ---------------------------------------------------------------- TMA ----
@@ -445,44 +442,60 @@ struct __align__(64) QgArgs {
     int *err;                  // set to 1 when a wait timed out
 };
 
-// Warps 0-3: weight producers (raw prefetch + dequant into the A stage), then
-// the epilogue; warp 4: TMEM allocation and the MMA issuer (lane 0); warp 5
-// lane 0: TMA loads of the x hi / lo tiles into the B stage.
+// Persistent CTAs (one per SM), tiles (128 weight rows x 128 tokens) taken
+// round-robin, row tiles fastest so neighbouring CTAs share the x tile in L2.
+// Warps 0-7: weight producers (raw prefetch + dequant into the A stage; each
+// warp owns 16 A rows, two threads per row); warp 8: TMEM allocation and the MMA
+// issuer (lane 0); warp 9 lane 0: TMA loads of the x hi / lo tiles into the B
+// stage; warps 10-13: epilogue.  Two TMEM
+// accumulators (2 x 256 columns) let the epilogue of one tile overlap the
+// main loop of the next.  The stage and raw rings run continuously across tiles.
+constexpr int NTHREADS = 448;  // 8 producer warps, MMA, TMA, 4 epilogue warps
+
 template <int T, int EPI>
-__global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const __grid_constant__ QgArgs p) {
+__global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_constant__ QgArgs p) {
     using G = Geo<T>;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *raw = smem + STAGES * STAGE_BYTES;
     uint64_t *full = reinterpret_cast<uint64_t *>(raw + G::RAWD * G::SLOT);
     uint64_t *empty = full + STAGES;
-    uint64_t *done = empty + STAGES;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(done + 1);
+    uint64_t *acc_full = empty + STAGES;    // [2] MMA -> epilogue
+    uint64_t *acc_empty = acc_full + 2;     // [2] epilogue -> MMA
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_empty + 2);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
     volatile int *stop = abort_flag + 1;  // [2] producers' per-step snapshot of abort_flag
-    // SILU epilogue: up values handed to the gate rows, in stage 0 (free once every MMA completed)
-    float(*xchg)[33] = reinterpret_cast<float(*)[33]>(smem);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
     const uint32_t rows = p.w.rows, cols = p.w.cols;
     const uint32_t nkb = cols / BK;
-    const uint32_t row0 = blockIdx.x * (DUAL ? BM / 2 : BM);
-    const uint32_t tok0 = blockIdx.y * BN;
+    const uint32_t rows_per_tile = DUAL ? BM / 2 : BM;
+    const uint32_t mtiles = (rows + rows_per_tile - 1) / rows_per_tile, ntiles = (p.n + BN - 1) / BN;
+    const uint32_t ntile_total = mtiles * ntiles;
+    const uint32_t my_tiles = blockIdx.x < ntile_total ? (ntile_total - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+    auto tile_of = [&](uint32_t j, uint32_t &row0, uint32_t &tok0) {
+        const uint32_t i = blockIdx.x + j * gridDim.x;
+        row0 = (i % mtiles) * rows_per_tile;
+        tok0 = (i / mtiles) * BN;
+    };
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 129);  // 128 producer arrivals + the TMA thread's expect_tx
+            mbar_init(&full[s], 257);  // 256 producer arrivals + the TMA thread's expect_tx
             mbar_init(&empty[s], 1);
         }
-        mbar_init(done, 1);
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&acc_full[b], 1);
+            mbar_init(&acc_empty[b], 128);
+        }
         *abort_flag = 0;
         stop[0] = stop[1] = 0;
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
-    if (warp == 4) {  // tensor memory for the 128 x 256 fp32 accumulator
+    if (warp == 8) {  // tensor memory: two 128 x 256 fp32 accumulators
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(TMEM_COLS)
+                     "r"(2 * TMEM_COLS)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -490,70 +503,125 @@ __global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const __grid_constant_
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    const uint32_t total = my_tiles * nkb;  // steps this CTA runs
 
-    if (warp < 4) {
+    if (warp < 8) {
         // ---------------------------------------------------- producers
-        const int t = threadIdx.x;
-        for (uint32_t i = 0; i + 1 < (uint32_t)G::RAWD && i < nkb; i++) {
-            raw_issue<T>(p.w, p.w2, DUAL, row0, i, raw + i * G::SLOT, t);
+        const int pw = warp, ar = 16 * pw + (lane >> 1), half = lane & 1;
+        auto issue = [&](uint32_t gi) {
+            uint32_t row0, tok0;
+            tile_of(gi / nkb, row0, tok0);
+            raw_issue<T>(p.w, p.w2, DUAL, row0, gi % nkb, raw + (gi % G::RAWD) * G::SLOT, pw, lane);
+        };
+        for (uint32_t i = 0; i + 1 < (uint32_t)G::RAWD; i++) {
+            if (i < total) issue(i);
             cp_async_commit();
         }
-        for (uint32_t i = nkb; i + 1 < (uint32_t)G::RAWD; i++) cp_async_commit();  // keep the group count uniform
-        for (uint32_t kb = 0; kb < nkb; kb++) {
-            const int s = kb % STAGES;
-            if (t == 0) {
-                if (kb >= (uint32_t)STAGES) mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag);
-                stop[kb & 1] = *abort_flag;
+        for (uint32_t gs = 0; gs < total; gs++) {
+            const int s = gs % STAGES;
+            int stopw = 0;
+            if (lane == 0) {
+                if (gs >= (uint32_t)STAGES) mbar_wait(&empty[s], ((gs / STAGES) - 1) & 1, abort_flag);
+                stopw = *abort_flag;
             }
+            stopw = __shfl_sync(0xffffffffu, stopw, 0);
             cp_async_wait<G::RAWD - 2>();
-            asm volatile("bar.sync 1, 128;" ::: "memory");  // raw step kb landed; slot of kb-1 is free
-            if (stop[kb & 1]) break;
-            if (kb + G::RAWD - 1 < nkb)
-                raw_issue<T>(p.w, p.w2, DUAL, row0, kb + G::RAWD - 1, raw + ((kb + G::RAWD - 1) % G::RAWD) * G::SLOT, t);
+            __syncwarp();  // the warp's raw step gs landed; its slot of gs-1 is free
+            if (stopw) break;
+            if (gs + G::RAWD - 1 < total) issue(gs + G::RAWD - 1);
             cp_async_commit();
-            uint4 vals[8];
-            dequant_smem<T>(raw + (kb % G::RAWD) * G::SLOT, t, kb, DUAL, vals);
+            uint4 vals[4];
+            dequant_half<T>(raw + (gs % G::RAWD) * G::SLOT, ar, half, gs % nkb, DUAL, vals);
             uint8_t *A = smem + s * STAGE_BYTES;
 #pragma unroll
-            for (int c = 0; c < 8; c++) *reinterpret_cast<uint4 *>(A + t * 128 + ((c ^ (t & 7)) * 16)) = vals[c];
+            for (int c = 0; c < 4; c++) {
+                const int cc = 4 * half + c;
+                *reinterpret_cast<uint4 *>(A + ar * 128 + ((cc ^ (ar & 7)) * 16)) = vals[c];
+            }
             fence_async_smem();
             mbar_arrive(&full[s]);
         }
         cp_async_wait<0>();
-        // ---------------------------------------------------- epilogue
-        mbar_wait(done, 0, abort_flag);
-        asm volatile("bar.sync 1, 128;" ::: "memory");  // all producers past the wait: abort_flag is final
-        const bool ok = *abort_flag == 0;
-        tc_fence_after();
-        if (ok) {
-            const uint32_t lane_base = (uint32_t)warp * 32;
+    } else if (warp == 8) {
+        if (lane == 0) {
+            // ------------------------------------------------ MMA issuer
+            uint32_t gs = 0;
+            bool ok = true;
+            for (uint32_t j = 0; j < my_tiles && ok; j++) {
+                const uint32_t ab = j & 1;
+                if (j >= 2 && !mbar_wait(&acc_empty[ab], ((j >> 1) - 1) & 1, abort_flag)) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + ab * TMEM_COLS;
+                for (uint32_t kb = 0; kb < nkb; kb++, gs++) {
+                    const int s = gs % STAGES;
+                    if (!mbar_wait(&full[s], (gs / STAGES) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
+#pragma unroll
+                    for (int k = 0; k < BK / 16; k++)
+                        umma_f16(acc, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) ? 1u : 0u);
+                    umma_commit(&empty[s]);  // frees the stage when these MMAs complete
+                }
+                if (ok) umma_commit(&acc_full[ab]);
+            }
+        }
+    } else if (warp == 9) {
+        if (lane == 0) {
+            // ------------------------------------------------ TMA: x hi / lo
+            uint32_t gs = 0;
+            for (uint32_t j = 0; j < my_tiles; j++) {
+                uint32_t row0, tok0;
+                tile_of(j, row0, tok0);
+                bool ok = true;
+                for (uint32_t kb = 0; kb < nkb; kb++, gs++) {
+                    const int s = gs % STAGES;
+                    if (gs >= (uint32_t)STAGES && !mbar_wait(&empty[s], ((gs / STAGES) - 1) & 1, abort_flag)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t b = smem_u32(smem + s * STAGE_BYTES + A_BYTES);
+                    mbar_expect_tx(&full[s], B_BYTES);
+                    tma_load_2d(b, &p.mh, (int)(kb * BK), (int)tok0, &full[s]);
+                    tma_load_2d(b + B_BYTES / 2, &p.ml, (int)(kb * BK), (int)tok0, &full[s]);
+                }
+                if (!ok) break;
+            }
+        }
+    } else {
+        // ---------------------------------------------------- epilogue (warps 10-13)
+        const uint32_t quarter = (uint32_t)(warp & 3);  // TMEM lanes this warp may read
+        const uint32_t trow = quarter * 32 + lane;      // row of the tile = TMEM lane
+        for (uint32_t j = 0; j < my_tiles; j++) {
+            const uint32_t ab = j & 1;
+            if (!mbar_wait(&acc_full[ab], (j >> 1) & 1, abort_flag)) break;
+            tc_fence_after();
+            uint32_t row0, tok0;
+            tile_of(j, row0, tok0);
+            const uint32_t acc = tmem + ab * TMEM_COLS + ((quarter * 32) << 16);
 #pragma unroll 1
             for (int ch = 0; ch < BN / 32; ch++) {
                 float hi[32], lo[32];
-                tmem_ld32(tmem + (lane_base << 16) + ch * 32, hi);
-                tmem_ld32(tmem + (lane_base << 16) + BN + ch * 32, lo);
-                const uint32_t trow = lane_base + lane;  // row within the tile
+                tmem_ld32(acc + ch * 32, hi);
+                tmem_ld32(acc + BN + ch * 32, lo);
                 if (DUAL) {
-                    // rows 64..127 hold "up": hand them to the gate threads
-                    if (trow >= 64)
+                    // even lanes hold gate row row0 + trow/2, odd lanes the same row of up
+                    const uint32_t r = row0 + (trow >> 1);
 #pragma unroll
-                        for (int i = 0; i < 32; i++) xchg[trow - 64][i] = hi[i] + lo[i];
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
-                    if (trow < 64) {
-                        const uint32_t r = row0 + trow;
-#pragma unroll
-                        for (int i = 0; i < 32; i++) {
-                            const uint32_t tok = tok0 + ch * 32 + i;
-                            if (tok >= p.n || r >= rows) continue;
-                            float g = hi[i] + lo[i], u = xchg[trow][i];
-                            float sg = 1.0f / (1.0f + expf(-g));  // cpu.siluMul (cpu.zig:65-70)
-                            float act = (g * sg) * u;
-                            __half ah = __float2half_rn(act);
-                            p.oh[(size_t)tok * rows + r] = ah;
-                            p.ol[(size_t)tok * rows + r] = __float2half_rn(act - __half2float(ah));
-                        }
+                    for (int i = 0; i < 32; i++) {
+                        const float mine = hi[i] + lo[i];
+                        const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
+                        const uint32_t tok = tok0 + ch * 32 + i;
+                        if ((trow & 1) || tok >= p.n || r >= rows) continue;
+                        const float g = mine, u = other;
+                        const float sg = 1.0f / (1.0f + expf(-g));  // cpu.siluMul (cpu.zig:65-70)
+                        const float act = (g * sg) * u;
+                        const __half ah = __float2half_rn(act);
+                        p.oh[(size_t)tok * rows + r] = ah;
+                        p.ol[(size_t)tok * rows + r] = __float2half_rn(act - __half2float(ah));
                     }
-                    asm volatile("bar.sync 1, 128;" ::: "memory");
                 } else {
                     const uint32_t r = row0 + trow;
                     if (r < rows) {
@@ -573,44 +641,17 @@ __global__ void __launch_bounds__(192, 1) qgemm_tc_kernel(const __grid_constant_
                     }
                 }
             }
-        }
-    } else if (warp == 4) {
-        if (lane == 0) {
-            // ------------------------------------------------ MMA issuer
-            bool ok = true;
-            for (uint32_t kb = 0; kb < nkb; kb++) {
-                const int s = kb % STAGES;
-                if (!mbar_wait(&full[s], (kb / STAGES) & 1, abort_flag)) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
-#pragma unroll
-                for (int k = 0; k < BK / 16; k++)
-                    umma_f16(tmem, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) ? 1u : 0u);
-                umma_commit(&empty[s]);  // frees the stage when these MMAs complete
-            }
-            if (ok) umma_commit(done);
-            else mbar_arrive(done);      // let the epilogue stop waiting
-        }
-    } else if (lane == 0) {
-        // ---------------------------------------------------- TMA: x hi / lo
-        for (uint32_t kb = 0; kb < nkb; kb++) {
-            const int s = kb % STAGES;
-            if (kb >= (uint32_t)STAGES && !mbar_wait(&empty[s], ((kb / STAGES) - 1) & 1, abort_flag)) break;
-            const uint32_t b = smem_u32(smem + s * STAGE_BYTES + A_BYTES);
-            mbar_expect_tx(&full[s], B_BYTES);
-            tma_load_2d(b, &p.mh, (int)(kb * BK), (int)tok0, &full[s]);
-            tma_load_2d(b + B_BYTES / 2, &p.ml, (int)(kb * BK), (int)tok0, &full[s]);
+            tc_fence_before();
+            mbar_arrive(&acc_empty[ab]);  // this accumulator may be overwritten
         }
     }
     tc_fence_before();
     __syncthreads();
     if (*abort_flag && threadIdx.x == 0) *p.err = 1;
-    if (warp == 4) {
+    if (warp == 8) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * TMEM_COLS)
+                     : "memory");
     }
 }
 
@@ -626,9 +667,10 @@ int launch_tq(const QgArgs &a, uint32_t rows, uint32_t n, cudaStream_t s) {
         }
         attr_set = true;
     }
-    const uint32_t rows_per_cta = EPI == EPI_SILU_XQ ? BM / 2 : BM;
-    dim3 grid((rows + rows_per_cta - 1) / rows_per_cta, (n + BN - 1) / BN);
-    kern<<<grid, 192, Geo<T>::SMEM, s>>>(a);
+    const uint32_t rows_per_tile = EPI == EPI_SILU_XQ ? BM / 2 : BM;
+    const uint32_t tiles = ((rows + rows_per_tile - 1) / rows_per_tile) * ((n + BN - 1) / BN);
+    const uint32_t ctas = tiles < (uint32_t)sm_count_current() ? tiles : (uint32_t)sm_count_current();
+    kern<<<ctas, NTHREADS, Geo<T>::SMEM, s>>>(a);
     CUQ_CUDA_TRY(cudaGetLastError());
     return CUQ_OK;
 }

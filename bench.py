@@ -291,7 +291,7 @@ def run_ours(args, world, rank, local):
         dist.all_gather_object(out, h)
         return out
 
-    eng = E.Engine.from_synth(model, max_seq=max_seq, device=local, max_chunk=512,
+    eng = E.Engine.from_synth(model, max_seq=max_seq, device=local, max_chunk=2048,
                               tp_rank=rank if tp else 0, tp_size=world if tp else 1, exchange=exchange)
     stream_ptr = eng.stream
     stream = torch.cuda.ExternalStream(stream_ptr)
