@@ -25,11 +25,15 @@ int sm_count_current();
 
 namespace {
 
-constexpr int BM = 128, BN = 128, BK = 64, STAGES = 4;
-constexpr int A_BYTES = BM * BK * 2;        // 16 KB
+// Tile: 128 weight rows x 256 tokens.  Weights are dequantised 64 columns at a
+// time (RAW_K, one "raw step"), and fed to the MMA in stages of 32 columns
+// (BK): A = 128 x 32 fp16 and B = 256 x 32 x (hi, lo) fp16 in the 64-byte
+// swizzled K-major layout.  hi and lo accumulate into the same TMEM columns.
+constexpr int BM = 128, BN = 256, BK = 32, RAW_K = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;        // 8 KB
 constexpr int B_BYTES = 2 * BN * BK * 2;    // 32 KB (hi + lo)
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 256;         // one accumulator: 256 token columns
 constexpr unsigned long long WAIT_NS = 2000000000ull;  // a stage wait gives up after 2 s
 constexpr uint32_t SUSPEND_NS = 20000;                   // try_wait sleeps up to 20 us per poll
 
@@ -78,16 +82,18 @@ __device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.a
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
-// K-major, 128-byte swizzle, 8-row atoms of 1024 B stacked along M/N.
-__device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr) {
+// K-major, 64-byte swizzle: 8-row atoms of 512 B (rows of 64 B, 16-byte chunk c
+// of row r at chunk c ^ ((r >> 1) & 3)) stacked along M/N.
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t saddr) {
     uint64_t d = 0;
     d |= (uint64_t)((saddr >> 4) & 0x3FFFu);   // start address (16 B units)
     d |= (uint64_t)1u << 16;                   // leading byte offset (unused by swizzled K-major)
-    d |= (uint64_t)(1024u >> 4) << 32;         // stride byte offset: next 8-row group
+    d |= (uint64_t)(512u >> 4) << 32;          // stride byte offset: next 8-row group
     d |= (uint64_t)1u << 46;                   // descriptor version (sm_100)
-    d |= (uint64_t)2u << 61;                   // SWIZZLE_128B
+    d |= (uint64_t)4u << 61;                   // SWIZZLE_64B
     return d;
 }
+__device__ __forceinline__ int sw64_chunk(int r, int c) { return c ^ ((r >> 1) & 3); }
 
 // kind::f16 instruction descriptor: D f32, A/B f16, both K-major, M=128, N=256.
 constexpr uint32_t IDESC = (1u << 4) | ((256u >> 3) << 17) | ((128u >> 4) << 24);
@@ -432,7 +438,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 // ------------------------------------------------------------- kernel ----
 
 struct __align__(64) QgArgs {
-    CUtensorMap mh, ml;        // x hi / lo [n][cols] fp16, box 64 x 128, 128-byte swizzle
+    CUtensorMap mh, ml;        // x hi / lo [n][cols] fp16, box 32 x 256, 64-byte swizzle
     WPlanes w, w2;             // w2: the up matrix of a gate|up pair
     uint32_t n;
     float *y;                  // [n][ldy] fp32 output (STORE / ADD)
@@ -469,7 +475,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
     const uint32_t rows = p.w.rows, cols = p.w.cols;
-    const uint32_t nkb = cols / BK;
+    const uint32_t nkb = cols / RAW_K;  // raw steps per tile; 2 MMA stages each
     const uint32_t rows_per_tile = DUAL ? BM / 2 : BM;
     const uint32_t mtiles = (rows + rows_per_tile - 1) / rows_per_tile, ntiles = (p.n + BN - 1) / BN;
     const uint32_t ntile_total = mtiles * ntiles;
@@ -482,7 +488,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; s++) {
-            mbar_init(&full[s], 257);  // 256 producer arrivals + the TMA thread's expect_tx
+            mbar_init(&full[s], 129);  // 128 producer arrivals (one half each) + the TMA thread's expect_tx
             mbar_init(&empty[s], 1);
         }
         for (int b = 0; b < 2; b++) {
@@ -518,13 +524,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
             cp_async_commit();
         }
         for (uint32_t gs = 0; gs < total; gs++) {
-            const int s = gs % STAGES;
+            // raw step gs feeds MMA stages 2gs (columns 0-31, half 0) and 2gs+1 (half 1)
+            const uint32_t sg = 2 * gs + half;
+            const int s = sg % STAGES;
             int stopw = 0;
-            if (lane == 0) {
-                if (gs >= (uint32_t)STAGES) mbar_wait(&empty[s], ((gs / STAGES) - 1) & 1, abort_flag);
+            if (lane < 2) {  // lane 0 waits for the half-0 stage, lane 1 for the half-1 stage
+                if (sg >= (uint32_t)STAGES) mbar_wait(&empty[s], ((sg / STAGES) - 1) & 1, abort_flag);
                 stopw = *abort_flag;
             }
-            stopw = __shfl_sync(0xffffffffu, stopw, 0);
+            stopw = __shfl_sync(0xffffffffu, stopw, 0) | __shfl_sync(0xffffffffu, stopw, 1);
             cp_async_wait<G::RAWD - 2>();
             __syncwarp();  // the warp's raw step gs landed; its slot of gs-1 is free
             if (stopw) break;
@@ -534,10 +542,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
             dequant_half<T>(raw + (gs % G::RAWD) * G::SLOT, ar, half, gs % nkb, DUAL, vals);
             uint8_t *A = smem + s * STAGE_BYTES;
 #pragma unroll
-            for (int c = 0; c < 4; c++) {
-                const int cc = 4 * half + c;
-                *reinterpret_cast<uint4 *>(A + ar * 128 + ((cc ^ (ar & 7)) * 16)) = vals[c];
-            }
+            for (int c = 0; c < 4; c++) *reinterpret_cast<uint4 *>(A + ar * 64 + sw64_chunk(ar, c) * 16) = vals[c];
             fence_async_smem();
             mbar_arrive(&full[s]);
         }
@@ -552,7 +557,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
                 if (j >= 2 && !mbar_wait(&acc_empty[ab], ((j >> 1) - 1) & 1, abort_flag)) break;
                 tc_fence_after();
                 const uint32_t acc = tmem + ab * TMEM_COLS;
-                for (uint32_t kb = 0; kb < nkb; kb++, gs++) {
+                for (uint32_t ks = 0; ks < 2 * nkb; ks++, gs++) {
                     const int s = gs % STAGES;
                     if (!mbar_wait(&full[s], (gs / STAGES) & 1, abort_flag)) {
                         ok = false;
@@ -561,8 +566,11 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
                     tc_fence_after();
                     const uint32_t a = smem_u32(smem + s * STAGE_BYTES), b = a + A_BYTES;
 #pragma unroll
-                    for (int k = 0; k < BK / 16; k++)
-                        umma_f16(acc, sdesc_sw128(a + 32 * k), sdesc_sw128(b + 32 * k), (kb | k) ? 1u : 0u);
+                    for (int k = 0; k < BK / 16; k++) {
+                        const uint64_t ad = sdesc_sw64(a + 32 * k);
+                        umma_f16(acc, ad, sdesc_sw64(b + 32 * k), (ks | k) ? 1u : 0u);        // A x_hi
+                        umma_f16(acc, ad, sdesc_sw64(b + B_BYTES / 2 + 32 * k), 1u);          // + A x_lo
+                    }
                     umma_commit(&empty[s]);  // frees the stage when these MMAs complete
                 }
                 if (ok) umma_commit(&acc_full[ab]);
@@ -576,7 +584,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
                 uint32_t row0, tok0;
                 tile_of(j, row0, tok0);
                 bool ok = true;
-                for (uint32_t kb = 0; kb < nkb; kb++, gs++) {
+                for (uint32_t ks = 0; ks < 2 * nkb; ks++, gs++) {
                     const int s = gs % STAGES;
                     if (gs >= (uint32_t)STAGES && !mbar_wait(&empty[s], ((gs / STAGES) - 1) & 1, abort_flag)) {
                         ok = false;
@@ -584,8 +592,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
                     }
                     const uint32_t b = smem_u32(smem + s * STAGE_BYTES + A_BYTES);
                     mbar_expect_tx(&full[s], B_BYTES);
-                    tma_load_2d(b, &p.mh, (int)(kb * BK), (int)tok0, &full[s]);
-                    tma_load_2d(b + B_BYTES / 2, &p.ml, (int)(kb * BK), (int)tok0, &full[s]);
+                    tma_load_2d(b, &p.mh, (int)(ks * BK), (int)tok0, &full[s]);
+                    tma_load_2d(b + B_BYTES / 2, &p.ml, (int)(ks * BK), (int)tok0, &full[s]);
                 }
                 if (!ok) break;
             }
@@ -603,15 +611,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
             const uint32_t acc = tmem + ab * TMEM_COLS + ((quarter * 32) << 16);
 #pragma unroll 1
             for (int ch = 0; ch < BN / 32; ch++) {
-                float hi[32], lo[32];
+                float hi[32];
                 tmem_ld32(acc + ch * 32, hi);
-                tmem_ld32(acc + BN + ch * 32, lo);
                 if (DUAL) {
                     // even lanes hold gate row row0 + trow/2, odd lanes the same row of up
                     const uint32_t r = row0 + (trow >> 1);
 #pragma unroll
                     for (int i = 0; i < 32; i++) {
-                        const float mine = hi[i] + lo[i];
+                        const float mine = hi[i];
                         const float other = __shfl_xor_sync(0xffffffffu, mine, 1);
                         const uint32_t tok = tok0 + ch * 32 + i;
                         if ((trow & 1) || tok >= p.n || r >= rows) continue;
@@ -630,7 +637,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) qgemm_tc_kernel(const __grid_cons
                         for (int i = 0; i < 32; i++) {
                             const uint32_t tok = tok0 + ch * 32 + i;
                             if (tok >= p.n) continue;
-                            float v = hi[i] + lo[i];
+                            float v = hi[i];
                             if (p.bias) v = v + b;
                             float *dst = p.y + (size_t)tok * p.ldy + r;
                             if (EPI == EPI_ADD)
@@ -693,7 +700,7 @@ int dispatch(int type, const QgArgs &a, uint32_t rows, uint32_t n, cudaStream_t 
 }
 
 // Tensor map of an x part [n][cols] fp16 (row stride cols*2 bytes): boxes of
-// 64 columns x 128 tokens in the 128-byte swizzle the MMA descriptors expect;
+// 32 columns x 256 tokens in the 64-byte swizzle the MMA descriptors expect;
 // tokens past n read as zero.
 int make_x_map(CUtensorMap *m, const __half *base, uint32_t n, uint32_t cols) {
     if ((reinterpret_cast<uintptr_t>(base) & 15) || (cols * 2) % 16) {
@@ -702,11 +709,11 @@ int make_x_map(CUtensorMap *m, const __half *base, uint32_t n, uint32_t cols) {
     }
     cuuint64_t dims[2] = {cols, n};
     cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-    cuuint32_t box[2] = {BK, BN};
+    cuuint32_t box[2] = {BK, BN};  // 32 columns (64 bytes) x 256 tokens
     cuuint32_t estr[2] = {1, 1};
     CUresult r = cuTensorMapEncodeTiled(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims,
                                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
         set_error("qgemm: cuTensorMapEncodeTiled failed (%d)", (int)r);
@@ -734,8 +741,8 @@ int launch_qgemm(const QgemmArgs &g, int epi, cudaStream_t s) {
         set_error("UnsupportedType: no tensor-core GEMM for ggml type %d", w.type);
         return CUQ_EUNSUPPORTED;
     }
-    if (w.cols % BK) {
-        set_error("qgemm: cols (%u) must be a multiple of %d", w.cols, BK);
+    if (w.cols % RAW_K) {
+        set_error("qgemm: cols (%u) must be a multiple of %d", w.cols, RAW_K);
         return CUQ_EINVAL;
     }
     if (epi == EPI_SILU_XQ && (!g.w2 || g.w2->type != w.type || g.w2->rows != w.rows || g.w2->cols != w.cols)) {

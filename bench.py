@@ -28,7 +28,7 @@ is that sequence's tokens/s); c2-c4 do not shard and run one replica per rank
 + main.zig refForward; the Zig reference cannot be built here) on all host
 cores, rank 0 only, on a bounded sample of the same workload.
 `--profile gemv`: 6 launches of the roofline GEMV only; `--profile qgemm`: 4
-prefill GEMMs of the config's first ffn_gate on 512 tokens (for ncu captures).
+prefill GEMMs of the config's first ffn_gate on 2048 tokens (for ncu captures).
 """
 import argparse
 import ctypes
@@ -400,16 +400,16 @@ def profile_case(args):
         ttype, raw, rows, cols = head_shard(model, C, 0, 1)
         gemv_roofline(ttype, raw, rows, cols, s.cuda_stream, peaks()[0], name, reps=0)
     elif args.profile == "qgemm":
-        # the prefill GEMM of the config's first ffn_gate on a 512-token chunk, 4 launches
+        # the prefill GEMM of the config's first ffn_gate on a 2048-token chunk, 4 launches
         L = rt.load()
         t = model.tensor("blk.0.ffn_gate.weight")
         raw = np.frombuffer(t.data, dtype=np.uint8)
         h = L.cuq_weight_create(t.ggml_type, raw.ctypes.data_as(ctypes.c_void_p), raw.size, t.rows, t.cols)
         assert h, rt.last_error()
-        x = torch.randn(512, t.cols, device="cuda")
-        y = torch.empty(512, t.rows, device="cuda")
+        x = torch.randn(2048, t.cols, device="cuda")
+        y = torch.empty(2048, t.rows, device="cuda")
         for _ in range(4):
-            rt.check(L.cuq_gemm(h, ctypes.c_void_p(x.data_ptr()), 512, ctypes.c_void_p(y.data_ptr()), None))
+            rt.check(L.cuq_gemm(h, ctypes.c_void_p(x.data_ptr()), 2048, ctypes.c_void_p(y.data_ptr()), None))
         L.cuq_weight_free(h)
     torch.cuda.synchronize()
 
