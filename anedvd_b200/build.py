@@ -57,7 +57,7 @@ def build(force=False, verbose=False, jobs=None):
             _drain(procs)
     _drain(procs)
     if force or not os.path.exists(LIB) or any(os.path.getmtime(o) > os.path.getmtime(LIB) for o in objs):
-        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs + ["-lcuda"]
+        cmd = [NVCC] + ARCH + ["-shared", "-o", LIB] + objs
         r = subprocess.run(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)
         if r.returncode:
             raise RuntimeError("link failed:\n" + r.stdout)

@@ -1,0 +1,586 @@
+// gemv_impl.cuh -- the batch-1 quantized GEMV's per-type register decoders and
+// its CTA body, shared by gemv.cu (one kernel per projection) and the
+// persistent decode kernel.
+#pragma once
+
+#include "common.cuh"
+#include "tp.cuh"
+
+namespace cuq {
+
+namespace {
+
+struct W {
+    const uint8_t *q, *q2, *s, *s2;  // plane pointers (see common.cuh)
+    uint32_t rows, cols;
+};
+
+W wview(const Planes &p) {
+    W w;
+    w.q = p.base + p.off_q;
+    w.q2 = p.off_q2 == SIZE_MAX ? nullptr : p.base + p.off_q2;
+    w.s = p.off_s == SIZE_MAX ? nullptr : p.base + p.off_s;
+    w.s2 = p.off_s2 == SIZE_MAX ? nullptr : p.base + p.off_s2;
+    w.rows = p.rows;
+    w.cols = p.cols;
+    return w;
+}
+
+__device__ __forceinline__ uint4 ldg_stream(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
+__device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
+
+__device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+        "{%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// half2 with 0x6400 exponent over the low bits of both 16-bit lanes: 1024 + field.
+__device__ __forceinline__ uint32_t magic(uint32_t v, uint32_t mask) { return (v & mask) | 0x64006400u; }
+
+// ------------------------------------------------------------- per type ---
+// Each type provides SPAN (columns per lane-row per iteration x 4 lanes),
+// KSTEPS (MMA k-steps per iteration), load() of one iteration's bytes for rows
+// r0 and r0+8, frag() giving the A registers of k-step s, and koff() giving
+// the first column of the 4-column group the lane feeds at k-step s.
+
+struct TQ8_0 {
+    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 2;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 q[2]; __half2 d[2]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        uint32_t k = it * SPAN + tig * 16;
+        if (k < w.cols) {
+            R.q[0] = ldg_stream(w.q + (size_t)r0 * w.cols + k);
+            R.q[1] = ldg_stream(w.q + (size_t)(r0 + 8) * w.cols + k);
+            const __half *d = reinterpret_cast<const __half *>(w.s) + (size_t)(k >> 5) * w.rows;
+            R.d[0] = __half2half2(d[r0]);
+            R.d[1] = __half2half2(d[r0 + 8]);
+        } else {
+            R.q[0] = R.q[1] = make_uint4(0x80808080u, 0x80808080u, 0x80808080u, 0x80808080u);  // q = 0
+            R.d[0] = R.d[1] = __float2half2_rn(0.f);
+        }
+    }
+    __device__ static uint32_t word(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
+        const __half2 off = __float2half2_rn(1152.f);
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t u = word(R.q[rr], s) ^ 0x80808080u;  // int8 q -> q + 128 (unsigned byte)
+            __half2 p02 = u2h(__byte_perm(u, 0x64646464u, 0x4240u));  // 1152 + q for bytes 0, 2
+            __half2 p13 = u2h(__byte_perm(u, 0x64646464u, 0x4341u));
+            a[rr] = h2u(__hmul2(__hsub2(p02, off), R.d[rr]));        // RN16(q * d)
+            a[rr + 2] = h2u(__hmul2(__hsub2(p13, off), R.d[rr]));
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 16 + s * 4; }
+};
+
+// Legacy 32-blocks with 4-bit nibbles: one block per lane per iteration.
+template <int T>
+struct TQ4L {
+    static constexpr int SPAN = 128, KSTEPS = 8, DEPTH = 2;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 q[2]; __half2 d[2], m[2]; uint32_t qh[2]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        uint32_t k = it * SPAN + tig * 32;
+        if (k < w.cols) {
+            uint32_t b = k >> 5;
+            R.q[0] = ldg_stream(w.q + (size_t)r0 * (w.cols / 2) + b * 16);
+            R.q[1] = ldg_stream(w.q + (size_t)(r0 + 8) * (w.cols / 2) + b * 16);
+            if (T == CUQ_Q4_0 || T == CUQ_Q5_0) {
+                const __half *d = reinterpret_cast<const __half *>(w.s) + (size_t)b * w.rows;
+                R.d[0] = __half2half2(d[r0]);
+                R.d[1] = __half2half2(d[r0 + 8]);
+                R.m[0] = R.m[1] = __float2half2_rn(0.f);
+            } else {
+                const __half2 *dm = reinterpret_cast<const __half2 *>(w.s) + (size_t)b * w.rows;
+                __half2 x0 = dm[r0], x1 = dm[r0 + 8];
+                R.d[0] = __low2half2(x0);
+                R.m[0] = __high2half2(x0);
+                R.d[1] = __low2half2(x1);
+                R.m[1] = __high2half2(x1);
+            }
+            if (T == CUQ_Q5_0 || T == CUQ_Q5_1) {
+                const uint32_t *qh = reinterpret_cast<const uint32_t *>(w.q2) + (size_t)b * w.rows;
+                R.qh[0] = qh[r0];
+                R.qh[1] = qh[r0 + 8];
+            } else {
+                R.qh[0] = R.qh[1] = 0;
+            }
+        } else {
+            R.q[0] = R.q[1] = make_uint4(0, 0, 0, 0);
+            R.d[0] = R.d[1] = R.m[0] = R.m[1] = __float2half2_rn(0.f);
+            R.qh[0] = R.qh[1] = 0;
+        }
+    }
+    // k-step s: word i = s >> 1 of the block, low nibbles (s even) or high (s odd).
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
+        const int i = s >> 1;
+        const bool hi = s & 1;
+        constexpr bool five = (T == CUQ_Q5_0 || T == CUQ_Q5_1);
+        constexpr bool has_min = (T == CUQ_Q4_1 || T == CUQ_Q5_1);
+        // offset removed before scaling: 1024 + (8 | 16 for the signed types)
+        const float offv = 1024.f + (T == CUQ_Q4_0 ? 8.f : T == CUQ_Q5_0 ? 16.f : 0.f);
+        const __half2 off = __float2half2_rn(offv);
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t u = TQ8_0::word(R.q[rr], i);
+            uint32_t v02 = hi ? (u >> 4) : u, v13 = hi ? (u >> 12) : (u >> 8);
+            uint32_t p02 = magic(v02, 0x000F000Fu), p13 = magic(v13, 0x000F000Fu);
+            if (five) {
+                // 5th bits: weight j (< 16) uses qh bit j, weight 16+j uses bit 16+j.
+                uint32_t t = R.qh[rr] >> (4 * i);
+                if (!hi) {
+                    p02 |= ((t << 4) & 0x10u) | ((t << 18) & 0x100000u);
+                    p13 |= ((t << 3) & 0x10u) | ((t << 17) & 0x100000u);
+                } else {
+                    p02 |= ((t >> 12) & 0x10u) | ((t << 2) & 0x100000u);
+                    p13 |= ((t >> 13) & 0x10u) | ((t << 1) & 0x100000u);
+                }
+            }
+            __half2 x02 = __hsub2(u2h(p02), off), x13 = __hsub2(u2h(p13), off);
+            if (has_min) {
+                a[rr] = h2u(__hfma2(x02, R.d[rr], R.m[rr]));          // RN16(q*d + m)
+                a[rr + 2] = h2u(__hfma2(x13, R.d[rr], R.m[rr]));
+            } else {
+                a[rr] = h2u(__hmul2(x02, R.d[rr]));                    // RN16((q - 8|16) * d)
+                a[rr + 2] = h2u(__hmul2(x13, R.d[rr]));
+            }
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 32 + (s & 1) * 16 + (s >> 1) * 4; }
+};
+
+// Q4_K: one 256-superblock per iteration; lane tig owns the 32-byte group tig
+// (sub-blocks 2tig in the low nibbles and 2tig+1 in the high nibbles).
+// The reference weight is d1*q - m1 with d1 = d*sc, m1 = dmin*m, both exact in
+// fp32 (gguf.zig:975-992).  fma(1024+q, sc, -1024*sc) = q*sc is an integer
+// <= 945, exact in fp16; then one fma(q*sc, d, -m1h) with m1h = RN16(m1) rounds
+// d1*q - m1h once, at the weight's own magnitude (as the reference's fp16 weight
+// is rounded).  The small remainder (m1 - m1h) * sum(x) over the sub-block is
+// subtracted after the MMA in fp32, so no scale error is shared by a sub-block.
+struct TQ4K {
+    static constexpr int SPAN = 256, KSTEPS = 16, DEPTH = 1;
+    static constexpr bool HAS_CORR = true;
+    // prefetched: the quant bytes and the 16-byte scale record of rows r0, r0+8
+    struct Raw { uint4 q[2][2]; uint4 meta[2]; };
+    // derived at compute time (keeps the prefetch ring small)
+    struct Prep { __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t r = r0 + rr * 8;
+            const uint8_t *qp = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + tig * 32;
+            R.q[rr][0] = ldg_stream(qp);
+            R.q[rr][1] = ldg_stream(qp + 16);
+            R.meta[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
+        }
+    }
+    __device__ static void prep(const Raw &R, int tig, Prep &P) {
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const uint4 meta = R.meta[rr];
+            P.d[rr] = __half2half2(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
+            const float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
+#pragma unroll
+            for (int part = 0; part < 2; part++) {
+                // get_scale_min_k4 (gguf.zig:960-973) for sub-block j = 2*tig + part,
+                // from the 12 scale bytes held as words y, z, w (runtime shifts, so
+                // the lane-dependent byte index never touches local memory)
+                const int j = 2 * tig + part, sh = 8 * (j & 3);
+                const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
+                const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
+                const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
+                P.sc[rr][part] = __float2half2_rn((float)sc);
+                P.csc[rr][part] = __float2half2_rn(-1024.f * (float)sc);  // exact: |1024*63| < 65504
+                const float m1 = dmin * (float)mm;                         // exact in fp32
+                const __half m1h = __float2half_rn(m1);
+                P.nm1[rr][part] = __half2half2(__hneg(m1h));
+                P.m1[rr][part] = m1 - __half2float(m1h);                   // remainder, exact
+            }
+        }
+    }
+    // k-step s: word i = s & 7 of the group, part = s >> 3 (low nibbles, then high).
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
+        const int i = s & 7, part = s >> 3;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t u = TQ8_0::word(R.q[rr][i >> 2], i & 3);
+            uint32_t v02 = part ? (u >> 4) : u, v13 = part ? (u >> 12) : (u >> 8);
+            __half2 q02 = __hfma2(u2h(magic(v02, 0x000F000Fu)), P.sc[rr][part], P.csc[rr][part]);  // q*sc
+            __half2 q13 = __hfma2(u2h(magic(v13, 0x000F000Fu)), P.sc[rr][part], P.csc[rr][part]);
+            a[rr] = h2u(__hfma2(q02, P.d[rr], P.nm1[rr][part]));  // RN16(d1*q - m1h)
+            a[rr + 2] = h2u(__hfma2(q13, P.d[rr], P.nm1[rr][part]));
+        }
+    }
+    // sum over this lane's two sub-blocks of (m1 - m1h) * sum(x), for rows r0 and r0+8
+    __device__ static void correct(const Prep &P, const float *xsum, int it, int tig, float &c0, float &c1) {
+        float4 X = *reinterpret_cast<const float4 *>(xsum + 16 * it + 4 * tig);
+        float xl = X.x + X.y, xh = X.z + X.w;
+        c0 += P.m1[0][0] * xl + P.m1[0][1] * xh;
+        c1 += P.m1[1][0] * xl + P.m1[1][1] * xh;
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 64 + (s >> 3) * 32 + (s & 7) * 4; }
+};
+
+// Q6_K: one superblock per iteration; lane tig owns half h = tig/2 and the
+// 16 l-values starting at 16*(tig&1): ql bytes [64h+lh, +16) and [64h+32+lh, +16),
+// qh bytes [32h+lh, +16); it produces 64 weights per row.
+// The sub-block scale d*sc is exact in fp32 (11 x 8 bits); it is carried as
+// an fp16 pair s_hi + s_lo so each weight RN16((q-32) * d * sc) is rounded
+// once, like the reference's fp16 weight (gguf.zig:1036-1059, load_gguf.zig:371).
+struct TQ6K {
+    static constexpr int SPAN = 256, KSTEPS = 16, DEPTH = 1;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    // prefetched: ql/qh bytes, the 16 int8 scales and d of rows r0, r0+8
+    struct Raw { uint4 a[2], b[2], h[2], scv[2]; __half d[2]; };
+    // derived at compute time: d*sc as an fp16 hi + lo pair per quarter
+    struct Prep { __half2 s[2][4], sl[2][4]; };
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        const int hh = tig >> 1, lh = (tig & 1) * 16;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t r = r0 + rr * 8;
+            const uint8_t *ql = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + hh * 64 + lh;
+            R.a[rr] = ldg_stream(ql);
+            R.b[rr] = ldg_stream(ql + 32);
+            R.h[rr] = ldg_stream(w.q2 + (size_t)r * (w.cols / 4) + (size_t)it * 64 + hh * 32 + lh);
+            R.scv[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
+            R.d[rr] = reinterpret_cast<const __half *>(w.s2)[(size_t)it * w.rows + r];
+        }
+    }
+    __device__ static void prep(const Raw &R, int tig, Prep &P) {
+        const int hh = tig >> 1;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const float d = __half2float(R.d[rr]);
+            const uint4 scv = R.scv[rr];
+#pragma unroll
+            for (int t = 0; t < 4; t++) {
+                // int8 scale hh*8 + 2t + (tig&1), picked with a select and a runtime
+                // shift (no local-memory indexing)
+                const uint32_t wd = t < 2 ? (hh ? scv.z : scv.x) : (hh ? scv.w : scv.y);
+                const int sc = (int)(int8_t)((wd >> (8 * (2 * (t & 1) + (tig & 1)))) & 0xFFu);
+                const float scale = d * (float)sc;  // exact
+                const __half hi = __float2half_rn(scale);
+                P.s[rr][t] = __half2half2(hi);
+                P.sl[rr][t] = __float2half2_rn(scale - __half2float(hi));
+            }
+        }
+    }
+    // k-step s: t = s >> 2 (which quarter), word i = s & 3.
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
+        const int t = s >> 2, i = s & 3;
+        const __half2 off = __float2half2_rn(1056.f);  // 1024 + 32
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            uint32_t A = TQ8_0::word(R.a[rr], i), B = TQ8_0::word(R.b[rr], i), Q = TQ8_0::word(R.h[rr], i);
+            uint32_t p02, p13;
+            switch (t) {
+            case 0:
+                p02 = (A & 0x000F000Fu) | ((Q << 4) & 0x00300030u);
+                p13 = ((A >> 8) & 0x000F000Fu) | ((Q >> 4) & 0x00300030u);
+                break;
+            case 1:
+                p02 = (B & 0x000F000Fu) | ((Q << 2) & 0x00300030u);
+                p13 = ((B >> 8) & 0x000F000Fu) | ((Q >> 6) & 0x00300030u);
+                break;
+            case 2:
+                p02 = ((A >> 4) & 0x000F000Fu) | (Q & 0x00300030u);
+                p13 = ((A >> 12) & 0x000F000Fu) | ((Q >> 8) & 0x00300030u);
+                break;
+            default:
+                p02 = ((B >> 4) & 0x000F000Fu) | ((Q >> 2) & 0x00300030u);
+                p13 = ((B >> 12) & 0x000F000Fu) | ((Q >> 10) & 0x00300030u);
+                break;
+            }
+            __half2 x02 = __hsub2(u2h(p02 | 0x64006400u), off), x13 = __hsub2(u2h(p13 | 0x64006400u), off);
+            a[rr] = h2u(__hfma2(x02, P.s[rr][t], __hmul2(x02, P.sl[rr][t])));  // ~RN16((q-32) * scale)
+            a[rr + 2] = h2u(__hfma2(x13, P.s[rr][t], __hmul2(x13, P.sl[rr][t])));
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) {
+        return it * SPAN + (tig >> 1) * 128 + (s >> 2) * 32 + (tig & 1) * 16 + (s & 3) * 4;
+    }
+};
+
+// F16 / BF16: 16 weights per lane-row per iteration.
+template <int T>
+struct T16 {
+    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 2;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint4 q[2][2]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        uint32_t k = it * SPAN + tig * 16;
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            if (k < w.cols) {
+                const uint8_t *p = w.q + ((size_t)(r0 + rr * 8) * w.cols + k) * 2;
+                R.q[rr][0] = ldg_stream(p);
+                R.q[rr][1] = ldg_stream(p + 16);
+            } else {
+                R.q[rr][0] = R.q[rr][1] = make_uint4(0, 0, 0, 0);
+            }
+        }
+    }
+    __device__ static uint32_t cvt(uint32_t lo16src, uint32_t hi16src) {
+        // two bf16 (low halves of the sources) -> fp16x2, RN (Gguf.readF16 of a bf16 tensor)
+        float a = __uint_as_float(lo16src << 16), b = __uint_as_float(hi16src << 16);
+        return h2u(__floats2half2_rn(a, b));
+    }
+    __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const uint4 &v = R.q[rr][s >> 1];
+            uint32_t w0 = (s & 1) ? v.z : v.x, w1 = (s & 1) ? v.w : v.y;  // (e0,e1), (e2,e3)
+            if (T == CUQ_F16) {
+                a[rr] = __byte_perm(w0, w1, 0x5410u);      // (e0, e2)
+                a[rr + 2] = __byte_perm(w0, w1, 0x7632u);  // (e1, e3)
+            } else {
+                a[rr] = cvt(w0, w1);
+                a[rr + 2] = cvt(w0 >> 16, w1 >> 16);
+            }
+        }
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 16 + s * 4; }
+};
+
+// ------------------------------------------------------------------ kernel -
+
+struct KArgs {
+    W w, w2;
+    const __half *xq;
+    const float *xsum;  // per-16-column sums of x (xq_sums)
+    uint32_t kpad;
+    float *y;
+    const float *bias;
+    __half *xq_out;
+    uint32_t kpad_out;
+    unsigned long long *argmax64;
+    uint32_t row_base;
+    float *ws;
+    unsigned int *counters;
+    int ksplit;
+    GemvPost post;
+};
+
+__device__ __forceinline__ unsigned long long pack_argmax(float v, uint32_t idx) {
+    uint32_t u = __float_as_uint(v);
+    uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)key << 32) | (unsigned long long)(0xFFFFFFFFu - idx);
+}
+
+// End of a decode step (engine.zig:865-900 + generate.zig:217-244, greedy):
+// the packed argmax becomes the step's output token and, past the forced
+// prompt, the next step's input.
+__device__ void finish_step(StepState *st, const uint32_t *forced, uint32_t *out_tokens) {
+    unsigned long long a = st->argmax64;
+    uint32_t idx = 0xFFFFFFFFu - (uint32_t)(a & 0xFFFFFFFFull);
+    st->argmax64 = 0ull;
+    int s = st->step;
+    out_tokens[s] = idx;
+    st->step = s + 1;
+    st->pos = st->pos + 1;
+    st->token = (s + 1 < st->n_forced) ? (int)forced[s + 1] : (int)idx;
+}
+
+// CTA of 4 warps = TPC = 4 / KW tiles of 16 rows, KW warps per tile splitting
+// the CTA's K range (iteration it goes to warp it % KW of the tile).  Each warp
+// keeps D iterations of loads in flight ahead of the one it computes.
+// One CTA's share of a GEMV: tile group bx, K split part by.  Returns false
+// for a CTA that published a split-K partial and is not the tile's last (its
+// epilogue ran elsewhere); true once the epilogue is done.
+template <class TT, int EPI, int KW, int D, bool GRIDDEP>
+__device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t by) {
+    // Dual (gate|up): one tile per CTA, warps 0-1 stream the gate rows and
+    // warps 2-3 the same rows of up (KW = 2 per matrix), so no warp holds both.
+    constexpr bool DUAL = (EPI == EPI_SILU_XQ);
+    constexpr int TPC = DUAL ? 1 : 4 / KW;  // tiles per CTA
+    constexpr int KWE = DUAL ? 2 : KW;      // warps per tile and matrix
+    constexpr int NV = DUAL ? 32 : 16;      // values per tile (gate rows then up rows)
+    __shared__ float red[4][16];
+    __shared__ int is_last;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int lt = DUAL ? 0 : warp / KW, kw = warp % KWE;
+    const W &wm = (DUAL && warp >= 2) ? p.w2 : p.w;
+    const uint32_t ntiles = p.w.rows / 16;
+    const uint32_t tile = bx * TPC + lt;
+    const bool active = tile < ntiles;
+    const uint32_t r0 = tile * 16 + g;
+    const int ni = (int)((p.w.cols + TT::SPAN - 1) / TT::SPAN);
+    const int per = (ni + p.ksplit - 1) / p.ksplit;
+    const int it0 = by * per, it1 = active ? min(ni, it0 + per) : it0;
+
+    // The weights do not depend on the previous kernel: start streaming the
+    // warp's first D iterations before waiting for the activation.
+    typename TT::Raw ring[D];
+#pragma unroll
+    for (int j = 0; j < D; j++) {
+        const int itj = it0 + kw + KWE * j;
+        if (itj < it1) TT::load(ring[j], wm, r0, itj, tig);
+    }
+    if (GRIDDEP) {
+        griddep_wait();
+        griddep_launch();
+    }
+
+    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);  // B fragments: L1-cached, shared by the SM's CTAs
+    const bool bl = g < 2;
+
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    float k0 = 0.f, k1 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
+    for (int base = it0 + kw; base < it1; base += KWE * D) {
+#pragma unroll
+        for (int j = 0; j < D; j++) {
+            const int it = base + KWE * j;
+            if (it >= it1) break;  // uniform across the warp
+            typename TT::Raw R = ring[j];
+            const int itn = it + KWE * D;
+            if (itn < it1) TT::load(ring[j], wm, r0, itn, tig);  // refill this slot while the iteration computes
+            typename TT::Prep P;
+            TT::prep(R, tig, P);
+#pragma unroll
+            for (int s = 0; s < TT::KSTEPS; s++) {
+                uint2 b = make_uint2(0u, 0u);
+                if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
+                uint32_t a[4];
+                TT::frag(R, P, s, a);
+                mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
+            }
+            if (TT::HAS_CORR) TT::correct(P, p.xsum, it, tig, k0, k1);
+        }
+    }
+    if (TT::HAS_CORR) {  // the four lanes of a row hold different sub-blocks: sum them
+#pragma unroll
+        for (int sh = 1; sh <= 2; sh <<= 1) {
+            k0 += __shfl_xor_sync(0xffffffffu, k0, sh);
+            k1 += __shfl_xor_sync(0xffffffffu, k1, sh);
+        }
+    }
+    if (tig == 0) {
+        red[warp][g] = (c[0] + c[1]) - k0;
+        red[warp][g + 8] = (c[2] + c[3]) - k1;
+    }
+    __syncthreads();
+    // thread t < TPC * NV owns value vi of local tile tl (dual: vi < 16 gate, >= 16 up)
+    const int t = threadIdx.x;
+    const int tl = t / NV, vi = t % NV;
+    const bool own = t < TPC * NV && bx * TPC + tl < ntiles;
+    const uint32_t row = (bx * TPC + tl) * 16 + (vi & 15);
+    float v = 0.f;
+    if (own) {
+        const int w0 = DUAL ? 2 * (vi >> 4) : tl * KW;
+#pragma unroll
+        for (int w = 0; w < KWE; w++) v += red[w0 + w][vi & 15];
+    }
+    const uint32_t rows = p.w.rows;
+    if (p.ksplit > 1) {
+        // split-K: publish the partials, the last CTA of this column of the grid
+        // (atomic ticket per tile group) reduces them in a fixed order.
+        if (own) p.ws[((size_t)by * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row] = v;
+        __threadfence();
+        __syncthreads();
+        if (t == 0) {
+            unsigned int prev = atomicAdd(&p.counters[bx], 1u);
+            is_last = (prev == (unsigned)p.ksplit - 1u);
+        }
+        __syncthreads();
+        if (!is_last) return false;
+        __threadfence();
+        if (own) {
+            float acc = 0.f;
+            for (int ky = 0; ky < p.ksplit; ky++)
+                acc += __ldcg(&p.ws[((size_t)ky * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row]);
+            v = acc;
+        }
+        if (t == 0) p.counters[bx] = 0u;
+    }
+    if (EPI == EPI_SILU_XQ) {
+        __shared__ float gu[TPC][32];
+        __shared__ float act16[TPC][16];
+        if (own) gu[tl][vi] = v;
+        __syncthreads();
+        if (own && vi < 16) {
+            float gt = gu[tl][vi], ut = gu[tl][16 + vi];
+            // cpu.siluMul (cpu.zig:65-70): g * (1 / (1 + exp(-g))) * u
+            float sg = 1.0f / (1.0f + expf(-gt));
+            float act = (gt * sg) * ut;
+            if (p.y) p.y[row] = act;
+            __half hi = __float2half_rn(act);
+            __half lo = __float2half_rn(act - __half2float(hi));
+            uint32_t pos = xq_pos(row);
+            p.xq_out[pos] = hi;
+            p.xq_out[p.kpad_out + pos] = lo;
+            act16[tl][vi] = act;
+        }
+        __syncthreads();
+        if (t < TPC && bx * TPC + t < ntiles) {  // a tile's 16 rows are exactly one xq sum group
+            float acc = 0.f;
+            for (int j = 0; j < 16; j++) acc += act16[t][j];
+            xq_sums(p.xq_out, p.kpad_out)[bx * TPC + t] = acc;
+        }
+    } else if (EPI == EPI_TP_PUSH) {
+        // this rank's partial of rows [row] into slot [rank] of every rank's buffer
+        if (own)
+            for (int q = 0; q < p.post.tp.size; q++) tp_slot(p.post.tp, q, p.post.tp_phase, p.post.tp.rank)[row] = v;
+        __threadfence_system();
+        __syncthreads();
+        if (t == 0) tp_signal(p.post.tp, p.post.tp_phase);
+    } else {
+        if (own) {
+            if (EPI == EPI_STORE || EPI == EPI_ARGMAX) {
+                if (p.bias) v = v + p.bias[row];
+                p.y[row] = v;
+            } else if (EPI == EPI_ADD) {
+                if (p.bias) v = v + p.bias[row];
+                p.y[row] = p.y[row] + v;
+            }
+        }
+        if (EPI == EPI_ARGMAX) {
+            // first index of the maximum (cpu.zig:477-483) as a packed 64-bit max
+            // across the CTA, then across CTAs: larger value wins, then smaller index.
+            if (t < TPC * 16) {  // TPC * 16 is 16, 32 or 64 threads
+                unsigned long long key = own ? pack_argmax(v, p.row_base + row) : 0ull;
+                constexpr unsigned mask = TPC == 1 ? 0x0000ffffu : 0xffffffffu;
+#pragma unroll
+                for (int o = TPC == 1 ? 8 : 16; o > 0; o >>= 1) {
+                    unsigned long long other = __shfl_xor_sync(mask, key, o);
+                    key = other > key ? other : key;
+                }
+                if ((t & 31) == 0) atomicMax(p.argmax64, key);
+            }
+        }
+    }
+    return true;
+}
+
+}  // namespace
+
+}  // namespace cuq

@@ -3,6 +3,7 @@
 // Each kernel restates one reference CPU op (src/cpu.zig) and names it.  The
 // KV cache is fp16 like the reference's (engine.zig:447-458, 952-970) but laid
 // out [kv_head][position][head_dim] so one head's keys are contiguous.
+#include "attn_impl.cuh"
 #include "common.cuh"
 #include "ops.cuh"
 
@@ -96,247 +97,6 @@ __global__ void rope_cache_kernel(const float *__restrict__ qkv, uint32_t qkv_st
     }
 }
 
-// ------------------------------------------------------------ attention ---
-// cpu.attentionDecode (cpu.zig:323-395) as split-position flash decoding.  CTA
-// (kv head, split) covers a contiguous range of cache positions for every query
-// head of that KV group (GQA: query head h reads KV head h / (heads / kv_heads)).
-// hd/8 lanes share one position (8 dims each: one 16-byte K and V load); a warp
-// walks U * 32/(hd/8) positions per iteration with all their loads issued before
-// the math, and keeps an online softmax (m, l, o).  Scores are dot(q, k) *
-// (1 / sqrt(hd)) in fp32.  Splits write partial (o, m, l) to `part`:
-//   part[s][h][hd] (unnormalised o), then at part + nsplit*heads*hd: [s][h][2] (m, l).
-// Splits cover at least ATT_MIN_CHUNK positions, so a short context uses few
-// splits and the merge reads few partials.
-constexpr uint32_t ATT_MIN_CHUNK = 32;
-constexpr int ATT_MAX_SPLIT = 64;
-
-struct SplitRange {
-    uint32_t p0, p1, nact;
-};
-
-__device__ __forceinline__ SplitRange split_range(uint32_t n, int nsplit, uint32_t split) {
-    uint32_t chunk = (n + (uint32_t)nsplit - 1) / (uint32_t)nsplit;
-    chunk = (chunk + 15u) & ~15u;
-    if (chunk < ATT_MIN_CHUNK) chunk = ATT_MIN_CHUNK;
-    SplitRange r;
-    r.nact = (n + chunk - 1) / chunk;
-    r.p0 = split * chunk;
-    r.p1 = min(n, r.p0 + chunk);
-    return r;
-}
-
-// Walk positions [p0, p1) of one KV head with this CTA's 4 warps.  Warp-uniform
-// loop bound: every lane reaches every shuffle; lanes past the end load zeros
-// and score -inf.
-template <int HD, int G>
-__device__ __forceinline__ void attn_walk(const float (&qr)[G][8], const __half *kh, const __half *vh, uint32_t p0,
-                                          uint32_t p1, int warp, int lp, int pg, float (&m)[G], float (&l)[G],
-                                          float (&o)[G][8]) {
-    constexpr int E = 8, LPP = HD / E, PPW = 32 / LPP, U = G <= 4 ? 4 : 2;
-    const float scale = 1.0f / sqrtf((float)HD);
-    for (uint32_t pb = p0 + (uint32_t)warp * PPW * U; pb < p1; pb += 4u * PPW * U) {
-        uint4 ku[U], vu[U];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const uint32_t p = pb + u * PPW + pg;
-            ku[u] = make_uint4(0u, 0u, 0u, 0u);
-            vu[u] = ku[u];
-            if (p < p1) {
-                ku[u] = *reinterpret_cast<const uint4 *>(kh + (size_t)p * HD + lp * E);
-                vu[u] = *reinterpret_cast<const uint4 *>(vh + (size_t)p * HD + lp * E);
-            }
-        }
-        float s[U][G];
-#pragma unroll
-        for (int u = 0; u < U; u++) {
-            const __half2 *k2 = reinterpret_cast<const __half2 *>(&ku[u]);
-            float kf[E];
-#pragma unroll
-            for (int j = 0; j < 4; j++) {
-                float2 kk = __half22float2(k2[j]);
-                kf[2 * j] = kk.x;
-                kf[2 * j + 1] = kk.y;
-            }
-            const bool valid = pb + u * PPW + pg < p1;
-#pragma unroll
-            for (int g = 0; g < G; g++) {
-                float d = 0.f;
-#pragma unroll
-                for (int e = 0; e < E; e++) d = fmaf(qr[g][e], kf[e], d);
-#pragma unroll
-                for (int sh = 1; sh < LPP; sh <<= 1) d += __shfl_xor_sync(0xffffffffu, d, sh);
-                s[u][g] = valid ? d * scale : -INFINITY;
-            }
-        }
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            float mx = s[0][g];
-#pragma unroll
-            for (int u = 1; u < U; u++) mx = fmaxf(mx, s[u][g]);
-            const float mn = fmaxf(m[g], mx);
-            if (mn == -INFINITY) continue;  // nothing valid yet (no shuffles below)
-            const float corr = expf(m[g] - mn);
-            l[g] *= corr;
-#pragma unroll
-            for (int e = 0; e < E; e++) o[g][e] *= corr;
-#pragma unroll
-            for (int u = 0; u < U; u++) {
-                const float pe = expf(s[u][g] - mn);  // 0 for an invalid lane
-                const __half2 *v2 = reinterpret_cast<const __half2 *>(&vu[u]);
-                l[g] += pe;
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    float2 vv = __half22float2(v2[j]);
-                    o[g][2 * j] = fmaf(pe, vv.x, o[g][2 * j]);
-                    o[g][2 * j + 1] = fmaf(pe, vv.y, o[g][2 * j + 1]);
-                }
-            }
-            m[g] = mn;
-        }
-    }
-}
-
-// Merge the lanes of each warp and the CTA's 4 warps; write the split's partial
-// (o, m, l) for query heads kvh*G .. kvh*G+G-1.
-template <int HD, int G>
-__device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], float (&o)[G][8], int warp, int lp,
-                                                 int pg, float *part, uint32_t split, int nsplit, uint32_t heads,
-                                                 uint32_t kvh) {
-    constexpr int E = 8, LPP = HD / E;
-#pragma unroll
-    for (int g = 0; g < G; g++) {
-#pragma unroll
-        for (int sh = LPP; sh < 32; sh <<= 1) {
-            float mo = __shfl_xor_sync(0xffffffffu, m[g], sh);
-            float lo = __shfl_xor_sync(0xffffffffu, l[g], sh);
-            float mn = fmaxf(m[g], mo);
-            float ca = mn == -INFINITY ? 0.f : expf(m[g] - mn);
-            float cb = mn == -INFINITY ? 0.f : expf(mo - mn);
-            l[g] = l[g] * ca + lo * cb;
-#pragma unroll
-            for (int e = 0; e < E; e++) {
-                float oo = __shfl_xor_sync(0xffffffffu, o[g][e], sh);
-                o[g][e] = o[g][e] * ca + oo * cb;
-            }
-            m[g] = mn;
-        }
-    }
-    __shared__ float sm_m[4][G], sm_l[4][G], sm_o[4][G][HD];
-    if (pg == 0) {
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            if (lp == 0) {
-                sm_m[warp][g] = m[g];
-                sm_l[warp][g] = l[g];
-            }
-#pragma unroll
-            for (int e = 0; e < E; e++) sm_o[warp][g][lp * E + e] = o[g][e];
-        }
-    }
-    __syncthreads();
-    float *po = part + ((size_t)split * heads + kvh * G) * HD;
-    float *pml = part + (size_t)nsplit * heads * HD + ((size_t)split * heads + kvh * G) * 2;
-    for (int t = threadIdx.x; t < G * HD; t += blockDim.x) {
-        const int g = t / HD, dd = t % HD;
-        const float mm = fmaxf(fmaxf(sm_m[0][g], sm_m[1][g]), fmaxf(sm_m[2][g], sm_m[3][g]));
-        float acc = 0.f, ll = 0.f;
-#pragma unroll
-        for (int w = 0; w < 4; w++) {
-            const float c = mm == -INFINITY ? 0.f : expf(sm_m[w][g] - mm);
-            acc += sm_o[w][g][dd] * c;
-            ll += sm_l[w][g] * c;
-        }
-        po[t] = acc;
-        if (dd == 0) {
-            pml[2 * g] = mm;
-            pml[2 * g + 1] = ll;
-        }
-    }
-}
-
-// Merge the nact splits of query heads h0 .. h0+NH-1 (one CTA, any size):
-// out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.  Every split's weight is
-// computed once into shared memory, then each thread sums float4 columns with
-// independent loads.  `res` receives the NH*HD results.
-template <int HD, int NH>
-__device__ __forceinline__ void attn_merge(const float *part, int nsplit, uint32_t nact, uint32_t heads, uint32_t h0,
-                                           float *res) {
-    __shared__ float cw[ATT_MAX_SPLIT][NH];
-    __shared__ float inv_l[NH];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
-    const float *pml = part + (size_t)nsplit * heads * HD;
-    for (int g = warp; g < NH; g += nw) {
-        const uint32_t h = h0 + g;
-        float ms[2], ls[2];
-        float M = -INFINITY;
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const uint32_t s = lane + 32 * j;
-            ms[j] = s < nact ? __ldcg(pml + ((size_t)s * heads + h) * 2) : -INFINITY;
-            ls[j] = s < nact ? __ldcg(pml + ((size_t)s * heads + h) * 2 + 1) : 0.f;
-            M = fmaxf(M, ms[j]);
-        }
-#pragma unroll
-        for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
-        float L = 0.f;
-#pragma unroll
-        for (int j = 0; j < 2; j++) {
-            const uint32_t s = lane + 32 * j;
-            const float c = ms[j] == -INFINITY ? 0.f : expf(ms[j] - M);
-            if (s < nact) cw[s][g] = c;
-            L += ls[j] * c;
-        }
-#pragma unroll
-        for (int sh = 16; sh > 0; sh >>= 1) L += __shfl_xor_sync(0xffffffffu, L, sh);
-        if (lane == 0) inv_l[g] = 1.0f / L;
-    }
-    __syncthreads();
-    for (int t = threadIdx.x; t < NH * HD / 4; t += blockDim.x) {
-        const int g = t / (HD / 4), d4 = t % (HD / 4);
-        const float4 *src = reinterpret_cast<const float4 *>(part + (size_t)(h0 + g) * HD) + d4;
-        const size_t sstride = (size_t)heads * HD / 4;
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-        for (uint32_t s = 0; s < nact; s++) {
-            const float4 v = __ldcg(src + s * sstride);
-            const float c = cw[s][g];
-            acc.x = fmaf(v.x, c, acc.x);
-            acc.y = fmaf(v.y, c, acc.y);
-            acc.z = fmaf(v.z, c, acc.z);
-            acc.w = fmaf(v.w, c, acc.w);
-        }
-        const float il = inv_l[g];
-        res[4 * t] = acc.x * il;
-        res[4 * t + 1] = acc.y * il;
-        res[4 * t + 2] = acc.z * il;
-        res[4 * t + 3] = acc.w * il;
-    }
-    __syncthreads();
-}
-
-// Write merged head outputs as the o projection's xq input (hi/lo + per-16 sums)
-// and/or fp32.  `res` holds NH*HD values for columns c0 .. c0+NH*HD-1.
-__device__ __forceinline__ void attn_emit(const float *res, uint32_t count, uint32_t c0, float *out, __half *xq,
-                                          uint32_t kpad) {
-    for (uint32_t t = threadIdx.x; t < count; t += blockDim.x) {
-        const float r = res[t];
-        const uint32_t i = c0 + t;
-        if (out) out[i] = r;
-        if (xq) {
-            const __half hi = __float2half_rn(r);
-            xq[xq_pos(i)] = hi;
-            xq[kpad + xq_pos(i)] = __float2half_rn(r - __half2float(hi));
-        }
-    }
-    if (xq) {  // c0 and count are multiples of 16
-        for (uint32_t u = threadIdx.x; u < count / 16; u += blockDim.x) {
-            float a = 0.f;
-            for (int j = 0; j < 16; j++) a += res[16 * u + j];
-            xq_sums(xq, kpad)[c0 / 16 + u] = a;
-        }
-    }
-}
-
 template <int HD, int G>
 __global__ void __launch_bounds__(128) attn_decode_kernel(const float *__restrict__ q, const __half *__restrict__ kc,
                                                            const __half *__restrict__ vc, uint32_t cache_stride,
@@ -379,97 +139,9 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float *__restri
     attn_emit(res, HD, blockIdx.x * HD, out, xq, kpad);
 }
 
-// ---------------------------------------------------- fused decode attention
-// One decode step's attention for one layer, in one launch (engine.zig:595-612
-// + ropeAndCache 952-970 + cpu.attentionDecode 323-395):
-//   * every CTA rotates its KV group's queries from the qkv vector itself
-//     (RoPE from the host-built cos|sin table, cpu.zig:22-62);
-//   * the CTA whose split holds the step's position rotates k, rounds k and v
-//     to fp16 and writes them into the cache before it reads that position;
-//   * splits run attn_walk as attn_decode_kernel does;
-//   * the last split CTA of each KV group to finish (atomic ticket) merges the
-//     group's splits and writes the o projection's xq input directly.
-struct AttnStepArgs {
-    const float *qkv;            // [q | k | v] after bias
-    const float *cs;             // [max_seq][hd] cos | sin
-    const StepState *state;      // pos
-    __half *k_cache, *v_cache;   // [kv_heads][cache_stride][hd]
-    uint32_t cache_stride, heads, kv_heads;
-    int adjacent, nsplit;
-    float *part;                 // nsplit * heads * (hd + 2) floats
-    unsigned int *tickets;       // [kv_heads], self-resetting
-    __half *xq;                  // o-projection input (heads*hd columns)
-};
-
-template <int HD>
-__device__ __forceinline__ float rope_elem(const float *v, uint32_t d, const float *csr, int adjacent) {
-    // rotated element d of one head vector `v` (cpu.zig:33-36 / 57-60)
-    constexpr uint32_t half = HD / 2;
-    if (adjacent) {
-        uint32_t j = d >> 1;
-        float a = v[2 * j], b = v[2 * j + 1], c = csr[j], s = csr[half + j];
-        return (d & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
-    }
-    uint32_t i = d < half ? d : d - half;
-    float a = v[i], b = v[i + half], c = csr[i], s = csr[half + i];
-    return d < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
-}
-
 template <int HD, int G>
 __global__ void __launch_bounds__(128) attn_step_kernel(const AttnStepArgs p) {
-    constexpr int E = 8, LPP = HD / E;
-    griddep_wait();
-    griddep_launch();
-    const uint32_t kvh = blockIdx.x, split = blockIdx.y;
-    const uint32_t pos = (uint32_t)p.state->pos, n = pos + 1u;
-    const SplitRange r = split_range(n, p.nsplit, split);
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int lp = lane % LPP, pg = lane / LPP;
-    const uint32_t qd = p.heads * HD, kvd = p.kv_heads * HD;
-    const float *csr = p.cs + (size_t)pos * HD;
-    __half *kh = p.k_cache + (size_t)kvh * p.cache_stride * HD;
-    __half *vh = p.v_cache + (size_t)kvh * p.cache_stride * HD;
-
-    if (split < r.nact) {
-        if (pos >= r.p0 && pos < r.p1) {  // this CTA owns the new position: write its K/V row
-            const float *kin = p.qkv + qd + (size_t)kvh * HD;
-            const float *vin = p.qkv + qd + kvd + (size_t)kvh * HD;
-            for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
-                kh[(size_t)pos * HD + d] = __float2half_rn(rope_elem<HD>(kin, d, csr, p.adjacent));
-                vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
-            }
-        }
-        float qr[G][E];
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            const float *qh = p.qkv + (size_t)(kvh * G + g) * HD;
-#pragma unroll
-            for (int e = 0; e < E; e++) qr[g][e] = rope_elem<HD>(qh, lp * E + e, csr, p.adjacent);
-        }
-        __syncthreads();  // the K/V row written above is read below
-        float m[G], l[G], o[G][E];
-#pragma unroll
-        for (int g = 0; g < G; g++) {
-            m[g] = -INFINITY;
-            l[g] = 0.f;
-#pragma unroll
-            for (int e = 0; e < E; e++) o[g][e] = 0.f;
-        }
-        attn_walk<HD, G>(qr, kh, vh, r.p0, r.p1, warp, lp, pg, m, l, o);
-        attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh);
-    }
-    // the last CTA of this KV group (active or not) merges the group's heads
-    __shared__ int is_last;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(&p.tickets[kvh], 1u) == (unsigned)p.nsplit - 1u;
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    __shared__ float res[G * HD];
-    attn_merge<HD, G>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res);
-    attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
-    if (threadIdx.x == 0) p.tickets[kvh] = 0u;
+    attn_step_body<HD, G, true>(p, blockIdx.x, blockIdx.y);
 }
 
 // ------------------------------------------------------ prefill helpers --
