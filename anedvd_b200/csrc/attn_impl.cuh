@@ -21,6 +21,9 @@ namespace {
 // splits and the merge reads few partials.
 constexpr uint32_t ATT_MIN_CHUNK = 32;
 constexpr int ATT_MAX_SPLIT = 64;
+// Contexts up to this many positions are walked by one CTA per KV group, which
+// then writes the result directly (no partials, no merge).
+constexpr uint32_t ATT_DIRECT_MAX = 128;
 
 struct SplitRange {
     uint32_t p0, p1, nact;
@@ -30,6 +33,7 @@ __device__ __forceinline__ SplitRange split_range(uint32_t n, int nsplit, uint32
     uint32_t chunk = (n + (uint32_t)nsplit - 1) / (uint32_t)nsplit;
     chunk = (chunk + 15u) & ~15u;
     if (chunk < ATT_MIN_CHUNK) chunk = ATT_MIN_CHUNK;
+    if (n <= ATT_DIRECT_MAX) chunk = n;  // one split
     SplitRange r;
     r.nact = (n + chunk - 1) / chunk;
     r.p0 = split * chunk;
@@ -108,12 +112,26 @@ __device__ __forceinline__ void attn_walk(const float (&qr)[G][8], const __half 
     }
 }
 
+// Shared-memory scratch (floats) of the split store, the merge and the fused
+// step body for a group of G query heads of dimension HD.  The kernels own it
+// (a static array, or a slice of the persistent kernel's dynamic shared memory
+// that other phases reuse), so instantiations do not each add static memory.
+constexpr int attn_store_floats(int HD, int G) { return 8 * G + 4 * G * HD; }
+constexpr int attn_merge_floats(int NH) { return (ATT_MAX_SPLIT + 4) * NH; }  // cw, inv_l (16-byte aligned end)
+constexpr int attn_step_floats(int HD, int G) {
+    // the direct path keeps its result after the store scratch; the merge path after the merge scratch
+    return attn_store_floats(HD, G) > attn_merge_floats(G) ? attn_store_floats(HD, G) + G * HD
+                                                           : attn_merge_floats(G) + G * HD;
+}
+
 // Merge the lanes of each warp and the CTA's 4 warps; write the split's partial
-// (o, m, l) for query heads kvh*G .. kvh*G+G-1.
+// (o, m, l) for query heads kvh*G .. kvh*G+G-1, or, when `direct` is set (the
+// split is the whole context), the final o / l into direct[0 .. G*HD).
+// scr: attn_store_floats(HD, G).
 template <int HD, int G>
 __device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], float (&o)[G][8], int warp, int lp,
                                                  int pg, float *part, uint32_t split, int nsplit, uint32_t heads,
-                                                 uint32_t kvh) {
+                                                 uint32_t kvh, float *scr, float *direct = nullptr) {
     constexpr int E = 8, LPP = HD / E;
 #pragma unroll
     for (int g = 0; g < G; g++) {
@@ -133,7 +151,9 @@ __device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], f
             m[g] = mn;
         }
     }
-    __shared__ float sm_m[4][G], sm_l[4][G], sm_o[4][G][HD];
+    float(*sm_m)[G] = reinterpret_cast<float(*)[G]>(scr);
+    float(*sm_l)[G] = reinterpret_cast<float(*)[G]>(scr + 4 * G);
+    float(*sm_o)[G][HD] = reinterpret_cast<float(*)[G][HD]>(scr + 8 * G);
     if (pg == 0) {
 #pragma unroll
         for (int g = 0; g < G; g++) {
@@ -158,6 +178,10 @@ __device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], f
             acc += sm_o[w][g][dd] * c;
             ll += sm_l[w][g] * c;
         }
+        if (direct) {
+            direct[t] = acc * (1.0f / ll);  // as attn_merge does for a single split
+            continue;
+        }
         po[t] = acc;
         if (dd == 0) {
             pml[2 * g] = mm;
@@ -169,12 +193,13 @@ __device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], f
 // Merge the nact splits of query heads h0 .. h0+NH-1 (one CTA, any size):
 // out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.  Every split's weight is
 // computed once into shared memory, then each thread sums float4 columns with
-// independent loads.  `res` receives the NH*HD results.
+// independent loads.  `res` receives the NH*HD results; scr:
+// attn_merge_floats(NH), not overlapping res.
 template <int HD, int NH>
 __device__ __forceinline__ void attn_merge(const float *part, int nsplit, uint32_t nact, uint32_t heads, uint32_t h0,
-                                           float *res) {
-    __shared__ float cw[ATT_MAX_SPLIT][NH];
-    __shared__ float inv_l[NH];
+                                           float *res, float *scr) {
+    float(*cw)[NH] = reinterpret_cast<float(*)[NH]>(scr);
+    float *inv_l = scr + ATT_MAX_SPLIT * NH;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const float *pml = part + (size_t)nsplit * heads * HD;
     for (int g = warp; g < NH; g += nw) {
@@ -273,26 +298,26 @@ struct AttnStepArgs {
 
 template <int HD>
 __device__ __forceinline__ float rope_elem(const float *v, uint32_t d, const float *csr, int adjacent) {
-    // rotated element d of one head vector `v` (cpu.zig:33-36 / 57-60)
+    // rotated element d of one head vector `v` (cpu.zig:33-36 / 57-60); v was
+    // written by other CTAs, so it is read through L2
     constexpr uint32_t half = HD / 2;
     if (adjacent) {
         uint32_t j = d >> 1;
-        float a = v[2 * j], b = v[2 * j + 1], c = csr[j], s = csr[half + j];
+        float a = __ldcg(v + 2 * j), b = __ldcg(v + 2 * j + 1), c = csr[j], s = csr[half + j];
         return (d & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
     }
     uint32_t i = d < half ? d : d - half;
-    float a = v[i], b = v[i + half], c = csr[i], s = csr[half + i];
+    float a = __ldcg(v + i), b = __ldcg(v + i + half), c = csr[i], s = csr[half + i];
     return d < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
 }
 
-template <int HD, int G, bool GRIDDEP>
-__device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t kvh, uint32_t split) {
+// KV group kvh, position split `split` of the step at position pos; scr:
+// attn_step_floats(HD, G) floats of shared memory.
+template <int HD, int G>
+__device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t kvh, uint32_t split, uint32_t pos,
+                                               float *scr) {
     constexpr int E = 8, LPP = HD / E;
-    if (GRIDDEP) {
-        griddep_wait();
-        griddep_launch();
-    }
-    const uint32_t pos = (uint32_t)p.state->pos, n = pos + 1u;
+    const uint32_t n = pos + 1u;
     const SplitRange r = split_range(n, p.nsplit, split);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int lp = lane % LPP, pg = lane / LPP;
@@ -301,13 +326,15 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
     __half *kh = p.k_cache + (size_t)kvh * p.cache_stride * HD;
     __half *vh = p.v_cache + (size_t)kvh * p.cache_stride * HD;
 
+    const bool direct = r.nact == 1;  // one CTA per KV group: it writes the output itself
+    if (direct && split != 0) return;
     if (split < r.nact) {
         if (pos >= r.p0 && pos < r.p1) {  // this CTA owns the new position: write its K/V row
             const float *kin = p.qkv + qd + (size_t)kvh * HD;
             const float *vin = p.qkv + qd + kvd + (size_t)kvh * HD;
             for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
                 kh[(size_t)pos * HD + d] = __float2half_rn(rope_elem<HD>(kin, d, csr, p.adjacent));
-                vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
+                vh[(size_t)pos * HD + d] = __float2half_rn(__ldcg(vin + d));
             }
         }
         float qr[G][E];
@@ -327,7 +354,14 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
             for (int e = 0; e < E; e++) o[g][e] = 0.f;
         }
         attn_walk<HD, G>(qr, kh, vh, r.p0, r.p1, warp, lp, pg, m, l, o);
-        attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh);
+        if (direct) {
+            float *res = scr + attn_store_floats(HD, G);
+            attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh, scr, res);
+            __syncthreads();
+            attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
+            return;
+        }
+        attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh, scr);
     }
     // the last CTA of this KV group (active or not) merges the group's heads
     __shared__ int is_last;
@@ -337,8 +371,8 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    __shared__ float res[G * HD];
-    attn_merge<HD, G>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res);
+    float *res = scr + attn_merge_floats(G);
+    attn_merge<HD, G>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res, scr);
     attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
     if (threadIdx.x == 0) p.tickets[kvh] = 0u;
 }

@@ -27,7 +27,13 @@ namespace {
 
 template <class TT, int EPI, int KW, int D>
 __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
-    if (!gemv_body<TT, EPI, KW, D, true>(p, blockIdx.x, blockIdx.y)) return;
+    __shared__ GemvShared sh;
+    extern __shared__ __align__(16) uint8_t gemv_dyn[];  // the post-op's x stage
+    if (!gemv_body<TT, EPI, KW, D>(p, blockIdx.x, blockIdx.y, sh, [] {
+            griddep_wait();
+            griddep_launch();
+        }))
+        return;
     const int t = threadIdx.x;
     __shared__ int is_last;
     if (p.post.op == POST_NONE) return;
@@ -41,7 +47,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     __syncthreads();
     if (!is_last) return;
     __threadfence();
-    extern __shared__ float4 rn_stage[];  // n floats when the launch gave them (fast path)
+    float4 *rn_stage = reinterpret_cast<float4 *>(gemv_dyn);  // n floats when the launch gave them (fast path)
     const bool fast = p.post.n % 16 == 0 && p.post.n <= RN_MAX;
     if (p.post.op == POST_TP_REDUCE) {
         // every rank's CTAs pushed once: x += sum over ranks (+ bias), then the RMSNorm
@@ -120,22 +126,7 @@ cudaError_t launch_epi(const GemvArgs &a, const KArgs &k, int kw, cudaStream_t s
 
 template <class TT>
 int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
-    KArgs k;
-    k.w = wview(*a.w);
-    if (a.w2) k.w2 = wview(*a.w2);
-    k.xq = a.xq;
-    k.kpad = xq_pad(a.w->cols);
-    k.xsum = xq_sums(a.xq, k.kpad);
-    k.y = a.y;
-    k.bias = a.bias;
-    k.xq_out = a.xq_out;
-    k.kpad_out = xq_pad(a.w->rows);
-    k.argmax64 = a.argmax64;
-    k.row_base = a.row_base;
-    k.ws = a.ws;
-    k.counters = a.counters;
-    k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
-    k.post = a.post;
+    const KArgs k = make_kargs(a);
     const int kw = gemv_pick_plan(*a.w, 0).kw;
     cudaError_t e;
     switch (epi) {

@@ -10,9 +10,13 @@ namespace cuq {
 
 namespace {
 
+// A weight as the decoders see it: the planes of a whole matrix in global
+// memory, or one pipeline stage of a tile in shared memory (rows = 16, cols =
+// the stage's valid columns, qs / q2s = padded row strides).
 struct W {
     const uint8_t *q, *q2, *s, *s2;  // plane pointers (see common.cuh)
     uint32_t rows, cols;
+    uint32_t qs, q2s;                // bytes per row of the row-major q plane and of Q6_K's qh plane
 };
 
 W wview(const Planes &p) {
@@ -23,6 +27,12 @@ W wview(const Planes &p) {
     w.s2 = p.off_s2 == SIZE_MAX ? nullptr : p.base + p.off_s2;
     w.rows = p.rows;
     w.cols = p.cols;
+    switch (p.type) {
+    case CUQ_Q8_0: w.qs = p.cols; break;
+    case CUQ_F16: case CUQ_BF16: w.qs = p.cols * 2; break;
+    default: w.qs = p.cols / 2; break;
+    }
+    w.q2s = p.type == CUQ_Q6_K ? p.cols / 4 : 0;
     return w;
 }
 
@@ -33,6 +43,12 @@ __device__ __forceinline__ uint4 ldg_stream(const void *p) {
                  : "l"(p));
     return v;
 }
+
+// Where a decoder's 16-byte quant loads come from: the planes in global memory,
+// streamed past L1.
+struct SrcGlobal {
+    __device__ static uint4 ld16(const void *p) { return ldg_stream(p); }
+};
 
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
@@ -63,11 +79,12 @@ struct TQ8_0 {
     struct Raw { uint4 q[2]; __half2 d[2]; };
     struct Prep {};
     __device__ static void prep(const Raw &, int, Prep &) {}
+    template <class Src = SrcGlobal>
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         uint32_t k = it * SPAN + tig * 16;
         if (k < w.cols) {
-            R.q[0] = ldg_stream(w.q + (size_t)r0 * w.cols + k);
-            R.q[1] = ldg_stream(w.q + (size_t)(r0 + 8) * w.cols + k);
+            R.q[0] = Src::ld16(w.q + (size_t)r0 * w.qs + k);
+            R.q[1] = Src::ld16(w.q + (size_t)(r0 + 8) * w.qs + k);
             const __half *d = reinterpret_cast<const __half *>(w.s) + (size_t)(k >> 5) * w.rows;
             R.d[0] = __half2half2(d[r0]);
             R.d[1] = __half2half2(d[r0 + 8]);
@@ -101,12 +118,13 @@ struct TQ4L {
     struct Raw { uint4 q[2]; __half2 d[2], m[2]; uint32_t qh[2]; };
     struct Prep {};
     __device__ static void prep(const Raw &, int, Prep &) {}
+    template <class Src = SrcGlobal>
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         uint32_t k = it * SPAN + tig * 32;
         if (k < w.cols) {
             uint32_t b = k >> 5;
-            R.q[0] = ldg_stream(w.q + (size_t)r0 * (w.cols / 2) + b * 16);
-            R.q[1] = ldg_stream(w.q + (size_t)(r0 + 8) * (w.cols / 2) + b * 16);
+            R.q[0] = Src::ld16(w.q + (size_t)r0 * w.qs + b * 16);
+            R.q[1] = Src::ld16(w.q + (size_t)(r0 + 8) * w.qs + b * 16);
             if (T == CUQ_Q4_0 || T == CUQ_Q5_0) {
                 const __half *d = reinterpret_cast<const __half *>(w.s) + (size_t)b * w.rows;
                 R.d[0] = __half2half2(d[r0]);
@@ -186,13 +204,14 @@ struct TQ4K {
     struct Raw { uint4 q[2][2]; uint4 meta[2]; };
     // derived at compute time (keeps the prefetch ring small)
     struct Prep { __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
+    template <class Src = SrcGlobal>
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             uint32_t r = r0 + rr * 8;
-            const uint8_t *qp = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + tig * 32;
-            R.q[rr][0] = ldg_stream(qp);
-            R.q[rr][1] = ldg_stream(qp + 16);
+            const uint8_t *qp = w.q + (size_t)r * w.qs + (size_t)it * 128 + tig * 32;
+            R.q[rr][0] = Src::ld16(qp);
+            R.q[rr][1] = Src::ld16(qp + 16);
             R.meta[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
         }
     }
@@ -258,15 +277,16 @@ struct TQ6K {
     struct Raw { uint4 a[2], b[2], h[2], scv[2]; __half d[2]; };
     // derived at compute time: d*sc as an fp16 hi + lo pair per quarter
     struct Prep { __half2 s[2][4], sl[2][4]; };
+    template <class Src = SrcGlobal>
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         const int hh = tig >> 1, lh = (tig & 1) * 16;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             uint32_t r = r0 + rr * 8;
-            const uint8_t *ql = w.q + (size_t)r * (w.cols / 2) + (size_t)it * 128 + hh * 64 + lh;
-            R.a[rr] = ldg_stream(ql);
-            R.b[rr] = ldg_stream(ql + 32);
-            R.h[rr] = ldg_stream(w.q2 + (size_t)r * (w.cols / 4) + (size_t)it * 64 + hh * 32 + lh);
+            const uint8_t *ql = w.q + (size_t)r * w.qs + (size_t)it * 128 + hh * 64 + lh;
+            R.a[rr] = Src::ld16(ql);
+            R.b[rr] = Src::ld16(ql + 32);
+            R.h[rr] = Src::ld16(w.q2 + (size_t)r * w.q2s + (size_t)it * 64 + hh * 32 + lh);
             R.scv[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
             R.d[rr] = reinterpret_cast<const __half *>(w.s2)[(size_t)it * w.rows + r];
         }
@@ -336,14 +356,15 @@ struct T16 {
     struct Raw { uint4 q[2][2]; };
     struct Prep {};
     __device__ static void prep(const Raw &, int, Prep &) {}
+    template <class Src = SrcGlobal>
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
         uint32_t k = it * SPAN + tig * 16;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             if (k < w.cols) {
-                const uint8_t *p = w.q + ((size_t)(r0 + rr * 8) * w.cols + k) * 2;
-                R.q[rr][0] = ldg_stream(p);
-                R.q[rr][1] = ldg_stream(p + 16);
+                const uint8_t *p = w.q + (size_t)(r0 + rr * 8) * w.qs + (size_t)k * 2;
+                R.q[rr][0] = Src::ld16(p);
+                R.q[rr][1] = Src::ld16(p + 16);
             } else {
                 R.q[rr][0] = R.q[rr][1] = make_uint4(0, 0, 0, 0);
             }
@@ -390,6 +411,27 @@ struct KArgs {
     GemvPost post;
 };
 
+// Kernel arguments of a GEMV described by GemvArgs (host).
+inline KArgs make_kargs(const GemvArgs &a) {
+    KArgs k;
+    k.w = wview(*a.w);
+    if (a.w2) k.w2 = wview(*a.w2);
+    k.xq = a.xq;
+    k.kpad = xq_pad(a.w->cols);
+    k.xsum = a.xq ? xq_sums(a.xq, k.kpad) : nullptr;
+    k.y = a.y;
+    k.bias = a.bias;
+    k.xq_out = a.xq_out;
+    k.kpad_out = xq_pad(a.w->rows);
+    k.argmax64 = a.argmax64;
+    k.row_base = a.row_base;
+    k.ws = a.ws;
+    k.counters = a.counters;
+    k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
+    k.post = a.post;
+    return k;
+}
+
 __device__ __forceinline__ unsigned long long pack_argmax(float v, uint32_t idx) {
     uint32_t u = __float_as_uint(v);
     uint32_t key = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
@@ -410,78 +452,36 @@ __device__ void finish_step(StepState *st, const uint32_t *forced, uint32_t *out
     st->token = (s + 1 < st->n_forced) ? (int)forced[s + 1] : (int)idx;
 }
 
-// CTA of 4 warps = TPC = 4 / KW tiles of 16 rows, KW warps per tile splitting
-// the CTA's K range (iteration it goes to warp it % KW of the tile).  Each warp
-// keeps D iterations of loads in flight ahead of the one it computes.
-// One CTA's share of a GEMV: tile group bx, K split part by.  Returns false
-// for a CTA that published a split-K partial and is not the tile's last (its
-// epilogue ran elsewhere); true once the epilogue is done.
-template <class TT, int EPI, int KW, int D, bool GRIDDEP>
-__device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t by) {
-    // Dual (gate|up): one tile per CTA, warps 0-1 stream the gate rows and
-    // warps 2-3 the same rows of up (KW = 2 per matrix), so no warp holds both.
+// Shared memory of gemv_body, owned by the calling kernel so that the body's
+// instantiations share one copy.
+struct GemvShared {
+    float red[4][16];    // per-warp partial sums
+    float gu[4][32];     // EPI_SILU_XQ: gate and up values of a tile
+    float act16[4][16];  // EPI_SILU_XQ: activations of a tile
+    int is_last;
+};
+
+// Everything after a CTA's main loop: the cross-warp sum of the tile's rows,
+// the split-K reduction and the epilogue.  c / k0 / k1: this lane's MMA
+// accumulators and K-quant corrections.  Returns false for a CTA whose split-K
+// partial was not the tile's last.
+template <class TT, int EPI, int KW>
+__device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_t by, GemvShared &sh, float (&c)[4],
+                                            float k0, float k1) {
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
-    constexpr int TPC = DUAL ? 1 : 4 / KW;  // tiles per CTA
-    constexpr int KWE = DUAL ? 2 : KW;      // warps per tile and matrix
-    constexpr int NV = DUAL ? 32 : 16;      // values per tile (gate rows then up rows)
-    __shared__ float red[4][16];
-    __shared__ int is_last;
+    constexpr int TPC = DUAL ? 1 : 4 / KW;
+    constexpr int KWE = DUAL ? 2 : KW;
+    constexpr int NV = DUAL ? 32 : 16;
+    float(&red)[4][16] = sh.red;
+    int &is_last = sh.is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
-    const int lt = DUAL ? 0 : warp / KW, kw = warp % KWE;
-    const W &wm = (DUAL && warp >= 2) ? p.w2 : p.w;
     const uint32_t ntiles = p.w.rows / 16;
-    const uint32_t tile = bx * TPC + lt;
-    const bool active = tile < ntiles;
-    const uint32_t r0 = tile * 16 + g;
-    const int ni = (int)((p.w.cols + TT::SPAN - 1) / TT::SPAN);
-    const int per = (ni + p.ksplit - 1) / p.ksplit;
-    const int it0 = by * per, it1 = active ? min(ni, it0 + per) : it0;
-
-    // The weights do not depend on the previous kernel: start streaming the
-    // warp's first D iterations before waiting for the activation.
-    typename TT::Raw ring[D];
-#pragma unroll
-    for (int j = 0; j < D; j++) {
-        const int itj = it0 + kw + KWE * j;
-        if (itj < it1) TT::load(ring[j], wm, r0, itj, tig);
-    }
-    if (GRIDDEP) {
-        griddep_wait();
-        griddep_launch();
-    }
-
-    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);  // B fragments: L1-cached, shared by the SM's CTAs
-    const bool bl = g < 2;
-
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
-    float k0 = 0.f, k1 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
-    for (int base = it0 + kw; base < it1; base += KWE * D) {
-#pragma unroll
-        for (int j = 0; j < D; j++) {
-            const int it = base + KWE * j;
-            if (it >= it1) break;  // uniform across the warp
-            typename TT::Raw R = ring[j];
-            const int itn = it + KWE * D;
-            if (itn < it1) TT::load(ring[j], wm, r0, itn, tig);  // refill this slot while the iteration computes
-            typename TT::Prep P;
-            TT::prep(R, tig, P);
-#pragma unroll
-            for (int s = 0; s < TT::KSTEPS; s++) {
-                uint2 b = make_uint2(0u, 0u);
-                if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
-                uint32_t a[4];
-                TT::frag(R, P, s, a);
-                mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
-            }
-            if (TT::HAS_CORR) TT::correct(P, p.xsum, it, tig, k0, k1);
-        }
-    }
     if (TT::HAS_CORR) {  // the four lanes of a row hold different sub-blocks: sum them
 #pragma unroll
-        for (int sh = 1; sh <= 2; sh <<= 1) {
-            k0 += __shfl_xor_sync(0xffffffffu, k0, sh);
-            k1 += __shfl_xor_sync(0xffffffffu, k1, sh);
+        for (int o = 1; o <= 2; o <<= 1) {
+            k0 += __shfl_xor_sync(0xffffffffu, k0, o);
+            k1 += __shfl_xor_sync(0xffffffffu, k1, o);
         }
     }
     if (tig == 0) {
@@ -523,8 +523,8 @@ __device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t 
         if (t == 0) p.counters[bx] = 0u;
     }
     if (EPI == EPI_SILU_XQ) {
-        __shared__ float gu[TPC][32];
-        __shared__ float act16[TPC][16];
+        float(&gu)[4][32] = sh.gu;
+        float(&act16)[4][16] = sh.act16;
         if (own) gu[tl][vi] = v;
         __syncthreads();
         if (own && vi < 16) {
@@ -560,7 +560,7 @@ __device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t 
                 p.y[row] = v;
             } else if (EPI == EPI_ADD) {
                 if (p.bias) v = v + p.bias[row];
-                p.y[row] = p.y[row] + v;
+                p.y[row] = __ldcg(p.y + row) + v;  // residual written by other CTAs
             }
         }
         if (EPI == EPI_ARGMAX) {
@@ -579,6 +579,76 @@ __device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t 
         }
     }
     return true;
+}
+
+// CTA of 4 warps = TPC = 4 / KW tiles of 16 rows, KW warps per tile splitting
+// the CTA's K range (iteration it goes to warp it % KW of the tile).  Each warp
+// keeps D iterations of loads in flight ahead of the one it computes.
+// One CTA's share of a GEMV: tile group bx, K split part by.  `before_x()` is
+// called by every thread once the first weight loads are in flight and before
+// anything written by earlier work (the activation) is read: the standalone
+// kernel waits there for its predecessor (PDL), the persistent decode kernel
+// for its grid barrier.  Returns false for a CTA that published a split-K
+// partial and is not the tile's last (its epilogue ran elsewhere); true once
+// the epilogue is done.
+
+template <class TT, int EPI, int KW, int D, class BeforeX>
+__device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t by, GemvShared &sh,
+                                          BeforeX &&before_x) {
+    // Dual (gate|up): one tile per CTA, warps 0-1 stream the gate rows and
+    // warps 2-3 the same rows of up (KW = 2 per matrix), so no warp holds both.
+    constexpr bool DUAL = (EPI == EPI_SILU_XQ);
+    constexpr int TPC = DUAL ? 1 : 4 / KW;  // tiles per CTA
+    constexpr int KWE = DUAL ? 2 : KW;      // warps per tile and matrix
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, tig = lane & 3;
+    const int lt = DUAL ? 0 : warp / KW, kw = warp % KWE;
+    const W &wm = (DUAL && warp >= 2) ? p.w2 : p.w;
+    const uint32_t ntiles = p.w.rows / 16;
+    const uint32_t tile = bx * TPC + lt;
+    const bool active = tile < ntiles;
+    const uint32_t r0 = tile * 16 + g;
+    const int ni = (int)((p.w.cols + TT::SPAN - 1) / TT::SPAN);
+    const int per = (ni + p.ksplit - 1) / p.ksplit;
+    const int it0 = by * per, it1 = active ? min(ni, it0 + per) : it0;
+
+    // The weights do not depend on the previous kernel: start streaming the
+    // warp's first D iterations before waiting for the activation.
+    typename TT::Raw ring[D];
+#pragma unroll
+    for (int j = 0; j < D; j++) {
+        const int itj = it0 + kw + KWE * j;
+        if (itj < it1) TT::load(ring[j], wm, r0, itj, tig);
+    }
+    before_x();
+
+    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);  // B fragments: L1-cached, shared by the SM's CTAs
+    const bool bl = g < 2;
+
+    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    float k0 = 0.f, k1 = 0.f;  // fp32 corrections (rows r0, r0+8), K-quants only
+    for (int base = it0 + kw; base < it1; base += KWE * D) {
+#pragma unroll
+        for (int j = 0; j < D; j++) {
+            const int it = base + KWE * j;
+            if (it >= it1) break;  // uniform across the warp
+            typename TT::Raw R = ring[j];
+            const int itn = it + KWE * D;
+            if (itn < it1) TT::load(ring[j], wm, r0, itn, tig);  // refill this slot while the iteration computes
+            typename TT::Prep P;
+            TT::prep(R, tig, P);
+#pragma unroll
+            for (int s = 0; s < TT::KSTEPS; s++) {
+                uint2 b = make_uint2(0u, 0u);
+                if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, s));
+                uint32_t a[4];
+                TT::frag(R, P, s, a);
+                mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
+            }
+            if (TT::HAS_CORR) TT::correct(P, p.xsum, it, tig, k0, k1);
+        }
+    }
+    return gemv_finish<TT, EPI, KW>(p, bx, by, sh, c, k0, k1);
 }
 
 }  // namespace

@@ -208,6 +208,14 @@ static int enqueue_step(cuq_model *m) {
 }
 
 static int run_steps(cuq_model *m, uint32_t n) {
+    if (m->mega.impl) {
+        if (n == 0) return CUQ_OK;
+        int rc = mega_launch(m->mega, n, m->stream);
+        if (rc) return rc;
+        m->mega_ran = true;
+        m->stats.kernel_launches += 1;
+        return CUQ_OK;
+    }
     for (uint32_t i = 0; i < n; i++) {
         if (m->graph_exec) {
             CUQ_CUDA_TRY(cudaGraphLaunch(m->graph_exec, m->stream));
@@ -491,6 +499,8 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
         if (cudaMalloc(&m->forced, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
         if (cudaMalloc(&m->out_tokens, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
         if (cudaMallocHost(&m->out_host, sizeof(uint32_t) * (o.max_seq + 1)) != cudaSuccess) break;
+        if (cudaMallocHost(&m->err_host, sizeof(int)) != cudaSuccess) break;
+        *m->err_host = 0;
         {
             const size_t C = o.max_chunk;
             const size_t wide = c.hidden > qd ? c.hidden : qd;
@@ -689,6 +699,82 @@ int cuq_upload_f32(cuq_model *m, int layer, int role, const float *v, size_t n) 
     return CUQ_OK;
 }
 
+// The decode step as a persistent-kernel program: the phases enqueue_step
+// launches as kernels, with the RMSNorms folded into the GEMV phases that
+// consume them and the embedding into the first.
+static int build_mega(cuq_model *m) {
+    const cuq_config &c = m->cfg, &lc = m->lc;
+    MegaStepSpec sp;
+    sp.embed = &m->embed.p;
+    sp.x = m->x;
+    sp.hidden = c.hidden;
+    sp.eps = c.eps;
+    sp.state = m->state;
+    sp.forced = m->forced;
+    sp.out_tokens = m->out_tokens;
+    if (m->opt.tp_size > 1) {
+        set_error("persistent decode: single GPU only");
+        return CUQ_EUNSUPPORTED;
+    }
+    auto seg = [](const Planes &w, const __half *xq, float *y, const float *bias, int epi) {
+        MegaSegSpec g;
+        g.a.w = &w;
+        g.a.xq = xq;
+        g.a.y = y;
+        g.a.bias = bias;
+        g.epi = epi;
+        return g;
+    };
+    for (uint32_t l = 0; l < c.layers; l++) {
+        Layer &L = m->layers[l];
+        if (!L.gate_up_dual) {
+            set_error("persistent decode: layer %u gate and up differ in type", l);
+            return CUQ_EUNSUPPORTED;
+        }
+        MegaPhaseSpec q;
+        q.norm_w = L.attn_norm;
+        q.embed = l == 0;
+        for (auto &sg : L.qkv)
+            q.segs.push_back(seg(sg.p, nullptr, m->qkv + sg.row_off, L.qkv_bias ? L.qkv_bias + sg.row_off : nullptr,
+                                 EPI_STORE));
+        sp.phases.push_back(q);
+        MegaPhaseSpec at;
+        at.kind = MEGA_ATTN;
+        at.attn.qkv = m->qkv;
+        at.attn.cs = m->rope_cs;
+        at.attn.k_cache = L.k_cache;
+        at.attn.v_cache = L.v_cache;
+        at.attn.cache_stride = m->opt.max_seq;
+        at.attn.heads = lc.heads;
+        at.attn.kv_heads = lc.kv_heads;
+        at.attn.hd = c.head_dim;
+        at.attn.adjacent = c.rope_adjacent;
+        at.attn.nsplit = m->attn_nsplit;
+        at.attn.xq = m->xq_attn;
+        sp.phases.push_back(at);
+        MegaPhaseSpec o;
+        o.segs.push_back(seg(L.o.p, m->xq_attn, m->x, L.o_bias, EPI_ADD));
+        sp.phases.push_back(o);
+        MegaPhaseSpec gu;
+        gu.norm_w = L.ffn_norm;
+        MegaSegSpec g = seg(L.gate.p, nullptr, nullptr, nullptr, EPI_SILU_XQ);
+        g.a.w2 = &L.up.p;
+        g.a.xq_out = m->xq_act;
+        gu.segs.push_back(g);
+        sp.phases.push_back(gu);
+        MegaPhaseSpec dn;
+        dn.segs.push_back(seg(L.down.p, m->xq_act, m->x, nullptr, EPI_ADD));
+        sp.phases.push_back(dn);
+    }
+    MegaPhaseSpec hd;
+    hd.norm_w = m->final_norm;
+    MegaSegSpec h = seg(head_proj(m).p, nullptr, m->logits, nullptr, EPI_ARGMAX);
+    h.a.row_base = m->vocab_base;
+    hd.segs.push_back(h);
+    sp.phases.push_back(hd);
+    return mega_build(sp, m->sm_count, m->opt.persistent_ctas, m->mega);
+}
+
 int cuq_model_finalize(cuq_model *m) {
     CUQ_CHECK_ARG(m, "cuq_model_finalize: null model");
     if (m->finalized) return CUQ_OK;
@@ -797,7 +883,14 @@ int cuq_model_finalize(cuq_model *m) {
     (void)qd;
     (void)kvd;
     m->finalized = true;
-    if (m->opt.use_graphs) {
+    if (m->opt.decode_kernel == CUQ_DECODE_PERSISTENT) {
+        rc = build_mega(m);
+        if (rc != CUQ_OK) {
+            m->finalized = false;
+            return rc;
+        }
+    }
+    if (m->opt.use_graphs && !m->mega.impl) {
         CUQ_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal));
         rc = enqueue_step(m);
         cudaGraph_t g = nullptr;
@@ -865,6 +958,12 @@ int cuq_model_get_config(const cuq_model *m, cuq_config *out) {
 
 static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint32_t *argmax_out, double *ms_out) {
     CUQ_CUDA_TRY(cudaEventRecord(m->ev1, m->stream));
+    const bool mega_ran = m->mega_ran;
+    m->mega_ran = false;
+    if (mega_ran) {
+        int rc = mega_err_copy(m->mega, m->err_host, m->stream);
+        if (rc) return rc;
+    }
     if (logits_host)
         CUQ_CUDA_TRY(cudaMemcpyAsync(logits_host, m->logits, sizeof(float) * m->lc.vocab, cudaMemcpyDeviceToHost,
                                      m->stream));
@@ -876,6 +975,10 @@ static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint3
     cudaEventElapsedTime(&ms, m->ev0, m->ev1);
     if (ms_out) *ms_out += ms;
     if (argmax_out && n_steps) *argmax_out = m->out_host[n_steps - 1];
+    if (mega_ran && *m->err_host) {
+        set_error("persistent decode: a grid barrier was not reached within its wait limit");
+        return CUQ_ETIMEOUT;
+    }
     if (m->tp_err) {
         int herr = 0;
         CUQ_CUDA_TRY(cudaMemcpy(&herr, m->tp_err, sizeof(int), cudaMemcpyDeviceToHost));
@@ -1015,6 +1118,7 @@ int cuq_reset(cuq_model *m) {
 int cuq_model_stats(const cuq_model *m, cuq_stats *out) {
     CUQ_CHECK_ARG(m && out, "cuq_model_stats: null argument");
     *out = m->stats;
+    out->persistent_ctas = m->mega.impl ? (uint64_t)m->mega.grid : 0;
     return CUQ_OK;
 }
 
@@ -1055,6 +1159,8 @@ void cuq_model_free(cuq_model *m) {
     if (m->tp_buf) cudaFree(m->tp_buf);
     if (m->state_host) cudaFreeHost(m->state_host);
     if (m->out_host) cudaFreeHost(m->out_host);
+    if (m->err_host) cudaFreeHost(m->err_host);
+    mega_free(m->mega);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
     if (m->stream) cudaStreamDestroy(m->stream);

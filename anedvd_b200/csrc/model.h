@@ -4,6 +4,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "mega.h"
 
 namespace cuq {
 
@@ -75,6 +76,10 @@ struct cuq_model {
     int *tp_err = nullptr;                       // wait time-outs (device)
     unsigned int *tp_done = nullptr;             // grid completion of the prefill reduce kernel
     float *pf_part = nullptr;                    // [max_chunk][hidden] partial of o / down
+
+    cuq::MegaProgram mega;                       // persistent decode kernel (decode_kernel != PER_OP)
+    bool mega_ran = false;                       // launched since the last finish_call
+    int *err_host = nullptr;                     // pinned: its error flag read back by finish_call
 
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;

@@ -124,7 +124,8 @@ __global__ void __launch_bounds__(128) attn_decode_kernel(const float *__restric
     }
     attn_walk<HD, G>(qr, kc + (size_t)kvh * cache_stride * HD, vc + (size_t)kvh * cache_stride * HD, r.p0, r.p1,
                      warp, lp, pg, m, l, o);
-    attn_store_split<HD, G>(m, l, o, warp, lp, pg, part, split, nsplit, heads, kvh);
+    __shared__ float scr[attn_store_floats(HD, G)];
+    attn_store_split<HD, G>(m, l, o, warp, lp, pg, part, split, nsplit, heads, kvh, scr);
 }
 
 // Merge for the standalone decode attention: CTA per query head.
@@ -133,15 +134,19 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const float *__restri
                                                             const int *pos_ptr, uint32_t n_val, uint32_t heads,
                                                             float *out, __half *xq, uint32_t kpad) {
     __shared__ float res[HD];
+    __shared__ float scr[attn_merge_floats(1)];
     const uint32_t n = pos_ptr ? (uint32_t)(*pos_ptr) + 1u : n_val;
     const SplitRange r = split_range(n, nsplit, 0);
-    attn_merge<HD, 1>(part, nsplit, r.nact, heads, blockIdx.x, res);
+    attn_merge<HD, 1>(part, nsplit, r.nact, heads, blockIdx.x, res, scr);
     attn_emit(res, HD, blockIdx.x * HD, out, xq, kpad);
 }
 
 template <int HD, int G>
 __global__ void __launch_bounds__(128) attn_step_kernel(const AttnStepArgs p) {
-    attn_step_body<HD, G, true>(p, blockIdx.x, blockIdx.y);
+    griddep_wait();
+    griddep_launch();
+    __shared__ __align__(16) float scr[attn_step_floats(HD, G)];
+    attn_step_body<HD, G>(p, blockIdx.x, blockIdx.y, (uint32_t)p.state->pos, scr);
 }
 
 // ------------------------------------------------------ prefill helpers --

@@ -85,6 +85,8 @@ __device__ __forceinline__ float tp_sum(const TpComm &t, int ph, size_t i) {
 // read from global memory once; loads are issued four float4 at a time per
 // thread, so the post-op costs a few memory round trips, not one per element.
 constexpr uint32_t RN_MAX = 8192;
+__device__ __forceinline__ void stage_norm_xq(const float4 *stage, float ss, const float *w, uint32_t n, float eps,
+                                              __half *xq, uint32_t kpad);
 __device__ __forceinline__ void reduce_norm_xq_block(float *x, const TpComm *tp, int ph, const float *bias,
                                                      const float *w, uint32_t n, float eps, __half *xq,
                                                      uint32_t kpad, float4 *stage) {
@@ -143,6 +145,15 @@ __device__ __forceinline__ void reduce_norm_xq_block(float *x, const TpComm *tp,
             ss += (v[k].x * v[k].x + v[k].y * v[k].y) + (v[k].z * v[k].z + v[k].w * v[k].w);
         }
     }
+    stage_norm_xq(stage, ss, w, n, eps, xq, kpad);
+}
+
+// Second half of the above, for x already staged in shared memory: `ss` is
+// this thread's share of sum(x^2) (any split of the elements across threads).
+__device__ __forceinline__ void stage_norm_xq(const float4 *stage, float ss, const float *w, uint32_t n, float eps,
+                                              __half *xq, uint32_t kpad) {
+    const int t = threadIdx.x, B = blockDim.x;
+    const uint32_t n4 = n / 4;
     __shared__ float part[32];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);

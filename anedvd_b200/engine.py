@@ -32,10 +32,12 @@ class Engine:
         self.vocab_base = self.local_vocab * tp_rank
 
     @classmethod
-    def from_gguf(cls, path, max_seq=2048, use_graphs=True, device=0, max_chunk=512):
+    def from_gguf(cls, path, max_seq=2048, use_graphs=True, device=0, max_chunk=512, decode_kernel=rt.DECODE_AUTO,
+                  persistent_ctas=0):
         L = rt.load()
         rt.init(device)
-        opts = rt.CuqOptions(max_seq=max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs), tp_rank=0, tp_size=1)
+        opts = rt.CuqOptions(max_seq=max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs), tp_rank=0, tp_size=1,
+                             decode_kernel=decode_kernel, persistent_ctas=persistent_ctas)
         h = L.cuq_model_load_gguf(path.encode(), ctypes.byref(opts))
         if not h:
             raise rt.CuqError(rt.EINVAL, rt.last_error())
@@ -45,7 +47,7 @@ class Engine:
 
     @classmethod
     def from_synth(cls, model, max_seq=None, use_graphs=True, device=0, max_chunk=512, tp_rank=0, tp_size=1,
-                   exchange=None):
+                   exchange=None, decode_kernel=rt.DECODE_AUTO, persistent_ctas=0):
         """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads).
 
         Tensor parallel (tp_size > 1, one process per GPU): every rank uploads
@@ -59,7 +61,8 @@ class Engine:
                            head_dim=c.head_dim, inter=c.inter, vocab=c.vocab, eps=c.eps, rope_theta=c.rope_theta,
                            rope_adjacent=int(c.rope_adjacent), tie_embeddings=int(c.tie_embeddings))
         opts = rt.CuqOptions(max_seq=max_seq or c.max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs),
-                             tp_rank=tp_rank, tp_size=tp_size)
+                             tp_rank=tp_rank, tp_size=tp_size, decode_kernel=decode_kernel,
+                             persistent_ctas=persistent_ctas)
         h = L.cuq_model_create(ctypes.byref(cfg), ctypes.byref(opts))
         if not h:
             raise rt.CuqError(rt.EINVAL, rt.last_error())
@@ -133,6 +136,11 @@ class Engine:
         s = rt.CuqStats()
         rt.check(rt.load().cuq_model_stats(self._h, ctypes.byref(s)))
         return s
+
+    @property
+    def persistent_ctas(self):
+        """CTAs of the persistent decode kernel (0: decode runs one kernel per op)."""
+        return int(self.stats.persistent_ctas)
 
     @property
     def stream(self):

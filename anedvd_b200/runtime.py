@@ -74,14 +74,18 @@ class CuqConfig(ctypes.Structure):
 
 class CuqOptions(ctypes.Structure):
     _fields_ = [("max_seq", U32), ("max_chunk", U32), ("use_graphs", ctypes.c_int32),
-                ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32)]
+                ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32),
+                ("decode_kernel", ctypes.c_int32), ("persistent_ctas", ctypes.c_int32)]
+
+
+DECODE_AUTO, DECODE_PER_OP, DECODE_PERSISTENT = 0, 1, 2
 
 
 class CuqStats(ctypes.Structure):
     _fields_ = [("tokens", U64), ("prefill_tokens", U64), ("decode_ms", ctypes.c_double),
                 ("prefill_ms", ctypes.c_double), ("weight_bytes", U64), ("kv_bytes", U64),
                 ("graph_replays", U64), ("kernels_per_step", U64),
-                ("kernel_launches", U64)]
+                ("kernel_launches", U64), ("persistent_ctas", U64)]
 
 
 class CuqError(RuntimeError):

@@ -75,6 +75,9 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default=None, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--decode-kernel", choices=["auto", "per_op", "persistent"], default="auto",
+                    help="decode steps in one persistent kernel (auto: when the model allows) or one kernel per op")
+    ap.add_argument("--persistent-ctas", type=int, default=0, help="CTAs per SM of the persistent kernel (0 = max)")
     ap.add_argument("--profile", choices=["gemv", "qgemm"], default=None,
                     help="run only the roofline kernel (a few launches) for an ncu capture, print nothing")
     return ap.parse_args()
@@ -291,8 +294,11 @@ def run_ours(args, world, rank, local):
         dist.all_gather_object(out, h)
         return out
 
+    dk = {"auto": 0, "per_op": 1, "persistent": 2}[args.decode_kernel]
     eng = E.Engine.from_synth(model, max_seq=max_seq, device=local, max_chunk=2048,
-                              tp_rank=rank if tp else 0, tp_size=world if tp else 1, exchange=exchange)
+                              tp_rank=rank if tp else 0, tp_size=world if tp else 1, exchange=exchange,
+                              decode_kernel=dk, persistent_ctas=args.persistent_ctas)
+    persistent = eng.persistent_ctas > 0
     stream_ptr = eng.stream
     stream = torch.cuda.ExternalStream(stream_ptr)
     ids = prompt_ids(model.cfg.vocab, n_prompt)
@@ -367,6 +373,8 @@ def run_ours(args, world, rank, local):
             "data": DATA[C["payload"]],
             "config": {"workload": C["desc"], "model": C["model"], "prompt": n_prompt, "decode": n_decode,
                        "parallelism": parallelism,
+                       "decode_kernel": ("persistent, %d CTAs" % eng.persistent_ctas) if persistent else
+                                        "one kernel per op (CUDA graph per step)",
                        "l2": "flushed between steps (256 MB write); weights %.1f MB" % (wbytes / 1e6)},
             "prefill": {"tok_per_s": prefill_tps, "ms": pre_ms_max / args.steps},
             "weight_bytes_per_token": wbytes,
@@ -375,7 +383,7 @@ def run_ours(args, world, rank, local):
                     "d2h_bytes_per_step": 4 * n_decode},
             "roofline": roof, "peak_kind": pk_kind, "cpu_baseline": cpu,
             "gpu_launches": int(launches),
-            "kernels_per_token": int(kps),
+            "kernels_per_token": (1.0 / n_decode) if persistent else int(kps),
             "clocks": clk,
         }
         print(json.dumps(line), flush=True)

@@ -166,7 +166,20 @@ typedef struct {
     int32_t use_graphs;      /* capture the decode step in a CUDA graph (default 1) */
     int32_t tp_rank, tp_size;/* tensor parallel slot (tp_size 1 = single GPU; up to 8, one
                               * process per GPU; see cuq_tp_connect) */
+    int32_t decode_kernel;   /* CUQ_DECODE_*: how decode steps run (default AUTO) */
+    int32_t persistent_ctas; /* CTAs per SM of the persistent decode kernel; 0 = as many as fit */
 } cuq_options;
+
+/* decode_kernel: PER_OP (and AUTO, the default) runs one kernel per op,
+ * captured in a CUDA graph when use_graphs; PERSISTENT runs every decode step
+ * of a call in one persistent cooperative kernel with grid-wide barriers
+ * between the phases (single GPU, gate/up of one type, hidden <= 8192;
+ * cuq_model_finalize fails when the model does not allow it).  On B200 the
+ * per-op path with programmatic dependent launch is the faster of the two for
+ * the BASELINE configs, so AUTO picks it. */
+#define CUQ_DECODE_AUTO 0
+#define CUQ_DECODE_PER_OP 1
+#define CUQ_DECODE_PERSISTENT 2
 
 /* Tensor roles for cuq_upload_*. */
 #define CUQ_ROLE_Q 0
@@ -199,6 +212,7 @@ typedef struct {
     uint64_t graph_replays;
     uint64_t kernels_per_step; /* kernel launches in one decode step */
     uint64_t kernel_launches;  /* all kernels this model has launched (graph nodes counted) */
+    uint64_t persistent_ctas;  /* CTAs of the persistent decode kernel; 0 when decode runs per op */
 } cuq_stats;
 
 /* Engine.init (engine.zig:320-521) without weights: allocates the KV cache and

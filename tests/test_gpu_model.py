@@ -32,11 +32,12 @@ def _margin_ok(logits, tol):
     return (top[1] - top[0]) > tol * np.max(np.abs(logits))
 
 
-def _compare(model, n_prompt, n_decode, threads=8, use_graphs=True, max_chunk=512):
+def _compare(model, n_prompt, n_decode, threads=8, use_graphs=True, max_chunk=512, decode_kernel=rt.DECODE_AUTO):
     cfg = model.cfg
     ref = orc.Model(cfg, threads=threads, max_seq=n_prompt + n_decode + 1)
     ref.load(model)
-    eng = E.Engine.from_synth(model, max_seq=n_prompt + n_decode + 1, use_graphs=use_graphs, max_chunk=max_chunk)
+    eng = E.Engine.from_synth(model, max_seq=n_prompt + n_decode + 1, use_graphs=use_graphs, max_chunk=max_chunk,
+                              decode_kernel=decode_kernel)
     ids = _prompt(cfg, n_prompt)
     errs = []
     # prefill: the reference's CPU path feeds the prompt token by token (main.zig:1255-1262)
@@ -60,10 +61,36 @@ def _compare(model, n_prompt, n_decode, threads=8, use_graphs=True, max_chunk=51
     return max(errs)
 
 
+DECODE = [("per_op", rt.DECODE_PER_OP), ("persistent", rt.DECODE_PERSISTENT)]
+
+
+@pytest.mark.parametrize("dk", [d[1] for d in DECODE], ids=[d[0] for d in DECODE])
 @pytest.mark.parametrize("name,kw", SMALL, ids=[s[0] for s in SMALL])
-def test_small_models_match_reference(name, kw):
-    e = _compare(synth.model(name, **kw), n_prompt=9, n_decode=6)
+def test_small_models_match_reference(name, kw, dk):
+    e = _compare(synth.model(name, **kw), n_prompt=9, n_decode=6, decode_kernel=dk)
     assert e < LOGIT_TOL, e
+
+
+@pytest.mark.parametrize("name,kw", SMALL, ids=[s[0] for s in SMALL])
+def test_persistent_generate_equals_single_steps(name, kw):
+    """One persistent launch over many steps takes the same tokens as one launch
+    per step, and as the per-op kernels wherever the oracle margin is clear."""
+    m = synth.model(name, **kw)
+    ids = _prompt(m.cfg, 6, salt=3)
+    eng = E.Engine.from_synth(m, max_seq=64, decode_kernel=rt.DECODE_PERSISTENT)
+    gen = list(E.Session(eng, 64).generate(ids, 20))
+    eng.reset()
+    _, am = eng.prefill(ids)
+    steps = [am]
+    for s in range(19):
+        _, am = eng.forward(steps[-1], len(ids) + s)
+        steps.append(am)
+    assert gen == steps
+    eng.close()
+    per_op = E.Engine.from_synth(m, max_seq=64, decode_kernel=rt.DECODE_PER_OP)
+    gen2 = list(E.Session(per_op, 64).generate(ids, 20))
+    per_op.close()
+    assert gen2 == gen
 
 
 def test_smollm2_full_size_matches_reference():
