@@ -215,39 +215,58 @@ struct TQ4K {
             R.meta[rr] = *reinterpret_cast<const uint4 *>(w.s + ((size_t)it * w.rows + r) * 16);
         }
     }
+    // get_scale_min_k4 (gguf.zig:960-973) for this lane's sub-blocks j0 = 2*tig and
+    // j0 + 1, all four 6-bit fields at once: V = [sc(j0), sc(j0+1), m(j0), m(j0+1)]
+    // as bytes.  Scale bytes b0..b11 are the words y, z, w of the record.
+    //   j < 4 : sc = b[j] & 63,                        m = b[j+4] & 63
+    //   j >= 4: sc = (b[j+4] & 15) | (b[j-4] >> 6) << 4, m = (b[j+4] >> 4) | (b[j] >> 6) << 4
+    __device__ static uint32_t scale_bytes(const uint4 &meta, int tig) {
+        const bool lo = tig < 2;
+        const uint32_t j0 = 2u * tig, j1 = j0 + 1u;
+        const uint32_t selA = lo ? (j0 | j1 << 4 | (j0 + 4u) << 8 | (j1 + 4u) << 12)
+                                 : ((j0 - 4u) | (j1 - 4u) << 4 | (j0 - 4u) << 8 | (j1 - 4u) << 12);
+        const uint32_t a = __byte_perm(lo ? meta.y : meta.w, lo ? meta.z : meta.w, selA);
+        const uint32_t a2 = __byte_perm(a, a >> 4, lo ? 0x3210u : 0x7610u);  // m bytes: high nibbles
+        const uint32_t b = __byte_perm(meta.y, meta.z, (j0 - 4u) | (j1 - 4u) << 4 | j0 << 8 | j1 << 12);
+        const uint32_t hb = (b >> 2) & (lo ? 0u : 0x30303030u);  // (x >> 6) << 4 in every byte
+        return (a2 & (lo ? 0x3F3F3F3Fu : 0x0F0F0F0Fu)) | hb;
+    }
     __device__ static void prep(const Raw &R, int tig, Prep &P) {
+        const __half2 k1024 = __float2half2_rn(1024.f);
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             const uint4 meta = R.meta[rr];
-            P.d[rr] = __half2half2(__ushort_as_half((uint16_t)(meta.x & 0xFFFF)));
-            const float dmin = __half2float(__ushort_as_half((uint16_t)(meta.x >> 16)));
-#pragma unroll
-            for (int part = 0; part < 2; part++) {
-                // get_scale_min_k4 (gguf.zig:960-973) for sub-block j = 2*tig + part,
-                // from the 12 scale bytes held as words y, z, w (runtime shifts, so
-                // the lane-dependent byte index never touches local memory)
-                const int j = 2 * tig + part, sh = 8 * (j & 3);
-                const uint32_t b0 = (meta.y >> sh) & 0xFFu, b1 = (meta.z >> sh) & 0xFFu, b2 = (meta.w >> sh) & 0xFFu;
-                const int sc = j < 4 ? (int)(b0 & 63u) : (int)((b2 & 0xFu) | ((b0 >> 6) << 4));
-                const int mm = j < 4 ? (int)(b1 & 63u) : (int)((b2 >> 4) | ((b1 >> 6) << 4));
-                P.sc[rr][part] = __float2half2_rn((float)sc);
-                P.csc[rr][part] = __float2half2_rn(-1024.f * (float)sc);  // exact: |1024*63| < 65504
-                const float m1 = dmin * (float)mm;                         // exact in fp32
-                const __half m1h = __float2half_rn(m1);
-                P.nm1[rr][part] = __half2half2(__hneg(m1h));
-                P.m1[rr][part] = m1 - __half2float(m1h);                   // remainder, exact
-            }
+            const uint32_t v = scale_bytes(meta, tig);
+            P.d[rr] = u2h(__byte_perm(meta.x, 0u, 0x1010u));
+            const __half2 dmin2 = u2h(__byte_perm(meta.x, 0u, 0x3232u));
+            // small integers as fp16 through the 0x64 exponent byte: 1024 + field
+            const __half2 sc0 = __hsub2(u2h(__byte_perm(v, 0x64646464u, 0x4040u)), k1024);
+            const __half2 sc1 = __hsub2(u2h(__byte_perm(v, 0x64646464u, 0x4141u)), k1024);
+            const __half2 mm = __hsub2(u2h(__byte_perm(v, 0x64646464u, 0x4342u)), k1024);  // (m0, m1)
+            // part 0 reads 1024 + q (low nibbles), part 1 1024 + 16 q (high
+            // nibbles in place): fma(x, sc', c') = q * sc exactly in both
+            P.sc[rr][0] = sc0;
+            P.csc[rr][0] = __hmul2(sc0, __float2half2_rn(-1024.f));
+            P.sc[rr][1] = __hmul2(sc1, __float2half2_rn(0.0625f));
+            P.csc[rr][1] = __hmul2(sc1, __float2half2_rn(-64.f));
+            const __half2 m1h = __hmul2(dmin2, mm);  // RN16(dmin * m), both sub-blocks
+            P.nm1[rr][0] = __hneg2(__low2half2(m1h));
+            P.nm1[rr][1] = __hneg2(__high2half2(m1h));
+            const float dmin = __low2float(dmin2);
+            const float2 mf = __half22float2(mm), m1f = __half22float2(m1h);
+            P.m1[rr][0] = fmaf(dmin, mf.x, -m1f.x);  // m1 - m1h, exact
+            P.m1[rr][1] = fmaf(dmin, mf.y, -m1f.y);
         }
     }
     // k-step s: word i = s & 7 of the group, part = s >> 3 (low nibbles, then high).
     __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
         const int i = s & 7, part = s >> 3;
+        const uint32_t mask = part ? 0x00F000F0u : 0x000F000Fu;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
-            uint32_t u = TQ8_0::word(R.q[rr][i >> 2], i & 3);
-            uint32_t v02 = part ? (u >> 4) : u, v13 = part ? (u >> 12) : (u >> 8);
-            __half2 q02 = __hfma2(u2h(magic(v02, 0x000F000Fu)), P.sc[rr][part], P.csc[rr][part]);  // q*sc
-            __half2 q13 = __hfma2(u2h(magic(v13, 0x000F000Fu)), P.sc[rr][part], P.csc[rr][part]);
+            const uint32_t u = TQ8_0::word(R.q[rr][i >> 2], i & 3);
+            __half2 q02 = __hfma2(u2h(magic(u, mask)), P.sc[rr][part], P.csc[rr][part]);  // q*sc
+            __half2 q13 = __hfma2(u2h(magic(u >> 8, mask)), P.sc[rr][part], P.csc[rr][part]);
             a[rr] = h2u(__hfma2(q02, P.d[rr], P.nm1[rr][part]));  // RN16(d1*q - m1h)
             a[rr + 2] = h2u(__hfma2(q13, P.d[rr], P.nm1[rr][part]));
         }
