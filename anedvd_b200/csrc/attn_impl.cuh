@@ -298,16 +298,15 @@ struct AttnStepArgs {
 
 template <int HD>
 __device__ __forceinline__ float rope_elem(const float *v, uint32_t d, const float *csr, int adjacent) {
-    // rotated element d of one head vector `v` (cpu.zig:33-36 / 57-60); v was
-    // written by other CTAs, so it is read through L2
+    // rotated element d of one head vector `v` (cpu.zig:33-36 / 57-60)
     constexpr uint32_t half = HD / 2;
     if (adjacent) {
         uint32_t j = d >> 1;
-        float a = __ldcg(v + 2 * j), b = __ldcg(v + 2 * j + 1), c = csr[j], s = csr[half + j];
+        float a = v[2 * j], b = v[2 * j + 1], c = csr[j], s = csr[half + j];
         return (d & 1) ? __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c)) : __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s));
     }
     uint32_t i = d < half ? d : d - half;
-    float a = __ldcg(v + i), b = __ldcg(v + i + half), c = csr[i], s = csr[half + i];
+    float a = v[i], b = v[i + half], c = csr[i], s = csr[half + i];
     return d < half ? __fsub_rn(__fmul_rn(a, c), __fmul_rn(b, s)) : __fadd_rn(__fmul_rn(a, s), __fmul_rn(b, c));
 }
 
@@ -334,7 +333,7 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
             const float *vin = p.qkv + qd + kvd + (size_t)kvh * HD;
             for (uint32_t d = threadIdx.x; d < HD; d += blockDim.x) {
                 kh[(size_t)pos * HD + d] = __float2half_rn(rope_elem<HD>(kin, d, csr, p.adjacent));
-                vh[(size_t)pos * HD + d] = __float2half_rn(__ldcg(vin + d));
+                vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
             }
         }
         float qr[G][E];

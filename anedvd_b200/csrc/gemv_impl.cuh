@@ -579,7 +579,7 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
                 p.y[row] = v;
             } else if (EPI == EPI_ADD) {
                 if (p.bias) v = v + p.bias[row];
-                p.y[row] = __ldcg(p.y + row) + v;  // residual written by other CTAs
+                p.y[row] = p.y[row] + v;
             }
         }
         if (EPI == EPI_ARGMAX) {

@@ -78,7 +78,7 @@ def parse():
     ap.add_argument("--decode-kernel", choices=["auto", "per_op", "persistent"], default="auto",
                     help="decode steps in one persistent kernel (auto: when the model allows) or one kernel per op")
     ap.add_argument("--persistent-ctas", type=int, default=0, help="CTAs per SM of the persistent kernel (0 = max)")
-    ap.add_argument("--profile", choices=["gemv", "qgemm"], default=None,
+    ap.add_argument("--profile", choices=["gemv", "qgemm", "prefill", "decode"], default=None,
                     help="run only the roofline kernel (a few launches) for an ncu capture, print nothing")
     return ap.parse_args()
 
@@ -392,8 +392,10 @@ def run_ours(args, world, rank, local):
 
 
 def profile_case(args):
-    """A handful of launches of the roofline kernel alone (6 launches), for
-    `ncu -k regex:gemv_kernel -s 3 -c 1`; nothing printed."""
+    """Small launch sets for ncu, nothing printed: gemv = the roofline kernel
+    alone (6 launches, `ncu -k regex:gemv_kernel -s 3 -c 1`); qgemm = one
+    prefill GEMM (4 launches); prefill / decode = the config's model end to end
+    (launch lists)."""
     import torch
     from anedvd_b200 import runtime as rt
     from anedvd_b200 import synth
@@ -419,6 +421,20 @@ def profile_case(args):
         for _ in range(4):
             rt.check(L.cuq_gemm(h, ctypes.c_void_p(x.data_ptr()), 2048, ctypes.c_void_p(y.data_ptr()), None))
         L.cuq_weight_free(h)
+    elif args.profile in ("prefill", "decode"):
+        # the config's prompt prefilled twice (chunks of 2048), or prefilled once
+        # and 8 tokens decoded with one kernel per op and no graph, so every
+        # launch of a step shows in a launch list
+        from anedvd_b200 import engine as E
+        ids = prompt_ids(model.cfg.vocab, C["prompt"])
+        eng = E.Engine.from_synth(model, max_seq=C["prompt"] + 16, max_chunk=2048,
+                                  use_graphs=args.profile == "prefill")
+        _, first = eng.prefill(ids, 0, want_logits=False)
+        if args.profile == "prefill":
+            eng.prefill(ids, 0, want_logits=False)
+        else:
+            eng.decode_greedy(first, C["prompt"], 8)
+        eng.close()
     torch.cuda.synchronize()
 
 
