@@ -11,7 +11,9 @@
 //     hi + lo (two MMAs), so scores keep ~22 bits of q like the reference's fp32;
 //   * scores are scaled by 1/sqrt(hd) (the reference's order: dot, then scale),
 //     masked causally, and folded into an online softmax (running max m, sum l);
-//   * O += P V with P also split into fp16 hi + lo.
+//   * O += P V with each probability rounded once to fp16 (a value in [0, 1]:
+//     relative error <= 2^-11) and l summing those same rounded values, so O is
+//     an exactly normalised mean over slightly perturbed weights.
 // The normalised O is written as fp16 hi + lo, the o projection GEMM's input.
 #include "common.cuh"
 #include "ops.cuh"
@@ -185,7 +187,9 @@ __global__ void __launch_bounds__(32 * G) fa_prefill_kernel(const float *__restr
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const int ri = e >> 1;
-                const float p = s[j][e] == -INFINITY ? 0.f : expf(s[j][e] - m[ri]);
+                // p rounded to fp16 once: the PV MMA reads it exactly and l sums
+                // the same values, so O is a weighted mean with exact weights
+                const float p = s[j][e] == -INFINITY ? 0.f : __half2float(__float2half_rn(expf(s[j][e] - m[ri])));
                 s[j][e] = p;
                 l[ri] += p;
             }
@@ -193,21 +197,19 @@ __global__ void __launch_bounds__(32 * G) fa_prefill_kernel(const float *__restr
         // ---- O += P V
 #pragma unroll
         for (int kk = 0; kk < 4; kk++) {  // 16 keys per k-step
-            uint32_t pa_hi[4], pa_lo[4];
-            split2(s[2 * kk][0], s[2 * kk][1], pa_hi[0], pa_lo[0]);
-            split2(s[2 * kk][2], s[2 * kk][3], pa_hi[1], pa_lo[1]);
-            split2(s[2 * kk + 1][0], s[2 * kk + 1][1], pa_hi[2], pa_lo[2]);
-            split2(s[2 * kk + 1][2], s[2 * kk + 1][3], pa_hi[3], pa_lo[3]);
+            uint32_t pa[4];  // exact: p is already an fp16 value
+            pa[0] = h2u(__floats2half2_rn(s[2 * kk][0], s[2 * kk][1]));
+            pa[1] = h2u(__floats2half2_rn(s[2 * kk][2], s[2 * kk][3]));
+            pa[2] = h2u(__floats2half2_rn(s[2 * kk + 1][0], s[2 * kk + 1][1]));
+            pa[3] = h2u(__floats2half2_rn(s[2 * kk + 1][2], s[2 * kk + 1][3]));
 #pragma unroll
             for (int nt = 0; nt < NT; nt += 2) {
                 uint32_t vb[4];  // b0, b1 of n-tile nt, then of nt + 1
                 const int mi = lane >> 3;
                 ldsm_x4_t(vtile + (uint32_t)((16 * kk + (lane & 7) + 8 * (mi & 1)) * ROW + (8 * (nt + (mi >> 1))) * 2),
                           vb);
-                mma16816(o[nt], pa_hi, vb[0], vb[1]);
-                mma16816(o[nt], pa_lo, vb[0], vb[1]);
-                mma16816(o[nt + 1], pa_hi, vb[2], vb[3]);
-                mma16816(o[nt + 1], pa_lo, vb[2], vb[3]);
+                mma16816(o[nt], pa, vb[0], vb[1]);
+                mma16816(o[nt + 1], pa, vb[2], vb[3]);
             }
         }
         __syncthreads();  // buffer b is refilled two blocks from now
