@@ -1,17 +1,21 @@
 // qgemm_tc.cu -- the prefill projection on the 5th-generation tensor cores:
 // Y[n][rows] = X[n][cols] W^T with W in its quantized planes (engine.zig:975-1329).
 //
-// One CTA computes a 128-row x 128-token tile.  Per 64-column K step:
-//   * 4 producer warps dequantise the 128 x 64 weight slice to the reference's
-//     fp16 values (RN16 of the fp32 dequant, gguf.zig:751-1071 / load_gguf.zig:371)
-//     straight into shared memory in the UMMA K-major 128-byte-swizzled layout,
-//     and copy the activation slice: x is carried as fp16 hi + lo (x = hi + lo
-//     to ~22 bits), stacked as 256 "tokens" (128 hi, then 128 lo);
-//   * one thread issues 4 x tcgen05.mma.cta_group::1.kind::f16 (M=128, N=256,
-//     K=16) accumulating fp32 in tensor memory (128 lanes x 256 columns);
-//   * tcgen05.commit releases the stage back to the producers (mbarriers, 4 stages).
-// The epilogue warps read TMEM with tcgen05.ld and write hi + lo (+ bias, or
-// += into the residual, or SiLU*mul for a gate|up pair) to global memory.
+// Persistent CTAs (one per SM, 448 threads) walk 128-row x 256-token tiles.
+//   * warps 0-7 copy each tile's raw quant bytes and scales with cp.async into a
+//     small ring (two threads per weight row) and dequantise them to the
+//     reference's fp16 values (RN16 of the fp32 dequant, gguf.zig:751-1071 /
+//     load_gguf.zig:371) straight into the A stage, UMMA K-major with a 64-byte
+//     swizzle, 32 columns per stage;
+//   * warp 9 loads the activation tiles by TMA: x as fp16 hi and lo (x = hi + lo
+//     to ~22 bits), 256 tokens x 32 columns each;
+//   * one lane of warp 8 issues tcgen05.mma.cta_group::1.kind::f16 (M=128,
+//     N=256, K=16) for hi and then lo into the same fp32 TMEM accumulator, and
+//     tcgen05.commit releases each stage (mbarriers, 4 stages); two accumulators
+//     alternate between tiles;
+//   * warps 10-13 read the finished accumulator with tcgen05.ld and write the
+//     output (+ bias, += into the residual, or SiLU*mul for an interleaved
+//     gate|up tile) while the next tile's MMAs run.
 // Every mbarrier wait is bounded: on timeout the CTA records an error, stops
 // issuing, releases its tensor memory and returns.
 #include <cuda.h>
