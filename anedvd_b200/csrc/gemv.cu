@@ -212,8 +212,18 @@ GemvPlan gemv_pick_plan(const Planes &w, int sm_count) {
     // many times over: two tiles per CTA with two warps each measured best.
     pl.kw = tiles >= 2048 ? 2 : 4;
     const int sm = sm_count > 0 ? sm_count : 148;
-    int want = (sm * 8 + tiles - 1) / tiles;  // ~8 CTAs of 4 warps per SM
-    int maxk = ni / 8;                        // keep >= 2 iterations per warp
+    int want, maxk;
+    if (tiles >= sm) {
+        // A tile per SM or more: about two CTAs per SM, and K parts of >= 16
+        // iterations (4 per warp), which a sweep of the c4/c5 shapes measured
+        // best: a split's partial store, ticket and reload cost more than the
+        // extra parallelism returns (14336x4096 Q4_K 24.7 -> 18.9 us unsplit).
+        want = (2 * sm + tiles - 1) / tiles;
+        maxk = ni / 16;
+    } else {
+        want = (sm * 8 + tiles - 1) / tiles;  // ~8 CTAs of 4 warps per SM
+        maxk = ni / 8;                        // keep >= 2 iterations per warp
+    }
     if (want > maxk) want = maxk;
     if (want > 16) want = 16;
     if (want < 1) want = 1;
