@@ -238,6 +238,12 @@ struct GemvArgs {
     unsigned int *counters = nullptr;  // one per 16-row tile, self-resetting
     int ksplit = 1;
     bool pdl = false;             // launch as a programmatic dependent of the previous kernel
+    // Input from the residual instead of xq: every CTA computes
+    // xq = split(rmsnorm(pre_x, pre_w, pre_eps)) into its own shared memory once
+    // the previous kernel is done (pre_n == cols, a multiple of 16, <= RN_MAX).
+    const float *pre_x = nullptr, *pre_w = nullptr;
+    uint32_t pre_n = 0;
+    float pre_eps = 0.f;
     GemvPost post;
 };
 

@@ -28,10 +28,24 @@ namespace {
 template <class TT, int EPI, int KW, int D>
 __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     __shared__ GemvShared sh;
-    extern __shared__ __align__(16) uint8_t gemv_dyn[];  // the post-op's x stage
-    if (!gemv_body<TT, EPI, KW, D>(p, blockIdx.x, blockIdx.y, sh, [] {
+    // the pre-norm's x stage and xq (before the body), the post-op's x stage (after)
+    extern __shared__ __align__(16) uint8_t gemv_dyn[];
+    const bool pre = p.pre_w != nullptr;
+    float4 *pre_stage = reinterpret_cast<float4 *>(gemv_dyn);
+    __half *pre_xq = reinterpret_cast<__half *>(gemv_dyn + sizeof(float) * p.pre_n);
+    KArgs k = p;
+    if (pre) {
+        k.xq = pre_xq;
+        k.xsum = xq_sums(pre_xq, p.kpad);
+    }
+    if (!gemv_body<TT, EPI, KW, D>(k, blockIdx.x, blockIdx.y, sh, [&] {
             griddep_wait();
             griddep_launch();
+            if (pre) {  // the RMSNorm this GEMV reads, computed by every CTA
+                reduce_norm_xq_block(const_cast<float *>(p.pre_x), nullptr, 0, nullptr, p.pre_w, p.pre_n,
+                                     p.pre_eps, pre_xq, p.kpad, pre_stage);
+                __syncthreads();
+            }
         }))
         return;
     const int t = threadIdx.x;
@@ -110,7 +124,11 @@ cudaError_t launch_kw(const GemvArgs &a, const KArgs &k, cudaStream_t s) {
     dim3 grid((a.w->rows / 16 + TPC - 1) / TPC, k.ksplit);
     // the RMSNorm post-ops stage x in dynamic shared memory (reduce_norm_xq_block)
     const bool norm = a.post.op == POST_RMSNORM || a.post.op == POST_TP_REDUCE;
-    const size_t smem = norm && a.post.n % 16 == 0 && a.post.n <= RN_MAX ? sizeof(float) * a.post.n : 0;
+    size_t smem = norm && a.post.n % 16 == 0 && a.post.n <= RN_MAX ? sizeof(float) * a.post.n : 0;
+    if (a.pre_w) {
+        const size_t pre = sizeof(float) * a.pre_n + sizeof(__half) * xq_halves(a.pre_n);
+        if (pre > smem) smem = pre;
+    }
     return launch_maybe_pdl(gemv_kernel<TT, EPI, KW, D>, grid, dim3(128), smem, s, a.pdl, k);
 }
 
@@ -249,6 +267,10 @@ int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
     }
     if (epi == EPI_SILU_XQ && (!a.w2 || a.w2->type != w.type || a.w2->rows != w.rows || a.w2->cols != w.cols)) {
         set_error("gemv: gate/up must share type and shape");
+        return CUQ_EINVAL;
+    }
+    if (a.pre_w && (!a.pre_x || a.pre_n != w.cols || a.pre_n % 16 || a.pre_n > RN_MAX)) {
+        set_error("gemv: the pre-norm needs x of cols (%u) floats, a multiple of 16 up to %u", w.cols, RN_MAX);
         return CUQ_EINVAL;
     }
     if (a.ksplit > 1 && (!a.ws || !a.counters)) {

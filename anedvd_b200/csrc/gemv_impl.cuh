@@ -427,6 +427,9 @@ struct KArgs {
     float *ws;
     unsigned int *counters;
     int ksplit;
+    const float *pre_x, *pre_w;  // GemvArgs::pre_* (pre_w null: input is xq)
+    uint32_t pre_n;
+    float pre_eps;
     GemvPost post;
 };
 
@@ -447,6 +450,10 @@ inline KArgs make_kargs(const GemvArgs &a) {
     k.ws = a.ws;
     k.counters = a.counters;
     k.ksplit = a.ksplit < 1 ? 1 : a.ksplit;
+    k.pre_x = a.pre_x;
+    k.pre_w = a.pre_w;
+    k.pre_n = a.pre_n;
+    k.pre_eps = a.pre_eps;
     k.post = a.post;
     return k;
 }

@@ -142,13 +142,28 @@ static int enqueue_step(cuq_model *m) {
         a.post.done = m->done;
         return a;
     };
-    // engine.zig:561-564 embedding, then layer 0's attention RMSNorm
-    TRY(launch_embed_norm(m->embed.p, m->state, m->x, m->layers[0].attn_norm, c.hidden, c.eps, m->xq_h, pdl, s));
+    // Single GPU: each RMSNorm is computed by every CTA of the GEMV that reads it
+    // (pre-norm), after its first weight loads are in flight, instead of by the
+    // last CTA of the GEMV that wrote the residual.
+    const bool pre = m->opt.tp_size == 1 && c.hidden % 16 == 0 && c.hidden <= RN_MAX;
+    auto prenorm = [&](GemvArgs &a, const float *w) {
+        if (!pre) return;
+        a.pre_x = m->x;
+        a.pre_w = w;
+        a.pre_n = c.hidden;
+        a.pre_eps = c.eps;
+    };
+    // engine.zig:561-564 embedding (then layer 0's attention RMSNorm)
+    if (pre)
+        TRY(launch_embed_row(m->embed.p, &m->state->token, m->x, s));
+    else
+        TRY(launch_embed_norm(m->embed.p, m->state, m->x, m->layers[0].attn_norm, c.hidden, c.eps, m->xq_h, pdl, s));
     for (uint32_t l = 0; l < c.layers; l++) {
         Layer &L = m->layers[l];
         // qkv projection + bias (main.zig:435-436)
         for (auto &seg : L.qkv) {
             GemvArgs a = gemv(seg.p, m->xq_h, m->qkv + seg.row_off, L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr);
+            prenorm(a, L.attn_norm);
             TRY(launch_gemv(a, EPI_STORE, s));
         }
         // RoPE + fp16 KV write + attention (main.zig:457-472), this rank's heads
@@ -160,6 +175,7 @@ static int enqueue_step(cuq_model *m) {
             GemvArgs a = gemv(L.o.p, m->xq_attn, nullptr, nullptr);
             int epi;
             residual_out(m, a, epi, L.o_bias, L.ffn_norm, 0);
+            if (pre) a.post.op = POST_NONE;
             TRY(launch_gemv(a, epi, s));
         }
         // gate/up with the SiLU*mul epilogue (engine.zig:645-668 split path)
@@ -167,11 +183,14 @@ static int enqueue_step(cuq_model *m) {
             GemvArgs a = gemv(L.gate.p, m->xq_h, nullptr, nullptr);
             a.w2 = &L.up.p;
             a.xq_out = m->xq_act;
+            prenorm(a, L.ffn_norm);
             TRY(launch_gemv(a, EPI_SILU_XQ, s));
         } else {
             GemvArgs a = gemv(L.gate.p, m->xq_h, m->gate_buf, nullptr);
+            prenorm(a, L.ffn_norm);
             TRY(launch_gemv(a, EPI_STORE, s));
             a = gemv(L.up.p, m->xq_h, m->up_buf, nullptr);
+            prenorm(a, L.ffn_norm);
             TRY(launch_gemv(a, EPI_STORE, s));
             TRY(launch_silu_mul(m->act, m->gate_buf, m->up_buf, lc.inter, s));
             TRY(launch_to_xq(m->act, lc.inter, 1, lc.inter, m->xq_act, s));
@@ -182,6 +201,7 @@ static int enqueue_step(cuq_model *m) {
             GemvArgs a = gemv(L.down.p, m->xq_act, nullptr, nullptr);
             int epi;
             residual_out(m, a, epi, nullptr, l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm, 1);
+            if (pre) a.post.op = POST_NONE;
             TRY(launch_gemv(a, epi, s));
         }
     }
@@ -190,6 +210,7 @@ static int enqueue_step(cuq_model *m) {
     // the cross-rank argmax under tensor parallelism.
     {
         GemvArgs a = gemv(head_proj(m).p, m->xq_h, m->logits, nullptr);
+        prenorm(a, m->final_norm);
         a.argmax64 = &m->state->argmax64;
         a.row_base = m->vocab_base;
         a.post.op = m->opt.tp_size > 1 ? POST_TP_FINISH : POST_FINISH;
