@@ -49,19 +49,33 @@ __device__ __forceinline__ void attn_walk(const float (&qr)[G][8], const __half 
                                           uint32_t p1, int warp, int lp, int pg, float (&m)[G], float (&l)[G],
                                           float (&o)[G][8]) {
     constexpr int E = 8, LPP = HD / E, PPW = 32 / LPP, U = G <= 4 ? 4 : 2;
+    constexpr uint32_t STEP = 4u * PPW * U;  // positions per iteration of the CTA's 4 warps
     const float scale = 1.0f / sqrtf((float)HD);
-    for (uint32_t pb = p0 + (uint32_t)warp * PPW * U; pb < p1; pb += 4u * PPW * U) {
-        uint4 ku[U], vu[U];
+    // K/V of this warp's positions pb + u*PPW + pg; the next iteration's are
+    // loaded before this one computes, so the walk keeps one round trip in flight
+    auto fetch = [&](uint32_t pb, uint4 (&kx)[U], uint4 (&vx)[U]) {
 #pragma unroll
         for (int u = 0; u < U; u++) {
             const uint32_t p = pb + u * PPW + pg;
-            ku[u] = make_uint4(0u, 0u, 0u, 0u);
-            vu[u] = ku[u];
+            kx[u] = make_uint4(0u, 0u, 0u, 0u);
+            vx[u] = kx[u];
             if (p < p1) {
-                ku[u] = *reinterpret_cast<const uint4 *>(kh + (size_t)p * HD + lp * E);
-                vu[u] = *reinterpret_cast<const uint4 *>(vh + (size_t)p * HD + lp * E);
+                kx[u] = *reinterpret_cast<const uint4 *>(kh + (size_t)p * HD + lp * E);
+                vx[u] = *reinterpret_cast<const uint4 *>(vh + (size_t)p * HD + lp * E);
             }
         }
+    };
+    uint4 kn[U], vn[U];
+    const uint32_t pb0 = p0 + (uint32_t)warp * PPW * U;
+    if (pb0 < p1) fetch(pb0, kn, vn);
+    for (uint32_t pb = pb0; pb < p1; pb += STEP) {
+        uint4 ku[U], vu[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            ku[u] = kn[u];
+            vu[u] = vn[u];
+        }
+        if (pb + STEP < p1) fetch(pb + STEP, kn, vn);
         float s[U][G];
 #pragma unroll
         for (int u = 0; u < U; u++) {
