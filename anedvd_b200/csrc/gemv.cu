@@ -33,20 +33,18 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
     const bool pre = p.pre_w != nullptr;
     float4 *pre_stage = reinterpret_cast<float4 *>(gemv_dyn);
     __half *pre_xq = reinterpret_cast<__half *>(gemv_dyn + sizeof(float) * p.pre_n);
-    KArgs k = p;
-    if (pre) {
-        k.xq = pre_xq;
-        k.xsum = xq_sums(pre_xq, p.kpad);
-    }
-    if (!gemv_body<TT, EPI, KW, D>(k, blockIdx.x, blockIdx.y, sh, [&] {
-            griddep_wait();
-            griddep_launch();
-            if (pre) {  // the RMSNorm this GEMV reads, computed by every CTA
-                reduce_norm_xq_block(const_cast<float *>(p.pre_x), nullptr, 0, nullptr, p.pre_w, p.pre_n,
-                                     p.pre_eps, pre_xq, p.kpad, pre_stage);
-                __syncthreads();
-            }
-        }))
+    if (!gemv_body<TT, EPI, KW, D>(
+            p, blockIdx.x, blockIdx.y, sh,
+            [&] {
+                griddep_wait();
+                griddep_launch();
+                if (pre) {  // the RMSNorm this GEMV reads, computed by every CTA
+                    reduce_norm_xq_block(const_cast<float *>(p.pre_x), nullptr, 0, nullptr, p.pre_w, p.pre_n,
+                                         p.pre_eps, pre_xq, p.kpad, pre_stage);
+                    __syncthreads();
+                }
+            },
+            pre ? pre_xq : nullptr, pre ? xq_sums(pre_xq, p.kpad) : nullptr))
         return;
     const int t = threadIdx.x;
     __shared__ int is_last;

@@ -72,7 +72,7 @@ __device__ __forceinline__ uint32_t magic(uint32_t v, uint32_t mask) { return (v
 // the first column of the 4-column group the lane feeds at k-step s.
 
 struct TQ8_0 {
-    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 2;
+    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 3;  // 3 x 16 rows x 64 columns in flight per warp
     static constexpr bool HAS_CORR = false;
     template <class R_>
     __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
@@ -620,7 +620,8 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
 
 template <class TT, int EPI, int KW, int D, class BeforeX>
 __device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t by, GemvShared &sh,
-                                          BeforeX &&before_x) {
+                                          BeforeX &&before_x, const __half *xq_in = nullptr,
+                                          const float *xsum_in = nullptr) {
     // Dual (gate|up): one tile per CTA, warps 0-1 stream the gate rows and
     // warps 2-3 the same rows of up (KW = 2 per matrix), so no warp holds both.
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
@@ -648,7 +649,10 @@ __device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t 
     }
     before_x();
 
-    const __half *xb = p.xq + (g == 1 ? p.kpad : 0);  // B fragments: L1-cached, shared by the SM's CTAs
+    // B fragments (L1-cached, shared by the SM's CTAs): p.xq, or xq_in / xsum_in
+    // when the caller built the input itself (shared memory)
+    const __half *xb = (xq_in ? xq_in : p.xq) + (g == 1 ? p.kpad : 0);
+    const float *xsum = xsum_in ? xsum_in : p.xsum;
     const bool bl = g < 2;
 
     float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -671,7 +675,7 @@ __device__ __forceinline__ bool gemv_body(const KArgs &p, uint32_t bx, uint32_t 
                 TT::frag(R, P, s, a);
                 mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
             }
-            if (TT::HAS_CORR) TT::correct(P, p.xsum, it, tig, k0, k1);
+            if (TT::HAS_CORR) TT::correct(P, xsum, it, tig, k0, k1);
         }
     }
     return gemv_finish<TT, EPI, KW>(p, bx, by, sh, c, k0, k1);
