@@ -1,7 +1,7 @@
 """The CPU oracle pinned against the reference's own golden vectors and tests.
 
 Each test restates one of the reference's tests (cited) against the oracle,
-so the oracle that later judges the CUDA kernels is itself pinned.
+so the oracle that later checks the CUDA kernels is itself pinned.
 """
 import os
 import struct
