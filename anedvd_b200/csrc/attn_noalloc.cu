@@ -8,6 +8,8 @@
 // allocator call can cause between decode steps.  For them this file keeps the
 // scratch in one fixed array compiled into the library; the caller still passes
 // its own q, K/V and output buffers.
+#include <cuda.h>  // CUcontext / CUresult types of the two driver calls fetched below
+
 #include <mutex>
 
 #include "common.cuh"
@@ -27,11 +29,39 @@ constexpr size_t kScratchFloats = 262144;
 static __device__ __align__(256) float g_attn_scratch[kScratchFloats];
 
 // Host code cannot use the name g_attn_scratch as a device address: it must ask
-// the runtime for the array's address on each device, once, with that device
-// current.
+// the runtime for the array's address on each device, with that device
+// current.  The answer is cached per device together with the id of the
+// context it was taken in; a context the host application destroyed and
+// recreated (cudaDeviceReset) has a new id, and the address is looked up again.
 constexpr int kMaxDevices = 64;
+struct ScratchSlot {
+    unsigned long long ctx_id = 0;
+    float *ptr = nullptr;
+};
 std::mutex g_mu;
-float *g_scratch_dev[kMaxDevices] = {};
+ScratchSlot g_slot[kMaxDevices];
+
+typedef CUresult (*CtxGetCurrentFn)(CUcontext *);
+typedef CUresult (*CtxGetIdFn)(CUcontext, unsigned long long *);
+
+// Id of the calling thread's current context (0 when none or unknown).
+unsigned long long current_ctx_id() {
+    static CtxGetCurrentFn get_current = nullptr;
+    static CtxGetIdFn get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &f, cudaEnableDefault) == cudaSuccess)
+            get_current = (CtxGetCurrentFn)f;
+        f = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &f, cudaEnableDefault) == cudaSuccess) get_id = (CtxGetIdFn)f;
+    });
+    if (!get_current || !get_id) return 0;
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS) return 0;
+    return id;
+}
 
 }  // namespace
 
@@ -42,8 +72,14 @@ extern "C" int cuq_attention_decode_noalloc(float *out_dev, const float *q_dev, 
                                             uint32_t heads, uint32_t kv_heads, uint32_t hd, void *stream) {
     CUQ_CHECK_ARG(out_dev && q_dev && k_dev && v_dev && n_past >= 1 && n_past <= cache_stride,
                   "cuq_attention_decode_noalloc: bad argument (n_past %u, stride %u)", n_past, cache_stride);
-    CUQ_CHECK_ARG(kv_heads > 0 && heads % kv_heads == 0, "cuq_attention_decode_noalloc: heads %% kv_heads != 0");
-    const size_t per_split = (size_t)heads * (hd + 2);
+    CUQ_CHECK_ARG(heads > 0 && kv_heads > 0 && heads % kv_heads == 0,
+                  "cuq_attention_decode_noalloc: heads (%u) must be a positive multiple of kv_heads (%u)", heads,
+                  kv_heads);
+    if (hd != 64 && hd != 128) {
+        set_error("cuq_attention_decode_noalloc: unsupported head_dim %u (64 or 128)", hd);
+        return CUQ_EUNSUPPORTED;
+    }
+    const size_t per_split = (size_t)heads * ((size_t)hd + 2);
     if (per_split > kScratchFloats) {
         set_error("cuq_attention_decode_noalloc: %u heads x head_dim %u need %zu scratch floats, more than the "
                   "library's fixed %zu (heads * (head_dim + 2) must be <= %zu)",
@@ -59,7 +95,9 @@ extern "C" int cuq_attention_decode_noalloc(float *out_dev, const float *q_dev, 
     float *scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_mu);
-        if (!g_scratch_dev[dev]) {  // first call on this device: look the array up
+        ScratchSlot &slot = g_slot[dev];
+        unsigned long long id = current_ctx_id();
+        if (!slot.ptr || id == 0 || id != slot.ctx_id) {  // set-up on this device (or in a new context)
             void *p = nullptr;
             cudaError_t e = cudaGetSymbolAddress(&p, g_attn_scratch);
             if (e != cudaSuccess || !p) {
@@ -67,9 +105,10 @@ extern "C" int cuq_attention_decode_noalloc(float *out_dev, const float *q_dev, 
                           cudaGetErrorString(e));
                 return CUQ_ECUDA;
             }
-            g_scratch_dev[dev] = (float *)p;
+            slot.ptr = (float *)p;
+            slot.ctx_id = current_ctx_id();  // the lookup made the primary context current if it was not
         }
-        scratch = g_scratch_dev[dev];
+        scratch = slot.ptr;
     }
     int nsplit = attn_pick_nsplit(kv_heads, n_past, sm_count_current());
     const int cap = (int)(kScratchFloats / per_split);

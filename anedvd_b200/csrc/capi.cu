@@ -315,11 +315,16 @@ int cuq_attention_decode(float *out_dev, const float *q_dev, const uint16_t *k_d
                          void *stream) {
     CUQ_CHECK_ARG(out_dev && q_dev && k_dev && v_dev && n_past >= 1 && n_past <= cache_stride,
                   "cuq_attention_decode: bad argument (n_past %u, stride %u)", n_past, cache_stride);
-    CUQ_CHECK_ARG(kv_heads > 0 && heads % kv_heads == 0, "cuq_attention_decode: heads %% kv_heads != 0");
+    CUQ_CHECK_ARG(heads > 0 && kv_heads > 0 && heads % kv_heads == 0,
+                  "cuq_attention_decode: heads (%u) must be a positive multiple of kv_heads (%u)", heads, kv_heads);
+    if (hd != 64 && hd != 128) {
+        set_error("cuq_attention_decode: unsupported head_dim %u (64 or 128)", hd);
+        return CUQ_EUNSUPPORTED;
+    }
     cudaStream_t s = (cudaStream_t)stream;
     int nsplit = attn_pick_nsplit(kv_heads, n_past, sm_count_current());
     float *part = nullptr;
-    CUQ_CUDA_TRY(cudaMallocAsync(&part, sizeof(float) * (size_t)nsplit * heads * (hd + 2), s));
+    CUQ_CUDA_TRY(cudaMallocAsync(&part, sizeof(float) * (size_t)nsplit * heads * ((size_t)hd + 2), s));
     int rc = launch_attention_decode(q_dev, (const __half *)k_dev, (const __half *)v_dev, cache_stride, nullptr,
                                      n_past, heads, kv_heads, hd, part, nsplit, out_dev, nullptr, s);
     cudaFreeAsync(part, s);

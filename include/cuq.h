@@ -141,8 +141,10 @@ int cuq_attention_decode(float *out_dev, const float *q_dev, const uint16_t *k_d
  * loads the library until exit); calls whose heads * (hd + 2) exceeds that are
  * rejected with CUQ_EINVAL.  The first call on each device looks the array's
  * device address up (cudaGetSymbolAddress), so make that first call before any
- * stream capture.  All calls share the one array: calls that overlap on the GPU
- * (other streams, other threads) race and must be serialised by the caller. */
+ * stream capture; the first call after the host application reset the device
+ * (cudaDeviceReset) looks it up again.  All calls share the one array: calls
+ * that overlap on the GPU (other streams, other threads) race and must be
+ * serialised by the caller. */
 int cuq_attention_decode_noalloc(float *out_dev, const float *q_dev, const uint16_t *k_dev,
                                  const uint16_t *v_dev, uint32_t n_past, uint32_t cache_stride,
                                  uint32_t heads, uint32_t kv_heads, uint32_t hd, void *stream);

@@ -34,7 +34,10 @@ def _inputs(heads, kv_heads, hd, n_past, stride, seed):
 
 def test_noalloc_matches_allocating_attention_twice_in_a_row():
     L = lib()
-    for call, (heads, kv_heads, hd, n_past) in enumerate([(32, 8, 128, 4608), (14, 2, 64, 459)]):
+    # the third shape wants 37 position splits, more than the 31 that fit the
+    # fixed array at 64 x (128 + 2) floats each: the split count is capped
+    for call, (heads, kv_heads, hd, n_past) in enumerate([(32, 8, 128, 4608), (14, 2, 64, 459),
+                                                          (64, 8, 128, 1200)]):
         stride = n_past + 3
         q, k, v, kd, vd = _inputs(heads, kv_heads, hd, n_past, stride, seed=100 + call)
         qd, kdd, vdd = dev(q), dev(kd), dev(vd)
@@ -58,3 +61,9 @@ def test_noalloc_rejects_heads_beyond_its_fixed_scratch():
     rc = L.cuq_attention_decode_noalloc(ptr(buf), ptr(buf), ptr(buf), ptr(buf), 1, 1, 2048, 256, 128, None)
     assert rc == rt.EINVAL
     assert "262144" in rt.last_error()
+    # no heads at all, and head dims the kernels do not have (one that would wrap
+    # heads * (head_dim + 2) in 32 bits among them), are argument errors
+    assert L.cuq_attention_decode_noalloc(ptr(buf), ptr(buf), ptr(buf), ptr(buf), 1, 1, 0, 1, 128, None) == rt.EINVAL
+    for hd in (0, 96, 0xFFFFFFFE):
+        rc = L.cuq_attention_decode_noalloc(ptr(buf), ptr(buf), ptr(buf), ptr(buf), 1, 1, 8, 1, hd, None)
+        assert rc == rt.EUNSUPPORTED, hd
