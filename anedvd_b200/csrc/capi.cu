@@ -279,30 +279,18 @@ int cuq_rmsnorm(float *out_dev, const float *x_dev, const float *w_dev, uint32_t
 }
 
 int cuq_rope(float *v_dev, uint32_t heads, uint32_t hd, uint32_t pos, float theta, int adjacent, void *stream) {
-    CUQ_CHECK_ARG(v_dev && hd >= 2 && hd % 2 == 0, "cuq_rope: bad argument");
-    cudaStream_t s = (cudaStream_t)stream;
+    CUQ_CHECK_ARG(v_dev && hd >= 2 && hd % 2 == 0 && hd <= 256, "cuq_rope: bad argument (head_dim %u)", hd);
     // one row of the table for this position, computed with the reference formula
-    float *row = (float *)malloc(sizeof(float) * hd);
+    // (cpu.zig:26-31) and handed to the kernel by value: nothing to copy or wait for
+    RopeRow row;
     uint32_t half = hd / 2;
     for (uint32_t i = 0; i < half; i++) {
         float freq = 1.0f / powf(theta, (float)(2 * i) / (float)hd);
         float angle = (float)pos * freq;
-        row[i] = cosf(angle);
-        row[half + i] = sinf(angle);
+        row.v[i] = cosf(angle);
+        row.v[half + i] = sinf(angle);
     }
-    float *d = nullptr;
-    cudaError_t e = cudaMallocAsync(&d, sizeof(float) * hd, s);
-    if (e == cudaSuccess) e = cudaMemcpyAsync(d, row, sizeof(float) * hd, cudaMemcpyHostToDevice, s);
-    int rc = CUQ_OK;
-    if (e == cudaSuccess) rc = launch_rope(v_dev, heads, hd, d, adjacent, s);
-    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
-    if (d) cudaFreeAsync(d, s);
-    free(row);
-    if (e != cudaSuccess) {
-        set_error("cuq_rope: %s", cudaGetErrorString(e));
-        return CUQ_ECUDA;
-    }
-    return rc;
+    return launch_rope(v_dev, heads, hd, row, adjacent, (cudaStream_t)stream);
 }
 
 int cuq_silu_mul(float *out_dev, const float *g_dev, const float *u_dev, uint32_t n, void *stream) {
@@ -328,6 +316,28 @@ int cuq_attention_decode(float *out_dev, const float *q_dev, const uint16_t *k_d
     int rc = launch_attention_decode(q_dev, (const __half *)k_dev, (const __half *)v_dev, cache_stride, nullptr,
                                      n_past, heads, kv_heads, hd, part, nsplit, out_dev, nullptr, s);
     cudaFreeAsync(part, s);
+    return rc;
+}
+
+int cuq_attention_prefill(float *out_dev, const float *q_dev, const uint16_t *k_dev, const uint16_t *v_dev,
+                          uint32_t n, uint32_t pos0, uint32_t cache_stride, uint32_t heads, uint32_t kv_heads,
+                          uint32_t hd, void *stream) {
+    CUQ_CHECK_ARG(out_dev && q_dev && k_dev && v_dev && n >= 1 && (uint64_t)pos0 + n <= cache_stride,
+                  "cuq_attention_prefill: bad argument (n %u, pos0 %u, stride %u)", n, pos0, cache_stride);
+    CUQ_CHECK_ARG(heads > 0 && kv_heads > 0 && heads % kv_heads == 0,
+                  "cuq_attention_prefill: heads (%u) must be a positive multiple of kv_heads (%u)", heads, kv_heads);
+    if (hd != 64 && hd != 128) {
+        set_error("cuq_attention_prefill: unsupported head_dim %u (64 or 128)", hd);
+        return CUQ_EUNSUPPORTED;
+    }
+    cudaStream_t s = (cudaStream_t)stream;
+    const size_t count = (size_t)n * heads * hd;
+    __half *hl = nullptr;  // the kernel's output: fp16 hi and lo planes (the o GEMM's input)
+    CUQ_CUDA_TRY(cudaMallocAsync(&hl, sizeof(__half) * 2 * count, s));
+    int rc = launch_attention_prefill(q_dev, (const __half *)k_dev, (const __half *)v_dev, cache_stride, pos0, n,
+                                      heads, kv_heads, hd, hl, hl + count, s);
+    if (rc == CUQ_OK) rc = launch_hilo_sum(hl, hl + count, count, out_dev, s);
+    cudaFreeAsync(hl, s);
     return rc;
 }
 

@@ -244,6 +244,7 @@ struct GemvArgs {
     const float *pre_x = nullptr, *pre_w = nullptr;
     uint32_t pre_n = 0;
     float pre_eps = 0.f;
+    int *err = nullptr;           // set to 1 when a bounded wait of the TMA GEMV gave up (may be null)
     GemvPost post;
 };
 
@@ -300,8 +301,15 @@ __device__ __forceinline__ void rmsnorm_xq_block(const float *x, const float *w,
 }
 
 int launch_gemv(const GemvArgs &a, int epilogue, cudaStream_t s);
-// Scratch a GEMV of this weight needs for a given ksplit (floats, counters).
-int gemv_pick_ksplit(const Planes &w, int sm_count);
+// K parts (CTAs along K) of a GEMV of this weight; nmat 2 for a gate|up pair.
+// Callers size the split-K workspace with the same value they launch with.
+int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat = 1);
+// The TMA-fed GEMV (gemv_tma.cu): the types it covers, its K split, and its
+// launcher (CUQ_EUNSUPPORTED for a type or form it does not cover; then the
+// register-prefetch kernel runs).
+bool gemv_tma_supported(int type);
+int gemv_tma_ksplit(const Planes &w, int nmat, int sm_count);
+int launch_gemv_tma(const GemvArgs &a, int epilogue, cudaStream_t s);
 struct GemvPlan {
     int kw = 4;      // warps per 16-row tile
     int ksplit = 1;  // CTAs along K

@@ -46,73 +46,7 @@ __global__ void __launch_bounds__(128) gemv_kernel(const KArgs p) {
             },
             pre ? pre_xq : nullptr, pre ? xq_sums(pre_xq, p.kpad) : nullptr))
         return;
-    const int t = threadIdx.x;
-    __shared__ int is_last;
-    if (p.post.op == POST_NONE) return;
-    // Grid completion: the CTA that finishes last runs the post-op.
-    __threadfence();
-    __syncthreads();
-    if (t == 0) {
-        unsigned int prev = atomicAdd(p.post.done, 1u);
-        is_last = (prev == gridDim.x - 1u);
-    }
-    __syncthreads();
-    if (!is_last) return;
-    __threadfence();
-    float4 *rn_stage = reinterpret_cast<float4 *>(gemv_dyn);  // n floats when the launch gave them (fast path)
-    const bool fast = p.post.n % 16 == 0 && p.post.n <= RN_MAX;
-    if (p.post.op == POST_TP_REDUCE) {
-        // every rank's CTAs pushed once: x += sum over ranks (+ bias), then the RMSNorm
-        const TpComm &tp = p.post.tp;
-        __shared__ int ok;
-        if (t == 0) ok = tp_wait(tp, p.post.tp_phase, (unsigned)tp.size * gridDim.x);
-        __syncthreads();
-        if (fast) {
-            reduce_norm_xq_block(p.post.xr, ok ? &tp : nullptr, p.post.tp_phase, p.post.bias, p.post.w, p.post.n,
-                                 p.post.eps, p.post.xq, xq_pad(p.post.n), rn_stage);
-        } else {
-            if (ok) {
-                for (uint32_t i = t; i < p.post.n; i += blockDim.x) {
-                    float sum = tp_sum(tp, p.post.tp_phase, i);
-                    if (p.post.bias) sum = sum + p.post.bias[i];
-                    p.post.xr[i] = __ldcg(p.post.xr + i) + sum;
-                }
-            }
-            __threadfence();
-            __syncthreads();
-            rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
-        }
-        __syncthreads();
-        if (t == 0) tp_reset(tp, p.post.tp_phase);
-    } else if (p.post.op == POST_RMSNORM) {
-        if (fast)
-            reduce_norm_xq_block(const_cast<float *>(p.post.x), nullptr, 0, nullptr, p.post.w, p.post.n, p.post.eps,
-                                 p.post.xq, xq_pad(p.post.n), rn_stage);
-        else
-            rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
-    } else if (p.post.op == POST_FINISH) {
-        if (t == 0) finish_step(p.post.state, p.post.forced, p.post.out_tokens);
-    } else if (p.post.op == POST_TP_FINISH) {
-        // cross-rank argmax: every rank publishes its packed key, all take the max
-        // (the packing keeps the reference's first-index tie rule, cpu.zig:477-483)
-        if (t == 0) {
-            const TpComm &tp = p.post.tp;
-            const unsigned long long mine = __ldcg(&p.post.state->argmax64);
-            for (int q = 0; q < tp.size; q++) tp_am(tp, q)[tp.rank] = mine;
-            tp_signal(tp, TP_CTR_ARGMAX);
-            unsigned long long best = mine;
-            if (tp_wait(tp, TP_CTR_ARGMAX, (unsigned)tp.size)) {
-                for (int r = 0; r < tp.size; r++) {
-                    const unsigned long long k = __ldcv(tp_am(tp, tp.rank) + r);
-                    best = k > best ? k : best;
-                }
-            }
-            tp_reset(tp, TP_CTR_ARGMAX);
-            p.post.state->argmax64 = best;
-            finish_step(p.post.state, p.post.forced, p.post.out_tokens);
-        }
-    }
-    if (t == 0) *p.post.done = 0u;
+    gemv_post_op(p, gemv_dyn);
 }
 
 template <class TT, int EPI, int KW>
@@ -247,7 +181,10 @@ GemvPlan gemv_pick_plan(const Planes &w, int sm_count) {
     return pl;
 }
 
-int gemv_pick_ksplit(const Planes &w, int sm_count) { return gemv_pick_plan(w, sm_count).ksplit; }
+int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat) {
+    if (gemv_tma_supported(w.type)) return gemv_tma_ksplit(w, nmat, sm_count);
+    return gemv_pick_plan(w, sm_count).ksplit;
+}
 
 int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
     const Planes &w = *a.w;
@@ -275,6 +212,7 @@ int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
         set_error("gemv: split-K needs a workspace");
         return CUQ_EINVAL;
     }
+    if (!a.pre_w && gemv_tma_supported(w.type)) return launch_gemv_tma(a, epi, s);
     switch (w.type) {
     case CUQ_Q8_0: return launch_t<TQ8_0>(a, epi, s);
     case CUQ_Q4_0: return launch_t<TQ4L<CUQ_Q4_0>>(a, epi, s);

@@ -53,6 +53,32 @@ struct SrcGlobal {
 __device__ __forceinline__ uint32_t h2u(__half2 h) { return *reinterpret_cast<uint32_t *>(&h); }
 __device__ __forceinline__ __half2 u2h(uint32_t u) { return *reinterpret_cast<__half2 *>(&u); }
 
+// Packed fp32 pairs (lane 0 in the low word) for the f32x2 instructions.
+__device__ __forceinline__ unsigned long long pack_f2(float a, float b) {
+    return (unsigned long long)__float_as_uint(a) | ((unsigned long long)__float_as_uint(b) << 32);
+}
+__device__ __forceinline__ unsigned long long ffma_f2(unsigned long long a, unsigned long long b,
+                                                      unsigned long long c) {
+    unsigned long long d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ unsigned long long fsub_f2(unsigned long long a, unsigned long long b) {
+    unsigned long long d;
+    asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+// RN16 of both lanes -> half2 (lane 0 low)
+__device__ __forceinline__ uint32_t cvt_rn_h2(unsigned long long v) {
+    return h2u(__floats2half2_rn(__uint_as_float((uint32_t)v), __uint_as_float((uint32_t)(v >> 32))));
+}
+// two bytes of w (small unsigned integers, selected by byte_perm selectors
+// 0x744b) as the floats 2^23 + byte, packed
+__device__ __forceinline__ unsigned long long magic23_bytes(uint32_t w, uint32_t sel0, uint32_t sel1) {
+    return (unsigned long long)__byte_perm(w, 0x4B000000u, sel0) |
+           ((unsigned long long)__byte_perm(w, 0x4B000000u, sel1) << 32);
+}
+
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
     asm volatile(
@@ -191,19 +217,22 @@ struct TQ4L {
 
 // Q4_K: one 256-superblock per iteration; lane tig owns the 32-byte group tig
 // (sub-blocks 2tig in the low nibbles and 2tig+1 in the high nibbles).
-// The reference weight is d1*q - m1 with d1 = d*sc, m1 = dmin*m, both exact in
-// fp32 (gguf.zig:975-992).  fma(1024+q, sc, -1024*sc) = q*sc is an integer
-// <= 945, exact in fp16; then one fma(q*sc, d, -m1h) with m1h = RN16(m1) rounds
-// d1*q - m1h once, at the weight's own magnitude (as the reference's fp16 weight
-// is rounded).  The small remainder (m1 - m1h) * sum(x) over the sub-block is
-// subtracted after the MMA in fp32, so no scale error is shared by a sub-block.
+// The reference weight is RN16 of the fp32 value d1*q - m1 with d1 = d*sc and
+// m1 = dmin*m, both exact in fp32 (gguf.zig:975-992, load_gguf.zig:371); d1*q
+// is exact too, so one fp32 fma(d1, q, -m1) rounds exactly where the
+// reference's subtraction rounds, and cvt.rn.f16x2 then rounds like readF16.
+// q becomes an exact float through the 2^23 exponent (bits 0x4B0000qq minus
+// 2^23), two weights per packed f32x2 operation.
 struct TQ4K {
     static constexpr int SPAN = 256, KSTEPS = 16, DEPTH = 1;
-    static constexpr bool HAS_CORR = true;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
     // prefetched: the quant bytes and the 16-byte scale record of rows r0, r0+8
     struct Raw { uint4 q[2][2]; uint4 meta[2]; };
-    // derived at compute time (keeps the prefetch ring small)
-    struct Prep { __half2 d[2], sc[2][2], csc[2][2], nm1[2][2]; float m1[2][2]; };
+    // derived at compute time (keeps the prefetch ring small): packed (d1, d1)
+    // and (-m1, -m1) per row and sub-block part
+    struct Prep { unsigned long long d1[2][2], nm1[2][2]; };
     template <class Src = SrcGlobal>
     __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
 #pragma unroll
@@ -232,51 +261,35 @@ struct TQ4K {
         return (a2 & (lo ? 0x3F3F3F3Fu : 0x0F0F0F0Fu)) | hb;
     }
     __device__ static void prep(const Raw &R, int tig, Prep &P) {
-        const __half2 k1024 = __float2half2_rn(1024.f);
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             const uint4 meta = R.meta[rr];
             const uint32_t v = scale_bytes(meta, tig);
-            P.d[rr] = u2h(__byte_perm(meta.x, 0u, 0x1010u));
-            const __half2 dmin2 = u2h(__byte_perm(meta.x, 0u, 0x3232u));
-            // small integers as fp16 through the 0x64 exponent byte: 1024 + field
-            const __half2 sc0 = __hsub2(u2h(__byte_perm(v, 0x64646464u, 0x4040u)), k1024);
-            const __half2 sc1 = __hsub2(u2h(__byte_perm(v, 0x64646464u, 0x4141u)), k1024);
-            const __half2 mm = __hsub2(u2h(__byte_perm(v, 0x64646464u, 0x4342u)), k1024);  // (m0, m1)
-            // part 0 reads 1024 + q (low nibbles), part 1 1024 + 16 q (high
-            // nibbles in place): fma(x, sc', c') = q * sc exactly in both
-            P.sc[rr][0] = sc0;
-            P.csc[rr][0] = __hmul2(sc0, __float2half2_rn(-1024.f));
-            P.sc[rr][1] = __hmul2(sc1, __float2half2_rn(0.0625f));
-            P.csc[rr][1] = __hmul2(sc1, __float2half2_rn(-64.f));
-            const __half2 m1h = __hmul2(dmin2, mm);  // RN16(dmin * m), both sub-blocks
-            P.nm1[rr][0] = __hneg2(__low2half2(m1h));
-            P.nm1[rr][1] = __hneg2(__high2half2(m1h));
-            const float dmin = __low2float(dmin2);
-            const float2 mf = __half22float2(mm), m1f = __half22float2(m1h);
-            P.m1[rr][0] = fmaf(dmin, mf.x, -m1f.x);  // m1 - m1h, exact
-            P.m1[rr][1] = fmaf(dmin, mf.y, -m1f.y);
+            const float d = __half2float(__ushort_as_half((unsigned short)(meta.x & 0xFFFFu)));
+            const float dmin = __half2float(__ushort_as_half((unsigned short)(meta.x >> 16)));
+#pragma unroll
+            for (int part = 0; part < 2; part++) {
+                const float d1 = __fmul_rn(d, (float)((v >> (8 * part)) & 0xFFu));          // exact
+                const float m1 = __fmul_rn(dmin, (float)((v >> (8 * (part + 2))) & 0xFFu));  // exact
+                P.d1[rr][part] = pack_f2(d1, d1);
+                P.nm1[rr][part] = pack_f2(-m1, -m1);
+            }
         }
     }
     // k-step s: word i = s & 7 of the group, part = s >> 3 (low nibbles, then high).
     __device__ static void frag(const Raw &R, const Prep &P, int s, uint32_t (&a)[4]) {
         const int i = s & 7, part = s >> 3;
-        const uint32_t mask = part ? 0x00F000F0u : 0x000F000Fu;
+        const unsigned long long mg = pack_f2(8388608.f, 8388608.f);
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             const uint32_t u = TQ8_0::word(R.q[rr][i >> 2], i & 3);
-            __half2 q02 = __hfma2(u2h(magic(u, mask)), P.sc[rr][part], P.csc[rr][part]);  // q*sc
-            __half2 q13 = __hfma2(u2h(magic(u >> 8, mask)), P.sc[rr][part], P.csc[rr][part]);
-            a[rr] = h2u(__hfma2(q02, P.d[rr], P.nm1[rr][part]));  // RN16(d1*q - m1h)
-            a[rr + 2] = h2u(__hfma2(q13, P.d[rr], P.nm1[rr][part]));
+            const uint32_t nib = part ? ((u >> 4) & 0x0F0F0F0Fu) : (u & 0x0F0F0F0Fu);
+            // columns 0, 2 and 1, 3 of the word's four (the fragment's pairs)
+            const unsigned long long q02 = fsub_f2(magic23_bytes(nib, 0x7440u, 0x7442u), mg);
+            const unsigned long long q13 = fsub_f2(magic23_bytes(nib, 0x7441u, 0x7443u), mg);
+            a[rr] = cvt_rn_h2(ffma_f2(P.d1[rr][part], q02, P.nm1[rr][part]));  // RN16(fp32(d1*q - m1))
+            a[rr + 2] = cvt_rn_h2(ffma_f2(P.d1[rr][part], q13, P.nm1[rr][part]));
         }
-    }
-    // sum over this lane's two sub-blocks of (m1 - m1h) * sum(x), for rows r0 and r0+8
-    __device__ static void correct(const Prep &P, const float *xsum, int it, int tig, float &c0, float &c1) {
-        float4 X = *reinterpret_cast<const float4 *>(xsum + 16 * it + 4 * tig);
-        float xl = X.x + X.y, xh = X.z + X.w;
-        c0 += P.m1[0][0] * xl + P.m1[0][1] * xh;
-        c1 += P.m1[1][0] * xl + P.m1[1][1] * xh;
     }
     __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 64 + (s >> 3) * 32 + (s & 7) * 4; }
 };
@@ -605,6 +618,81 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         }
     }
     return true;
+}
+
+// Grid completion of a GEMV: the CTA that finishes last runs the post-op
+// (the next RMSNorm, the end of a decode step, or the cross-rank reduction
+// before them).  `dyn`: dynamic shared memory of at least post.n floats when the
+// post-op is a norm with post.n % 16 == 0 and post.n <= RN_MAX (staging), free
+// for reuse at this point.  Every thread of the CTA calls it.
+__device__ __forceinline__ void gemv_post_op(const KArgs &p, uint8_t *gemv_dyn) {
+    const int t = threadIdx.x;
+    __shared__ int is_last;
+    if (p.post.op == POST_NONE) return;
+    // Grid completion: the CTA that finishes last runs the post-op.
+    __threadfence();
+    __syncthreads();
+    if (t == 0) {
+        unsigned int prev = atomicAdd(p.post.done, 1u);
+        is_last = (prev == gridDim.x - 1u);
+    }
+    __syncthreads();
+    if (!is_last) return;
+    __threadfence();
+    float4 *rn_stage = reinterpret_cast<float4 *>(gemv_dyn);  // n floats when the launch gave them (fast path)
+    const bool fast = p.post.n % 16 == 0 && p.post.n <= RN_MAX;
+    if (p.post.op == POST_TP_REDUCE) {
+        // every rank's CTAs pushed once: x += sum over ranks (+ bias), then the RMSNorm
+        const TpComm &tp = p.post.tp;
+        __shared__ int ok;
+        if (t == 0) ok = tp_wait(tp, p.post.tp_phase, (unsigned)tp.size * gridDim.x);
+        __syncthreads();
+        if (fast) {
+            reduce_norm_xq_block(p.post.xr, ok ? &tp : nullptr, p.post.tp_phase, p.post.bias, p.post.w, p.post.n,
+                                 p.post.eps, p.post.xq, xq_pad(p.post.n), rn_stage);
+        } else {
+            if (ok) {
+                for (uint32_t i = t; i < p.post.n; i += blockDim.x) {
+                    float sum = tp_sum(tp, p.post.tp_phase, i);
+                    if (p.post.bias) sum = sum + p.post.bias[i];
+                    p.post.xr[i] = __ldcg(p.post.xr + i) + sum;
+                }
+            }
+            __threadfence();
+            __syncthreads();
+            rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
+        }
+        __syncthreads();
+        if (t == 0) tp_reset(tp, p.post.tp_phase);
+    } else if (p.post.op == POST_RMSNORM) {
+        if (fast)
+            reduce_norm_xq_block(const_cast<float *>(p.post.x), nullptr, 0, nullptr, p.post.w, p.post.n, p.post.eps,
+                                 p.post.xq, xq_pad(p.post.n), rn_stage);
+        else
+            rmsnorm_xq_block(p.post.x, p.post.w, p.post.n, p.post.eps, p.post.xq, xq_pad(p.post.n), nullptr);
+    } else if (p.post.op == POST_FINISH) {
+        if (t == 0) finish_step(p.post.state, p.post.forced, p.post.out_tokens);
+    } else if (p.post.op == POST_TP_FINISH) {
+        // cross-rank argmax: every rank publishes its packed key, all take the max
+        // (the packing keeps the reference's first-index tie rule, cpu.zig:477-483)
+        if (t == 0) {
+            const TpComm &tp = p.post.tp;
+            const unsigned long long mine = __ldcg(&p.post.state->argmax64);
+            for (int q = 0; q < tp.size; q++) tp_am(tp, q)[tp.rank] = mine;
+            tp_signal(tp, TP_CTR_ARGMAX);
+            unsigned long long best = mine;
+            if (tp_wait(tp, TP_CTR_ARGMAX, (unsigned)tp.size)) {
+                for (int r = 0; r < tp.size; r++) {
+                    const unsigned long long k = __ldcv(tp_am(tp, tp.rank) + r);
+                    best = k > best ? k : best;
+                }
+            }
+            tp_reset(tp, TP_CTR_ARGMAX);
+            p.post.state->argmax64 = best;
+            finish_step(p.post.state, p.post.forced, p.post.out_tokens);
+        }
+    }
+    if (t == 0) *p.post.done = 0u;
 }
 
 // CTA of 4 warps = TPC = 4 / KW tiles of 16 rows, KW warps per tile splitting

@@ -117,17 +117,35 @@ static void residual_out(cuq_model *m, GemvArgs &a, int &epi, const float *bias,
     }
 }
 
+// cuq_profile_decode: record the next event of the pool after a launch, tagged
+// with the node being enqueued.
+static int prof_mark(cuq_model *m) {
+    if (m->prof_n >= m->prof_ev.size()) {
+        cudaEvent_t e;
+        CUQ_CUDA_TRY(cudaEventCreate(&e));
+        m->prof_ev.push_back(e);
+        m->prof_tag.push_back(0);
+    }
+    m->prof_tag[m->prof_n] = m->prof_node;
+    CUQ_CUDA_TRY(cudaEventRecord(m->prof_ev[m->prof_n], m->stream));
+    m->prof_n++;
+    return CUQ_OK;
+}
+
 static int enqueue_step(cuq_model *m) {
     const cuq_config &c = m->cfg, &lc = m->lc;
     cudaStream_t s = m->stream;
     const bool pdl = true;  // every launch below waits for its predecessor with griddepcontrol.wait
     int rc;
     uint64_t nk = 0;  // kernel launches in the step
-#define TRY(x)                       \
-    do {                             \
-        rc = (x);                    \
-        if (rc != CUQ_OK) return rc; \
-        nk++;                        \
+#define TRY(x)                                \
+    do {                                      \
+        rc = (x);                             \
+        if (rc != CUQ_OK) return rc;          \
+        nk++;                                 \
+        if (m->profiling) {                   \
+            if ((rc = prof_mark(m))) return rc; \
+        }                                     \
     } while (0)
     auto gemv = [&](const Planes &w, const __half *xq, float *y, const float *bias) {
         GemvArgs a;
@@ -139,13 +157,17 @@ static int enqueue_step(cuq_model *m) {
         a.counters = m->counters;
         a.ksplit = gemv_pick_ksplit(w, m->sm_count);
         a.pdl = pdl;
+        a.err = m->gemm_err;
         a.post.done = m->done;
         return a;
     };
-    // Single GPU: each RMSNorm is computed by every CTA of the GEMV that reads it
-    // (pre-norm), after its first weight loads are in flight, instead of by the
-    // last CTA of the GEMV that wrote the residual.
-    const bool pre = m->opt.tp_size == 1 && c.hidden % 16 == 0 && c.hidden <= RN_MAX;
+    // Single GPU with register-prefetch GEMVs: each RMSNorm is computed by every
+    // CTA of the GEMV that reads it (pre-norm), after its first weight loads are
+    // in flight, instead of by the last CTA of the GEMV that wrote the residual.
+    // TMA-fed GEMVs request all their weights at launch, before the activation
+    // exists, so the norm stays the producer's post-op (computed once) and runs
+    // while the consumer's weights stream in.
+    const bool pre = m->opt.tp_size == 1 && c.hidden % 16 == 0 && c.hidden <= RN_MAX && !m->all_tma;
     auto prenorm = [&](GemvArgs &a, const float *w) {
         if (!pre) return;
         a.pre_x = m->x;
@@ -154,6 +176,7 @@ static int enqueue_step(cuq_model *m) {
         a.pre_eps = c.eps;
     };
     // engine.zig:561-564 embedding (then layer 0's attention RMSNorm)
+    m->prof_node = CUQ_NODE_EMBED;
     if (pre)
         TRY(launch_embed_row(m->embed.p, &m->state->token, m->x, s));
     else
@@ -161,16 +184,19 @@ static int enqueue_step(cuq_model *m) {
     for (uint32_t l = 0; l < c.layers; l++) {
         Layer &L = m->layers[l];
         // qkv projection + bias (main.zig:435-436)
+        m->prof_node = CUQ_NODE_QKV;
         for (auto &seg : L.qkv) {
             GemvArgs a = gemv(seg.p, m->xq_h, m->qkv + seg.row_off, L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr);
             prenorm(a, L.attn_norm);
             TRY(launch_gemv(a, EPI_STORE, s));
         }
         // RoPE + fp16 KV write + attention (main.zig:457-472), this rank's heads
+        m->prof_node = CUQ_NODE_ATTN;
         TRY(launch_attention_step(m->qkv, m->rope_cs, m->state, L.k_cache, L.v_cache, m->opt.max_seq, lc.heads,
                                   lc.kv_heads, c.head_dim, c.rope_adjacent, m->attn_part, m->attn_nsplit, m->tickets,
                                   m->xq_attn, pdl, s));
         // o projection + o_bias into the residual (main.zig:477-485), then ffn RMSNorm (main.zig:487)
+        m->prof_node = CUQ_NODE_O;
         {
             GemvArgs a = gemv(L.o.p, m->xq_attn, nullptr, nullptr);
             int epi;
@@ -179,8 +205,10 @@ static int enqueue_step(cuq_model *m) {
             TRY(launch_gemv(a, epi, s));
         }
         // gate/up with the SiLU*mul epilogue (engine.zig:645-668 split path)
+        m->prof_node = CUQ_NODE_GATE_UP;
         if (L.gate_up_dual) {
             GemvArgs a = gemv(L.gate.p, m->xq_h, nullptr, nullptr);
+            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count, 2);
             a.w2 = &L.up.p;
             a.xq_out = m->xq_act;
             prenorm(a, L.ffn_norm);
@@ -197,6 +225,7 @@ static int enqueue_step(cuq_model *m) {
         }
         // down projection into the residual, then the next RMSNorm (next layer's
         // attention norm, or the final norm before the lm_head, main.zig:532)
+        m->prof_node = CUQ_NODE_DOWN;
         {
             GemvArgs a = gemv(L.down.p, m->xq_act, nullptr, nullptr);
             int epi;
@@ -208,6 +237,7 @@ static int enqueue_step(cuq_model *m) {
     // lm_head with the fused argmax (main.zig:534, cpu.zig:477-483); the last CTA
     // turns the argmax into the next step's token (generate.zig:217-244), after
     // the cross-rank argmax under tensor parallelism.
+    m->prof_node = CUQ_NODE_HEAD;
     {
         GemvArgs a = gemv(head_proj(m).p, m->xq_h, m->logits, nullptr);
         prenorm(a, m->final_norm);
@@ -267,6 +297,7 @@ static int enqueue_head(cuq_model *m, const float *x_row, bool pdl) {
     a.counters = m->counters;
     a.ksplit = gemv_pick_ksplit(head.p, m->sm_count);
     a.pdl = pdl;
+    a.err = m->gemm_err;
     a.post.done = m->done;
     a.post.op = m->opt.tp_size > 1 ? POST_TP_FINISH : POST_FINISH;
     a.post.tp = m->tpc;
@@ -821,7 +852,7 @@ int cuq_model_finalize(cuq_model *m) {
     }
     size_t ws_need = 0, ctr_need = 0;
     auto account = [&](const Planes &p, int dual) {
-        int k = gemv_pick_ksplit(p, m->sm_count);
+        int k = gemv_pick_ksplit(p, m->sm_count, dual ? 2 : 1);
         if (k > 1) {
             size_t need = (size_t)k * p.rows * (dual ? 2 : 1);
             if (need > ws_need) ws_need = need;
@@ -895,6 +926,16 @@ int cuq_model_finalize(cuq_model *m) {
         free_pending(m->pend_output);
     }
     account(head_proj(m).p, 0);
+    {
+        // every decode GEMV on the TMA-fed kernel: the norms stay post-ops
+        bool all = gemv_tma_supported(head_proj(m).p.type);
+        for (auto &L : m->layers) {
+            for (auto &sg : L.qkv) all = all && gemv_tma_supported(sg.p.type);
+            all = all && gemv_tma_supported(L.o.p.type) && gemv_tma_supported(L.gate.p.type) &&
+                  gemv_tma_supported(L.up.p.type) && gemv_tma_supported(L.down.p.type) && L.gate_up_dual;
+        }
+        m->all_tma = all;
+    }
     m->ws_floats = ws_need;
     m->n_counters = ctr_need + 1;
     if (ws_need) CUQ_CUDA_TRY(cudaMalloc(&m->ws, sizeof(float) * ws_need));
@@ -999,6 +1040,15 @@ static int finish_call(cuq_model *m, uint32_t n_steps, float *logits_host, uint3
     if (mega_ran && *m->err_host) {
         set_error("persistent decode: a grid barrier was not reached within its wait limit");
         return CUQ_ETIMEOUT;
+    }
+    if (m->gemm_err) {
+        int herr = 0;
+        CUQ_CUDA_TRY(cudaMemcpy(&herr, m->gemm_err, sizeof(int), cudaMemcpyDeviceToHost));
+        if (herr) {
+            cudaMemset(m->gemm_err, 0, sizeof(int));
+            set_error("decode: a weight-stream wait timed out");
+            return CUQ_ETIMEOUT;
+        }
     }
     if (m->tp_err) {
         int herr = 0;
@@ -1123,6 +1173,45 @@ int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_ste
     return CUQ_OK;
 }
 
+// Rows [pos0, pos0 + n) of one layer's cache between the reference's host
+// layout [pos][kv_heads * hd] (full width) and the device's [kv_head][max_seq][hd]
+// (this rank's heads): one strided copy per local KV head and tensor.
+static int kv_copy(const cuq_model *m, uint32_t layer, uint32_t pos0, uint32_t n, uint16_t *k_host, uint16_t *v_host,
+                   bool to_device) {
+    CUQ_CHECK_ARG(m && k_host && v_host, "cuq_kv_%s: null argument", to_device ? "write" : "read");
+    CUQ_CHECK_ARG(layer < m->cfg.layers && (uint64_t)pos0 + n <= m->opt.max_seq,
+                  "cuq_kv_%s: layer %u rows [%u, %u) outside the cache (%u layers, max_seq %u)",
+                  to_device ? "write" : "read", layer, pos0, pos0 + n, m->cfg.layers, m->opt.max_seq);
+    if (n == 0) return CUQ_OK;
+    const uint32_t hd = m->cfg.head_dim, kvd = m->cfg.kv_heads * hd;
+    const uint32_t h0 = (uint32_t)m->opt.tp_rank * m->lc.kv_heads;  // this rank's first KV head
+    const cuq::Layer &L = m->layers[layer];
+    for (uint32_t h = 0; h < m->lc.kv_heads; h++) {
+        __half *kd = L.k_cache + ((size_t)h * m->opt.max_seq + pos0) * hd;
+        __half *vd = L.v_cache + ((size_t)h * m->opt.max_seq + pos0) * hd;
+        uint16_t *kh = k_host + (size_t)(h0 + h) * hd, *vh = v_host + (size_t)(h0 + h) * hd;
+        const size_t w = sizeof(__half) * hd, hp = sizeof(uint16_t) * kvd;
+        if (to_device) {
+            CUQ_CUDA_TRY(cudaMemcpy2DAsync(kd, w, kh, hp, w, n, cudaMemcpyHostToDevice, m->stream));
+            CUQ_CUDA_TRY(cudaMemcpy2DAsync(vd, w, vh, hp, w, n, cudaMemcpyHostToDevice, m->stream));
+        } else {
+            CUQ_CUDA_TRY(cudaMemcpy2DAsync(kh, hp, kd, w, w, n, cudaMemcpyDeviceToHost, m->stream));
+            CUQ_CUDA_TRY(cudaMemcpy2DAsync(vh, hp, vd, w, w, n, cudaMemcpyDeviceToHost, m->stream));
+        }
+    }
+    CUQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    return CUQ_OK;
+}
+
+int cuq_kv_write(cuq_model *m, uint32_t layer, uint32_t pos0, uint32_t n, const uint16_t *k_host,
+                 const uint16_t *v_host) {
+    return kv_copy(m, layer, pos0, n, const_cast<uint16_t *>(k_host), const_cast<uint16_t *>(v_host), true);
+}
+
+int cuq_kv_read(const cuq_model *m, uint32_t layer, uint32_t pos0, uint32_t n, uint16_t *k_host, uint16_t *v_host) {
+    return kv_copy(m, layer, pos0, n, k_host, v_host, false);
+}
+
 int cuq_reset(cuq_model *m) {
     CUQ_CHECK_ARG(m, "cuq_reset: null model");
     // Engine.reset (engine.zig:1479): the cache is simply overwritten from position 0
@@ -1140,6 +1229,67 @@ int cuq_model_stats(const cuq_model *m, cuq_stats *out) {
     CUQ_CHECK_ARG(m && out, "cuq_model_stats: null argument");
     *out = m->stats;
     out->persistent_ctas = m->mega.impl ? (uint64_t)m->mega.grid : 0;
+    return CUQ_OK;
+}
+
+int cuq_profile_decode(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps, cuq_node_time *out) {
+    CUQ_CHECK_ARG(m && out && n_steps > 0, "cuq_profile_decode: bad argument");
+    if (!m->finalized) {
+        set_error("cuq_profile_decode: model not finalized");
+        return CUQ_ENOTREADY;
+    }
+    if (m->mega.impl) {
+        set_error("cuq_profile_decode: per-op decode only (not the persistent kernel)");
+        return CUQ_EUNSUPPORTED;
+    }
+    if ((uint64_t)pos + n_steps > m->opt.max_seq) {
+        set_error("ContextOverflow: %u + %u > max_seq %u", pos, n_steps, m->opt.max_seq);
+        return CUQ_ECONTEXT;
+    }
+    int rc = check_token(m, token);
+    if (rc) return rc;
+    CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, &token, sizeof(uint32_t), cudaMemcpyHostToDevice, m->stream));
+    if ((rc = set_state(m, (int)token, (int)pos, 1))) return rc;
+    m->prof_n = 0;
+    m->prof_node = -1;
+    m->profiling = true;
+    rc = prof_mark(m);  // the start of the first launch
+    for (uint32_t i = 0; i < n_steps && rc == CUQ_OK; i++) rc = enqueue_step(m);
+    m->profiling = false;
+    if (rc) {
+        cudaStreamSynchronize(m->stream);
+        return rc;
+    }
+    CUQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
+    for (int k = 0; k < CUQ_NODES; k++) out[k] = cuq_node_time{0, 0.0, 0.0};
+    for (size_t i = 1; i < m->prof_n; i++) {
+        float ms = 0.f;
+        CUQ_CUDA_TRY(cudaEventElapsedTime(&ms, m->prof_ev[i - 1], m->prof_ev[i]));
+        const int k = m->prof_tag[i];
+        if (k < 0 || k >= CUQ_NODES) continue;
+        out[k].launches++;
+        out[k].ms += ms;
+    }
+    // algorithmic bytes: the weights as stored, and the K/V rows attention reads
+    const cuq_config &c = m->cfg, &lc = m->lc;
+    double wq = 0, wo = 0, wgu = 0, wd = 0;
+    for (auto &L : m->layers) {
+        for (auto &sg : L.qkv) wq += (double)sg.p.nbytes;
+        wo += (double)L.o.p.nbytes;
+        wgu += (double)L.gate.p.nbytes + (double)L.up.p.nbytes;
+        wd += (double)L.down.p.nbytes;
+    }
+    double kv = 0;
+    for (uint32_t i = 0; i < n_steps; i++) kv += 2.0 * (pos + i + 1) * kv_dim(lc) * sizeof(__half) * c.layers;
+    const double n = n_steps;
+    out[CUQ_NODE_EMBED].bytes = n * (double)m->embed.p.nbytes / c.vocab;
+    out[CUQ_NODE_QKV].bytes = n * wq;
+    out[CUQ_NODE_ATTN].bytes = kv;
+    out[CUQ_NODE_O].bytes = n * wo;
+    out[CUQ_NODE_GATE_UP].bytes = n * wgu;
+    out[CUQ_NODE_DOWN].bytes = n * wd;
+    out[CUQ_NODE_HEAD].bytes = n * (double)head_proj(m).p.nbytes;
+    m->stats.tokens += n_steps;
     return CUQ_OK;
 }
 
@@ -1182,6 +1332,7 @@ void cuq_model_free(cuq_model *m) {
     if (m->out_host) cudaFreeHost(m->out_host);
     if (m->err_host) cudaFreeHost(m->err_host);
     mega_free(m->mega);
+    for (cudaEvent_t e : m->prof_ev) cudaEventDestroy(e);
     if (m->ev0) cudaEventDestroy(m->ev0);
     if (m->ev1) cudaEventDestroy(m->ev1);
     if (m->stream) cudaStreamDestroy(m->stream);

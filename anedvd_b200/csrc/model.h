@@ -39,6 +39,7 @@ struct cuq_model {
     uint32_t vocab_base = 0;     // first lm_head row (global token id) held by this rank
     cuq_options opt{};
     bool finalized = false;
+    bool all_tma = false;        // every decode GEMV runs the TMA-fed kernel
     int sm_count = 148;
     cudaStream_t stream = nullptr;
     std::vector<cuq::Layer> layers;
@@ -80,6 +81,13 @@ struct cuq_model {
     cuq::MegaProgram mega;                       // persistent decode kernel (decode_kernel != PER_OP)
     bool mega_ran = false;                       // launched since the last finish_call
     int *err_host = nullptr;                     // pinned: its error flag read back by finish_call
+
+    // cuq_profile_decode: an event after every launch, tagged with its node
+    bool profiling = false;
+    int prof_node = 0;
+    std::vector<cudaEvent_t> prof_ev;
+    std::vector<int> prof_tag;
+    size_t prof_n = 0;
 
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;

@@ -45,11 +45,11 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, float c, float s) 
     b = nb;
 }
 
-__global__ void rope_kernel(float *v, uint32_t heads, uint32_t hd, const float *__restrict__ cs_row, int adjacent) {
+__global__ void rope_kernel(float *v, uint32_t heads, uint32_t hd, const RopeRow cs_row, int adjacent) {
     const uint32_t half = hd / 2;
     for (uint32_t t = threadIdx.x + blockIdx.x * blockDim.x; t < heads * half; t += blockDim.x * gridDim.x) {
         uint32_t h = t / half, i = t % half;
-        float c = cs_row[i], s = cs_row[half + i];
+        float c = cs_row.v[i], s = cs_row.v[half + i];
         float *base = v + (size_t)h * hd;
         if (adjacent)
             rope_pair(base[2 * i], base[2 * i + 1], c, s);
@@ -240,7 +240,20 @@ int launch_rmsnorm(float *out, const float *x, const float *w, uint32_t n, uint3
     return CUQ_OK;
 }
 
-int launch_rope(float *v, uint32_t heads, uint32_t hd, const float *cs_row, int adjacent, cudaStream_t s) {
+__global__ void hilo_sum_kernel(const __half *__restrict__ hi, const __half *__restrict__ lo, size_t count,
+                                float *__restrict__ out) {
+    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < count; i += (size_t)gridDim.x * blockDim.x)
+        out[i] = __half2float(hi[i]) + __half2float(lo[i]);
+}
+
+int launch_hilo_sum(const __half *hi, const __half *lo, size_t count, float *out, cudaStream_t s) {
+    const size_t blocks = (count + 255) / 256;
+    hilo_sum_kernel<<<(unsigned)(blocks < 4096 ? blocks : 4096), 256, 0, s>>>(hi, lo, count, out);
+    CUQ_CUDA_TRY(cudaGetLastError());
+    return CUQ_OK;
+}
+
+int launch_rope(float *v, uint32_t heads, uint32_t hd, const RopeRow &cs_row, int adjacent, cudaStream_t s) {
     rope_kernel<<<1, 256, 0, s>>>(v, heads, hd, cs_row, adjacent);
     CUQ_CUDA_TRY(cudaGetLastError());
     return CUQ_OK;

@@ -6,7 +6,11 @@ namespace cuq {
 
 int launch_rmsnorm(float *out, const float *x, const float *w, uint32_t n, uint32_t n_rows, float eps,
                    cudaStream_t s);
-int launch_rope(float *v, uint32_t heads, uint32_t hd, const float *cs_row, int adjacent, cudaStream_t s);
+// One position's cos | sin row (hd <= 256), passed to the kernel by value.
+struct RopeRow {
+    float v[256];
+};
+int launch_rope(float *v, uint32_t heads, uint32_t hd, const RopeRow &cs_row, int adjacent, cudaStream_t s);
 // cs: [max_seq][hd] table, each row cos(0..hd/2) then sin(0..hd/2).
 int launch_rope_cache(const float *qkv, uint32_t qkv_stride, float *q_out, __half *k_cache, __half *v_cache,
                       uint32_t cache_stride, const float *cs, const int *pos_ptr, uint32_t pos_val, uint32_t n_tok,
@@ -33,6 +37,8 @@ int launch_rmsnorm_hilo(const float *x, const float *w, uint32_t n, uint32_t n_r
 int launch_attention_prefill(const float *q, const __half *k_cache, const __half *v_cache, uint32_t cache_stride,
                              uint32_t pos0, uint32_t n_q, uint32_t heads, uint32_t kv_heads, uint32_t hd,
                              __half *oh, __half *ol, cudaStream_t s);
+// out[i] = hi[i] + lo[i] in fp32 (an activation split into fp16 hi and lo planes).
+int launch_hilo_sum(const __half *hi, const __half *lo, size_t count, float *out, cudaStream_t s);
 int launch_silu_hilo(const float *g, const float *u, size_t count, __half *hi, __half *lo, cudaStream_t s);
 int launch_embed_rows(const Planes &p, const uint32_t *ids, uint32_t n, float *x, cudaStream_t s);
 int launch_silu_mul(float *out, const float *g, const float *u, uint32_t n, cudaStream_t s);

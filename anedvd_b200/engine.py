@@ -131,6 +131,28 @@ class Engine:
     def reset(self):
         rt.check(rt.load().cuq_reset(self._h))
 
+    def kv_write(self, layer, pos0, k16, v16):
+        """Replace cache rows [pos0, pos0 + n) of `layer` (fp16 bits [n][kv_heads*head_dim])."""
+        k = np.ascontiguousarray(k16, dtype=np.uint16)
+        v = np.ascontiguousarray(v16, dtype=np.uint16)
+        n = k.size // (self.cfg.kv_heads * self.cfg.head_dim)
+        rt.check(rt.load().cuq_kv_write(self._h, layer, pos0, n, _ptr(k), _ptr(v)))
+
+    def kv_read(self, layer, pos0, n):
+        """Cache rows [pos0, pos0 + n) of `layer` as fp16 bits ([n][kv_heads*head_dim] each for k, v)."""
+        kvd = self.cfg.kv_heads * self.cfg.head_dim
+        k = np.zeros((n, kvd), dtype=np.uint16)
+        v = np.zeros((n, kvd), dtype=np.uint16)
+        rt.check(rt.load().cuq_kv_read(self._h, layer, pos0, n, _ptr(k), _ptr(v)))
+        return k, v
+
+    def profile_decode(self, token, pos, n_steps):
+        """Per-node decode timing (cuq_profile_decode, the `anedvd kernels` table):
+        {node: (launches, ms, algorithmic bytes)} over n_steps eager steps."""
+        tab = (rt.CuqNodeTime * len(rt.NODE_NAMES))()
+        rt.check(rt.load().cuq_profile_decode(self._h, token, pos, n_steps, tab))
+        return {name: (int(t.launches), float(t.ms), float(t.bytes)) for name, t in zip(rt.NODE_NAMES, tab)}
+
     @property
     def stats(self):
         s = rt.CuqStats()
@@ -147,19 +169,69 @@ class Engine:
         return rt.load().cuq_model_stream(self._h)
 
 
+def reuse_length(cached, prompt):
+    """generate.zig:456-460 reuseLength: how many leading prompt tokens may keep
+    their KV rows.  Only a prompt that covers the WHOLE cached sequence may reuse
+    it (a cache longer than the shared prefix would leave stale rows in front of
+    the new tokens); otherwise nothing is reused."""
+    n = min(len(cached), len(prompt))
+    shared = 0
+    while shared < n and int(cached[shared]) == int(prompt[shared]):
+        shared += 1
+    return shared if shared >= len(cached) else 0
+
+
 class Session:
-    """Session.generate (generate.zig:166-250), greedy: the decode loop runs on the device."""
+    """Session.generate (generate.zig:166-250), greedy: the decode loop runs on the device.
+
+    Like the reference's session it remembers which token ids the engine's KV
+    cache holds, and a prompt that extends them (a multi-turn transcript) only
+    prefills its new suffix (generate.zig:187-192)."""
 
     def __init__(self, engine, max_seq):
         self.engine = engine
         self.max_seq = max_seq
+        self.cached = []      # token ids whose K/V rows the cache holds, in position order
+        self.last = {}        # counters of the last call, as the reference's Stats
+
+    def reset(self):
+        self.engine.reset()
+        self.cached = []
 
     def generate(self, ids, n_decode):
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
-        # generate.zig:171-185: keep the tail of a prompt that does not fit
-        room = self.max_seq - n_decode + 1
-        if ids.size > room:
-            ids = ids[ids.size - room:]
+        sent = int(ids.size)
+        # generate.zig:171-185: keep the newest tokens of a prompt that does not
+        # leave room for the answer (and say how many were dropped)
+        if ids.size + n_decode + 1 > self.max_seq:
+            keep = self.max_seq - n_decode - 1
+            if keep <= 0:
+                raise rt.CuqError(rt.ECONTEXT, "PromptTooLong: %d prompt + %d decode > max_seq %d"
+                                  % (ids.size, n_decode, self.max_seq))
+            ids = ids[ids.size - keep:]
+        reuse = reuse_length(self.cached, ids)
+        # a prompt identical to the cache still needs its last position run for
+        # the first token's logits: recompute that one row (same values)
+        reuse = min(reuse, ids.size - 1)
+        if reuse == 0:
+            self.cached = []
+        self.last = {"prompt_tokens_sent": sent, "prompt_tokens": int(ids.size),
+                     "prompt_tokens_dropped": sent - int(ids.size), "prefill_reused": int(reuse)}
         out = np.empty(n_decode, dtype=np.uint32)
-        rt.check(rt.load().cuq_generate(self.engine._h, _ptr(ids), ids.size, n_decode, _ptr(out)))
+        L = rt.load()
+        if reuse == 0:
+            # prefill from position 0 and decode on the device in one call
+            rt.check(L.cuq_generate(self.engine._h, _ptr(ids), ids.size, n_decode, _ptr(out)))
+        else:
+            tail = np.ascontiguousarray(ids[reuse:])
+            am = ctypes.c_uint32(0)
+            rt.check(L.cuq_prefill(self.engine._h, _ptr(tail), tail.size, reuse, None, ctypes.byref(am)))
+            out[0] = am.value
+            if n_decode > 1:
+                rest = np.empty(n_decode - 1, dtype=np.uint32)
+                rt.check(L.cuq_decode_greedy(self.engine._h, am.value, ids.size, n_decode - 1, _ptr(rest)))
+                out[1:] = rest
+        # the cache now holds the prompt and every generated token but the last
+        # (which was produced, not yet fed back)
+        self.cached = [int(t) for t in ids] + [int(t) for t in out[:-1]]
         return out

@@ -44,6 +44,7 @@ SIGNATURES = [
     ("cuq_silu_mul", I32, [P, P, P, U32, P]),
     ("cuq_attention_decode", I32, [P, P, P, P, U32, U32, U32, U32, U32, P]),
     ("cuq_attention_decode_noalloc", I32, [P, P, P, P, U32, U32, U32, U32, U32, P]),
+    ("cuq_attention_prefill", I32, [P, P, P, P, U32, U32, U32, U32, U32, U32, P]),
     ("cuq_argmax", I32, [P, U32, P, P]),
     ("cuq_model_create", P, [P, P]),
     ("cuq_upload_tensor", I32, [P, I32, I32, I32, P, SZ, U32, U32]),
@@ -59,8 +60,11 @@ SIGNATURES = [
     ("cuq_prefill", I32, [P, P, U32, U32, P, P]),
     ("cuq_generate", I32, [P, P, U32, U32, P]),
     ("cuq_decode_greedy", I32, [P, U32, U32, U32, P]),
+    ("cuq_kv_write", I32, [P, U32, U32, U32, P, P]),
+    ("cuq_kv_read", I32, [P, U32, U32, U32, P, P]),
     ("cuq_reset", I32, [P]),
     ("cuq_model_stats", I32, [P, P]),
+    ("cuq_profile_decode", I32, [P, U32, U32, U32, P]),
     ("cuq_model_stream", P, [P]),
     ("cuq_model_free", None, [P]),
 ]
@@ -86,6 +90,13 @@ class CuqStats(ctypes.Structure):
                 ("prefill_ms", ctypes.c_double), ("weight_bytes", U64), ("kv_bytes", U64),
                 ("graph_replays", U64), ("kernels_per_step", U64),
                 ("kernel_launches", U64), ("persistent_ctas", U64)]
+
+
+NODE_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "lm_head"]
+
+
+class CuqNodeTime(ctypes.Structure):
+    _fields_ = [("launches", U64), ("ms", ctypes.c_double), ("bytes", ctypes.c_double)]
 
 
 class CuqError(RuntimeError):

@@ -4,31 +4,40 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                     [--config c2|c3|c4|c5] [--profile gemv]
 
-Workloads are BASELINE.json's configs (random-init synthetic models of the
-named architectures, seeded random prompt ids):
-  c2  SmolLM2-135M-arch, Q8_0, 16-token prompt + 128 greedy tokens  (default at N=1)
+Workloads are the configs of the benchmark (random-init synthetic models of
+the named architectures, seeded random prompt ids):
+  c2  SmolLM2-135M-arch, Q8_0, 16-token prompt + 128 greedy tokens
   c3  Qwen2.5-0.5B-arch, Q8_0, 203 + 256
   c4  Qwen2.5-1.5B-arch, Q4_K_M mix, 2048 + 256
-  c5  Llama-3-8B-arch, Q4_K_M mix, 4096 + 512  (default at N>1: tensor parallel over the N ranks)
+  c5  Llama-3-8B-arch, Q4_K_M mix, 4096 + 512  (the default: 1 GPU, or tensor
+      parallel over the N ranks of a torchrun launch)
 
 A step is one generation: prefill the prompt, then the decode tokens.  `value`
 is decode tokens/s over the timed steps (device time from CUDA events on the
 engine's stream, max over ranks); `prefill` reports the prompt pass the same
 way.  `e2e` is the same workload through the public API (cuq_generate: host
 prompt ids in, host tokens out) timed by the host clock, prefill included.
-`roofline` measures the config's largest GEMV (the lm_head, this rank's shard
-under tensor parallelism) alone: CUDA events around back-to-back launches over
-rotating weight copies larger than L2.  L2 (126 MB) is flushed between timed
-steps.
+`kernels` is the per-node table of cuq_profile_decode (8 decode steps in the
+timed window, one launch at a time with a CUDA event after each on the
+engine's stream); `roofline` is that table's dominant node (algorithmic bytes
+per launch / mean launch time) and `step_hbm` the whole decode step (weights +
+the K/V rows read, per token, at the measured tok/s).  L2 (126 MB) is flushed
+between timed steps; the weights (4.6 GB for c5) are far larger than L2.
 
 N > 1 (torchrun): c5 runs tensor-parallel (one sequence, strong scaling: value
 is that sequence's tokens/s); c2-c4 do not shard and run one replica per rank
 (weak scaling: value = all ranks' tokens / max rank time).
 `--impl reference`: the reference CPU path (the C oracle restating src/cpu.zig
 + main.zig refForward; the Zig reference cannot be built here) on all host
-cores, rank 0 only, on a bounded sample of the same workload.
-`--profile gemv`: 6 launches of the roofline GEMV only; `--profile qgemm`: 4
-prefill GEMMs of the config's first ffn_gate on 2048 tokens (for ncu captures).
+cores, rank 0 only (the other ranks exit at once), loaded once; each step
+times decode tokens at positions inside the same decode window as this arm
+(the attention walks the same number of cached positions; a CPU prefill of
+the 4096-token prompt would take hours, and the work of a decode step does not
+depend on the cached values).
+`--profile gemv`: 6 launches of the config's lm_head GEMV only; `--profile
+qgemm`: 4 prefill GEMMs of the config's first ffn_gate on 2048 tokens;
+`--profile prefill` / `decode`: the model's prefill twice / 4 eager decode
+steps (for ncu captures; nothing is printed).
 """
 import argparse
 import ctypes
@@ -46,19 +55,19 @@ sys.path.insert(0, ROOT)
 
 CONFIGS = {
     "c2": dict(model="smollm2-135m", prompt=16, decode=128, payload="quantized", head="token_embd.weight",
-               ref_sample=(4, 4), cpu_sample=(16, 48), cpu_threads=1,
+               ref_tokens=8, cpu_tokens=48, cpu_threads=1,
                desc="c2: SmolLM2-135M-arch Q8_0 (30 layers, hidden 576, vocab 49152), batch-1 greedy decode of 128 "
                     "tokens after a 16-token prompt"),
     "c3": dict(model="qwen2.5-0.5b", prompt=203, decode=256, payload="tiled", head="token_embd.weight",
-               ref_sample=(2, 2), cpu_sample=(2, 6), cpu_threads=1,
+               ref_tokens=4, cpu_tokens=12, cpu_threads=1,
                desc="c3: Qwen2.5-0.5B-arch Q8_0 (24 layers, hidden 896, vocab 151936), 203-token prompt + 256 "
                     "greedy tokens"),
     "c4": dict(model="qwen2.5-1.5b", prompt=2048, decode=256, payload="tiled", head="token_embd.weight",
-               ref_sample=(1, 2), cpu_sample=(1, 4), cpu_threads=0,
+               ref_tokens=2, cpu_tokens=8, cpu_threads=0,
                desc="c4: Qwen2.5-1.5B-arch Q4_K_M mix (28 layers, hidden 1536, vocab 151936), 2048-token prompt + "
                     "256 greedy tokens"),
     "c5": dict(model="llama3-8b", prompt=4096, decode=512, payload="tiled", head="output.weight",
-               ref_sample=(1, 1), cpu_sample=(1, 2), cpu_threads=0,
+               ref_tokens=2, cpu_tokens=8, cpu_threads=0,
                desc="c5: Llama-3-8B-arch Q4_K_M mix (32 layers, hidden 4096, vocab 128256 untied), 4096-token "
                     "prompt + 512 greedy tokens"),
 }
@@ -160,26 +169,55 @@ def prompt_ids(vocab, n, seed=0):
     return np.random.default_rng(seed).integers(0, vocab, size=n).astype(np.uint32)
 
 
-def cpu_baseline(model, threads, n_prompt, n_decode):
-    """The oracle (CPU restatement of the reference path) on a bounded sample:
-    decode tokens/s after an n_prompt-token prompt."""
-    from oracle import oracle as orc
-    ref = orc.Model(model.cfg, threads=threads, max_seq=n_prompt + n_decode + 1)
-    ref.load(model)
-    ids = prompt_ids(model.cfg.vocab, n_prompt)
-    for p, t in enumerate(ids):
-        lg = ref.forward(int(t), p)
-    tok = orc.argmax(lg)
-    t0 = time.perf_counter()
-    for s in range(n_decode):
-        lg = ref.forward(tok, n_prompt + s)
-        tok = orc.argmax(lg)
-    dt = time.perf_counter() - t0
-    return n_decode / dt
+class CpuReference:
+    """The oracle (CPU restatement of the reference path, refForward in the
+    reference's per-row order) for one config, loaded once.  Decode tokens are
+    timed at positions inside the config's decode window: a decode step's work
+    (every weight once, attention over pos + 1 cached rows) does not depend on
+    the cached values, so no CPU prefill of the prompt is needed first."""
+
+    def __init__(self, model, C, threads):
+        from oracle import oracle as orc
+        self.orc = orc
+        self.C = C
+        self.threads = threads
+        self.ref = orc.Model(model.cfg, threads=threads, max_seq=C["prompt"] + C["decode"] + 1)
+        self.ref.load(model)
+        self.vocab = model.cfg.vocab
+        self.k = 0
+
+    def positions(self, n):
+        """n positions spread over the decode window [prompt, prompt + decode)."""
+        P, D = self.C["prompt"], self.C["decode"]
+        out = []
+        for _ in range(n):
+            out.append(P + (self.k * 97) % D)
+            self.k += 1
+        return out
+
+    def time_tokens(self, n):
+        """Seconds for n decode tokens (greedy: each token is the previous argmax)."""
+        tok = 1
+        t0 = time.perf_counter()
+        for pos in self.positions(n):
+            tok = self.orc.argmax(self.ref.forward(tok, pos))
+        return time.perf_counter() - t0
+
+    def sample_desc(self, n, what):
+        return ("%s: %d greedy decode tokens at positions spread over the decode window [%d, %d) of the same "
+                "workload, oracle refForward (rows and query heads split across %d threads, reference per-row "
+                "order)" % (what, n, self.C["prompt"], self.C["prompt"] + self.C["decode"], self.threads))
 
 
 def pick_config(args, world):
-    return args.config or ("c2" if world == 1 else "c5")
+    return args.config or "c5"
+
+
+def line_config(C, name, world, tp):
+    parallelism = ("tensor parallel x%d" % world) if tp else ("replicas x%d" % world if world > 1 else "single GPU")
+    return {"workload": C["desc"], "model": C["model"], "prompt": C["prompt"], "decode": C["decode"],
+            "parallelism": parallelism,
+            "l2": "flushed between timed steps (256 MB write); the weights stream from HBM every token"}
 
 
 def run_reference(args, world, rank):
@@ -188,25 +226,25 @@ def run_reference(args, world, rank):
     from anedvd_b200 import synth
     name = pick_config(args, world)
     C = CONFIGS[name]
+    tp = world > 1 and name == "c5"
     model = synth.model(C["model"], payload=C["payload"], cache=False)
     threads = os.cpu_count() or 1
-    n_prompt, n_decode = C["ref_sample"]
-    vals = []
+    ref = CpuReference(model, C, threads)
+    n_tok = C["ref_tokens"]
+    dt = 0.0
     for i in range(args.warmup + args.steps):
-        v = cpu_baseline(model, threads, n_prompt, n_decode)
+        t = ref.time_tokens(n_tok)
         if i >= args.warmup:
-            vals.append(v)
-    value = float(np.mean(vals))
+            dt += t
+    value = n_tok * args.steps / dt
     print(json.dumps({
         "impl": "reference", "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-        "scaling": "strong" if (world > 1 and name == "c5") else "weak", "vs_baseline": None, "dtype": "f32",
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3 / args.steps, "higher_is_better": True,
+        "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "f32",
         "data": DATA[C["payload"]],
-        "config": {"workload": C["desc"], "model": C["model"], "prompt": C["prompt"], "decode": C["decode"]},
+        "config": line_config(C, name, world, tp),
         "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": "per step: %d-token prompt then %d greedy decode tokens timed, oracle refForward "
-                                   "(rows split across %d threads, reference per-row order)"
-                                   % (n_prompt, n_decode, threads)},
+                         "sample": ref.sample_desc(n_tok, "per step")},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
@@ -272,6 +310,13 @@ def gemv_roofline(ttype, raw, rows, cols, stream_ptr, pk, label, reps=64):
     return {"kernel": "gemv_kernel<%s> (%s %dx%d)" % (tname, label, rows, cols), "bound": "hbm",
             "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
             "traffic": traffic, "algorithmic_bytes": alg, "launch_us": ms * 1e3}
+
+
+# the kernel behind each node of the per-op decode step
+NODE_KERNEL = {"embed": "embed_row_kernel", "qkv": "gemv_kernel, RMSNorm per CTA + q||k||v",
+               "attention": "attn_step_kernel", "o": "gemv_kernel + residual",
+               "gate_up": "dual gemv_kernel, RMSNorm per CTA + gate|up + SiLU*mul",
+               "down": "gemv_kernel + residual", "lm_head": "gemv_kernel + argmax"}
 
 
 def run_ours(args, world, rank, local):
@@ -349,21 +394,51 @@ def run_ours(args, world, rank, local):
     e2e_s = max_over_ranks(time.perf_counter() - t0, world)
     e2e = n_decode * args.steps * seqs / e2e_s
 
-    ttype, raw, rows, cols = head_shard(model, C, rank if tp else 0, world if tp else 1)
-    roof = gemv_roofline(ttype, raw, rows, cols, stream_ptr, pk, "%s lm_head" % name) if rank == 0 else None
+    # per-node decode table (cuq_profile_decode) in the timed decode window;
+    # the roofline is its dominant node, the step fraction the whole token
+    _, first = eng.prefill(ids, 0, want_logits=False)
+    n_prof = 8
+    table = eng.profile_decode(first, n_prompt, n_prof)
+    kernels = {k: {"launches": v[0], "ms": v[1], "bytes": v[2],
+                   "us_per_launch": (1e3 * v[1] / v[0]) if v[0] else None,
+                   "gbs": (v[2] / (v[1] * 1e-3) / 1e9) if v[1] > 0 else None} for k, v in table.items()}
+    dom = max(kernels, key=lambda k: kernels[k]["ms"])
+    dk_ = kernels[dom]
+    per_launch_bytes = dk_["bytes"] / max(dk_["launches"], 1)
+    achieved = dk_["gbs"]
+    traffic = None
+    try:
+        prof = json.load(open(os.path.join(ROOT, "profiles", "roofline_traffic.json")))
+        traffic = prof.get("%s %s" % (name, dom), {}).get("dram_bytes_per_launch")
+    except (OSError, ValueError):
+        pass
+    roof = {"kernel": "%s node of the %s decode step (%s)" % (dom, name, NODE_KERNEL.get(dom, dom)), "bound": "hbm",
+            "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
+            "traffic": traffic, "algorithmic_bytes": per_launch_bytes, "launch_us": dk_["us_per_launch"],
+            "timing": "in-step, %d decode steps at positions %d..%d, CUDA events after every launch on the "
+                      "engine's stream (no graph, no overlap between kernels)" % (n_prof, n_prompt,
+                                                                                 n_prompt + n_prof - 1),
+            "share_of_step": dk_["ms"] / sum(v["ms"] for v in kernels.values())}
+    # whole step: this rank's weights once + the K/V rows over the decode window, per token
+    wlocal = sum(v["bytes"] for k, v in kernels.items() if k != "attention") / n_prof
+    cfg = model.cfg
+    kvd_local = cfg.kv_heads * cfg.head_dim // (world if tp else 1)
+    kv_avg = 2 * 2 * kvd_local * cfg.layers * (n_prompt + (n_decode + 1) / 2.0)
+    step_bytes = wlocal + kv_avg
+    step_gbs = step_bytes * value / seqs / 1e9
+    step_hbm = {"bytes_per_token": step_bytes, "weight_bytes_per_token": wlocal, "kv_bytes_per_token": kv_avg,
+                "achieved": step_gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": step_gbs / pk["hbm_gbs"]}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        n_p, n_d = C["cpu_sample"]
         threads = C["cpu_threads"] or (os.cpu_count() or 1)
-        cpu = {"value": cpu_baseline(model, threads, n_p, n_d), "unit": "tok/s", "cores": threads, "kind": "port",
-               "sample": "%d-token prompt, then %d greedy decode tokens timed; %s, oracle refForward in the "
-                         "reference's per-row order" % (n_p, n_d, "single thread (the reference engine is "
-                                                                   "single-threaded)" if threads == 1 else
-                                                        "rows split across %d threads" % threads)}
+        ref = CpuReference(model, C, threads)
+        ref.time_tokens(1)  # warm-up
+        n_tok = C["cpu_tokens"]
+        cpu = {"value": n_tok / ref.time_tokens(n_tok), "unit": "tok/s", "cores": threads, "kind": "port",
+               "sample": ref.sample_desc(n_tok, "bounded sample")}
+        del ref
     wbytes = model.weight_bytes_per_token()
     if rank == 0:
-        parallelism = ("tensor parallel x%d" % world) if tp else ("replicas x%d" % world if world > 1 else
-                                                                  "single GPU")
         line = {
             "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": (dec_ms_max + pre_ms_max) / args.steps,
@@ -371,16 +446,15 @@ def run_ours(args, world, rank, local):
             "dtype": "%s weights dequantized exactly to fp16, fp16 tensor-core MMA with fp32 accumulate, fp32 "
                      "activations (split hi+lo fp16)" % ("q8_0" if name in ("c2", "c3") else "q4_k/q6_k"),
             "data": DATA[C["payload"]],
-            "config": {"workload": C["desc"], "model": C["model"], "prompt": n_prompt, "decode": n_decode,
-                       "parallelism": parallelism,
-                       "decode_kernel": ("persistent, %d CTAs" % eng.persistent_ctas) if persistent else
-                                        "one kernel per op (CUDA graph per step)",
-                       "l2": "flushed between steps (256 MB write); weights %.1f MB" % (wbytes / 1e6)},
+            "config": line_config(C, name, world, tp),
+            "decode_kernel": ("persistent, %d CTAs" % eng.persistent_ctas) if persistent else
+                             "one kernel per op (CUDA graph per step)",
             "prefill": {"tok_per_s": prefill_tps, "ms": pre_ms_max / args.steps},
             "weight_bytes_per_token": wbytes,
             "weight_stream_gbs": wbytes * value / seqs / 1e9,
             "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 4 * n_prompt + 4 * 1,
                     "d2h_bytes_per_step": 4 * n_decode},
+            "kernels": kernels, "step_hbm": step_hbm,
             "roofline": roof, "peak_kind": pk_kind, "cpu_baseline": cpu,
             "gpu_launches": int(launches),
             "kernels_per_token": (1.0 / n_decode) if persistent else int(kps),
@@ -402,7 +476,7 @@ def profile_case(args):
     rt.load()
     rt.init(0)
     torch.cuda.set_device(0)
-    name = args.config or "c2"
+    name = args.config or "c5"
     C = CONFIGS[name]
     model = synth.model(C["model"], payload=C["payload"], cache=False)
     if args.profile == "gemv":
@@ -422,18 +496,19 @@ def profile_case(args):
             rt.check(L.cuq_gemm(h, ctypes.c_void_p(x.data_ptr()), 2048, ctypes.c_void_p(y.data_ptr()), None))
         L.cuq_weight_free(h)
     elif args.profile in ("prefill", "decode"):
-        # the config's prompt prefilled twice (chunks of 2048), or prefilled once
-        # and 8 tokens decoded with one kernel per op and no graph, so every
-        # launch of a step shows in a launch list
+        # prefill: the config's prompt prefilled twice (chunks of 2048).
+        # decode: 4 tokens decoded at the first decode position with one kernel
+        # per op and no graph, so every launch of a step shows in a launch list;
+        # no prefill first (the KV cache is zeros: the same work per step)
         from anedvd_b200 import engine as E
         ids = prompt_ids(model.cfg.vocab, C["prompt"])
         eng = E.Engine.from_synth(model, max_seq=C["prompt"] + 16, max_chunk=2048,
                                   use_graphs=args.profile == "prefill")
-        _, first = eng.prefill(ids, 0, want_logits=False)
         if args.profile == "prefill":
             eng.prefill(ids, 0, want_logits=False)
+            eng.prefill(ids, 0, want_logits=False)
         else:
-            eng.decode_greedy(first, C["prompt"], 8)
+            eng.decode_greedy(1, C["prompt"], 4)
         eng.close()
     torch.cuda.synchronize()
 
@@ -443,12 +518,13 @@ def main():
     if args.profile:
         profile_case(args)
         return
+    if args.impl == "reference":
+        # CPU only, rank 0 alone: no process group (the other ranks exit at once)
+        run_reference(args, int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0")))
+        return
     world, rank, local = dist_init()
     try:
-        if args.impl == "reference":
-            run_reference(args, world, rank)
-        else:
-            run_ours(args, world, rank, local)
+        run_ours(args, world, rank, local)
     finally:
         if world > 1:
             import torch.distributed as dist

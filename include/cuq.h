@@ -11,7 +11,8 @@
  *   - "host" arguments are ordinary CPU memory owned by the caller;
  *   - "dev" arguments are CUDA device pointers on the current device;
  *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream);
- *     op entry points only enqueue work and return.
+ *     op entry points only enqueue work and return (cuq_gemm excepted: it
+ *     waits for its stream, see there).
  * Status: CUQ_OK (0) on success, a negative CUQ_E* code on failure, with
  * cuq_last_error() describing it.
  */
@@ -110,7 +111,10 @@ int cuq_prepare_x(const float *x_dev, uint32_t n, uint16_t *xq_dev, void *stream
 int cuq_gemv_prepared(const cuq_weight *w, const uint16_t *xq_dev, float *y_dev, void *stream);
 
 /* Y[n][rows] = X[n][cols] W^T for a chunk of n tokens (the prefill projection,
- * engine.zig:975-1329).  X, Y float32 row-major, dev. */
+ * engine.zig:975-1329).  X, Y float32 row-major, dev.  Returns after the GEMM
+ * has run (it synchronises `stream`): the tensor-core pipeline's bounded waits
+ * report through a device flag, read here, so a wait that gave up comes back
+ * as CUQ_ETIMEOUT from this call. */
 int cuq_gemm(const cuq_weight *w, const float *x_dev, uint32_t n, float *y_dev, void *stream);
 
 /* Dequantise W to fp16 [rows][cols] exactly as Gguf.readF16 (gguf.zig:554-578) does:
@@ -133,6 +137,14 @@ int cuq_silu_mul(float *out_dev, const float *g_dev, const float *u_dev, uint32_
 int cuq_attention_decode(float *out_dev, const float *q_dev, const uint16_t *k_dev,
                          const uint16_t *v_dev, uint32_t n_past, uint32_t cache_stride,
                          uint32_t heads, uint32_t kv_heads, uint32_t hd, void *stream);
+/* cpu.attentionPrefill (cpu.zig:165-217): causal attention of `n` prompt
+ * queries at positions pos0 .. pos0+n-1.  q [n][heads*hd] f32 (already
+ * rotated), out [n][heads*hd] f32; k/v fp16 caches [kv_heads][cache_stride][hd]
+ * holding positions [0, pos0 + n).  Query i sees positions [0, pos0 + i].  The
+ * tensor-core kernel the engine's prefill runs. */
+int cuq_attention_prefill(float *out_dev, const float *q_dev, const uint16_t *k_dev, const uint16_t *v_dev,
+                          uint32_t n, uint32_t pos0, uint32_t cache_stride, uint32_t heads, uint32_t kv_heads,
+                          uint32_t hd, void *stream);
 /* cuq_attention_decode without any allocation.  No counterpart in the
  * reference: it exists for callers that may not allocate device memory while
  * they run (an engine that reserved all device memory up front, or a loop that
@@ -276,9 +288,45 @@ int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t 
  * prefill/forward at position `pos` with next token `token` (no prefill). */
 int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps,
                       uint32_t *out_tokens);
+/* The fp16 KV cache of one layer, rows [pos0, pos0 + n) in the reference's
+ * layout (engine.zig:447-458, 966-969: row p holds kv_heads * head_dim halves,
+ * KV head major), host memory.  cuq_kv_write replaces the rows (a session
+ * restored from elsewhere, or a cache shared with another engine); cuq_kv_read
+ * copies them out.  Under tensor parallelism the rows are full width and each
+ * rank reads / writes its own KV heads (cuq_kv_read leaves the other heads'
+ * columns untouched).  Both synchronise the model's stream. */
+int cuq_kv_write(cuq_model *m, uint32_t layer, uint32_t pos0, uint32_t n, const uint16_t *k_host,
+                 const uint16_t *v_host);
+int cuq_kv_read(const cuq_model *m, uint32_t layer, uint32_t pos0, uint32_t n, uint16_t *k_host,
+                uint16_t *v_host);
 /* Engine.reset (engine.zig:1479): forget the KV cache. */
 int cuq_reset(cuq_model *m);
 int cuq_model_stats(const cuq_model *m, cuq_stats *out);
+/* Per-kernel decode timing, in the shape of the reference's `anedvd kernels`
+ * table (main.zig:1729-1791) and its per-node counters (engine.zig:83-131
+ * Stats.node_ns): `n_steps` decode steps from (`token`, `pos`) are enqueued one
+ * launch at a time (no CUDA graph) with a CUDA event recorded on the model's
+ * stream after every launch, and each launch's time (event to event: the
+ * kernel plus its launch gap, with no overlap between consecutive kernels) is
+ * added to its node.  `bytes` is the node's algorithmic traffic over the steps:
+ * weight bytes as stored (this rank's shard), plus the fp16 K/V rows the
+ * attention reads.  The KV cache and decode state advance as in cuq_forward;
+ * under tensor parallelism every rank makes the call together.  Per-op decode
+ * only (CUQ_EUNSUPPORTED with the persistent decode kernel). */
+#define CUQ_NODE_EMBED 0    /* embedding row */
+#define CUQ_NODE_QKV 1      /* q||k||v projection (+ its RMSNorm) */
+#define CUQ_NODE_ATTN 2     /* RoPE + KV write + attention */
+#define CUQ_NODE_O 3        /* o projection + residual */
+#define CUQ_NODE_GATE_UP 4  /* gate|up projections + SiLU*mul (+ RMSNorm) */
+#define CUQ_NODE_DOWN 5     /* down projection + residual */
+#define CUQ_NODE_HEAD 6     /* final RMSNorm + lm_head + argmax */
+#define CUQ_NODES 7
+typedef struct {
+    uint64_t launches;  /* kernel launches of this node over the steps */
+    double ms;          /* summed launch times */
+    double bytes;       /* algorithmic bytes over the steps */
+} cuq_node_time;
+int cuq_profile_decode(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps, cuq_node_time *out);
 /* The stream the model enqueues on (cudaStream_t as void*). */
 void *cuq_model_stream(const cuq_model *m);
 void cuq_model_free(cuq_model *m);

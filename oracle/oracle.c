@@ -614,34 +614,158 @@ static float dot_f32_f16(const float *a, const uint16_t *b, size_t n) {
 }
 
 /* cpu.zig:323-395 (window = 0, softcap = 0, scale = 1/sqrt(hd)). */
-void orc_attention_decode(float *out, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
-                          size_t n_past, uint32_t heads, uint32_t kv_heads, uint32_t hd) {
+/* One query head of cpu.attentionDecode: qh [hd]; kh / vh point at its KV
+ * head's first column, rows `row_stride` halves apart. */
+void orc_attention_decode_strided(float *oh, const float *qh, const uint16_t *kh, const uint16_t *vh,
+                                  size_t row_stride, size_t n_past, uint32_t hd) {
     pthread_once(&f16tab_once, f16tab_init);
-    size_t kv_dim = (size_t)kv_heads * hd;
-    uint32_t group = heads / kv_heads;
     float scale = 1.0f / sqrtf((float)hd);
     float *scores = (float *)malloc((n_past ? n_past : 1) * sizeof(float));
     if (!scores) return;
-    for (uint32_t h = 0; h < heads; h++) {
-        uint32_t kvh = h / group;
-        const float *qh = q + (size_t)h * hd;
-        for (size_t t = 0; t < n_past; t++) {
-            float d = dot_f32_f16(qh, k_cache + t * kv_dim + (size_t)kvh * hd, hd);
-            scores[t] = d * scale;
-        }
-        orc_softmax(scores, n_past);
-        float *oh = out + (size_t)h * hd;
-        for (uint32_t d = 0; d < hd; d++) oh[d] = 0;
-        for (size_t t = 0; t < n_past; t++) {
-            const uint16_t *vt = v_cache + t * kv_dim + (size_t)kvh * hd;
-            float w = scores[t];
-            for (uint32_t d = 0; d < hd; d++) {
-                float p = w * h2f(vt[d]);
-                oh[d] = oh[d] + p;
-            }
+    for (size_t t = 0; t < n_past; t++) {
+        float d = dot_f32_f16(qh, kh + t * row_stride, hd);
+        scores[t] = d * scale;
+    }
+    orc_softmax(scores, n_past);
+    for (uint32_t d = 0; d < hd; d++) oh[d] = 0;
+    for (size_t t = 0; t < n_past; t++) {
+        const uint16_t *vt = vh + t * row_stride;
+        float w = scores[t];
+        for (uint32_t d = 0; d < hd; d++) {
+            float p = w * h2f(vt[d]);
+            oh[d] = oh[d] + p;
         }
     }
     free(scores);
+}
+
+void orc_attention_decode(float *out, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                          size_t n_past, uint32_t heads, uint32_t kv_heads, uint32_t hd) {
+    size_t kv_dim = (size_t)kv_heads * hd;
+    uint32_t group = heads / kv_heads;
+    for (uint32_t h = 0; h < heads; h++) {
+        uint32_t kvh = h / group;
+        orc_attention_decode_strided(out + (size_t)h * hd, q + (size_t)h * hd, k_cache + (size_t)kvh * hd,
+                                     v_cache + (size_t)kvh * hd, kv_dim, n_past, hd);
+    }
+}
+
+/* orc_attention_decode with the query heads split across threads: each head's
+ * scores, softmax and weighted sum are computed exactly as above, by one
+ * thread, so the result does not depend on the split. */
+typedef struct {
+    float *out;
+    const float *q;
+    const uint16_t *k_cache, *v_cache;
+    size_t n_past;
+    uint32_t heads, kv_heads, hd, h0, h1;
+} att_job;
+
+static void *att_thread(void *arg) {
+    att_job *j = (att_job *)arg;
+    const uint32_t group = j->heads / j->kv_heads;
+    const size_t kv_dim = (size_t)j->kv_heads * j->hd;
+    for (uint32_t h = j->h0; h < j->h1; h++) {
+        /* one query head at a time through the single-threaded routine, on a
+         * one-head view (its KV head's columns at their offset in the row) */
+        const uint32_t kvh = h / group;
+        orc_attention_decode_strided(j->out + (size_t)h * j->hd, j->q + (size_t)h * j->hd,
+                                     j->k_cache + (size_t)kvh * j->hd, j->v_cache + (size_t)kvh * j->hd, kv_dim,
+                                     j->n_past, j->hd);
+    }
+    return NULL;
+}
+
+static void attention_decode_threads(float *out, const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                                     size_t n_past, uint32_t heads, uint32_t kv_heads, uint32_t hd, int threads) {
+    if (threads <= 1 || n_past < 256) {
+        orc_attention_decode(out, q, k_cache, v_cache, n_past, heads, kv_heads, hd);
+        return;
+    }
+    if ((uint32_t)threads > heads) threads = (int)heads;
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    att_job jobs[256];
+    int ok[256];
+    uint32_t per = (heads + (uint32_t)threads - 1) / (uint32_t)threads;
+    for (int t = 0; t < threads; t++) {
+        uint32_t h0 = (uint32_t)t * per, h1 = h0 + per < heads ? h0 + per : heads;
+        jobs[t] = (att_job){out, q, k_cache, v_cache, n_past, heads, kv_heads, hd, h0, h0 < heads ? h1 : h0};
+        ok[t] = pthread_create(&tid[t], NULL, att_thread, &jobs[t]) == 0;
+        if (!ok[t]) att_thread(&jobs[t]);
+    }
+    for (int t = 0; t < threads; t++)
+        if (ok[t]) pthread_join(tid[t], NULL);
+}
+
+/* cpu.attentionPrefill (cpu.zig:165-217): causal attention of n_q prompt
+ * queries starting at position q_pos0.  Query qi, head h, dim d is
+ * q[(h * hd + d) * chan_stride + qi * col_stride] (the engine's channel-major
+ * layout when chan_stride > 1; position-major with chan_stride 1, col_stride
+ * heads * hd); out uses the same layout.  Query qi sees cache positions
+ * [0, min(n_past, q_pos0 + qi + 1)), with the same dot / softmax / fp16 axpy
+ * as attentionDecode.  Queries are split across threads (each query's result
+ * is computed by one thread, so the split does not change it). */
+typedef struct {
+    float *out;
+    const float *q;
+    size_t chan_stride, col_stride;
+    const uint16_t *k_cache, *v_cache;
+    size_t n_past, q_pos0, qi0, qi1;
+    uint32_t heads, kv_heads, hd;
+} pf_job;
+
+static void *pf_thread(void *arg) {
+    pf_job *j = (pf_job *)arg;
+    const size_t hd = j->hd, kv_dim = (size_t)j->kv_heads * hd;
+    const uint32_t group = j->heads / j->kv_heads;
+    float *qs = (float *)malloc(hd * sizeof(float)), *os = (float *)malloc(hd * sizeof(float));
+    if (!qs || !os) {
+        free(qs);
+        free(os);
+        return NULL;
+    }
+    for (size_t qi = j->qi0; qi < j->qi1; qi++) {
+        const size_t pos = j->q_pos0 + qi;
+        const size_t visible = j->n_past < pos + 1 ? j->n_past : pos + 1;
+        const size_t col = qi * j->col_stride;
+        for (uint32_t h = 0; h < j->heads; h++) {
+            const uint32_t kvh = h / group;
+            const size_t base = (size_t)h * hd * j->chan_stride + col;
+            for (size_t d = 0; d < hd; d++) qs[d] = j->q[base + d * j->chan_stride];
+            orc_attention_decode_strided(os, qs, j->k_cache + (size_t)kvh * hd, j->v_cache + (size_t)kvh * hd,
+                                         kv_dim, visible, (uint32_t)hd);
+            for (size_t d = 0; d < hd; d++) j->out[base + d * j->chan_stride] = os[d];
+        }
+    }
+    free(qs);
+    free(os);
+    return NULL;
+}
+
+void orc_attention_prefill(float *out, const float *q, size_t chan_stride, size_t col_stride,
+                           const uint16_t *k_cache, const uint16_t *v_cache, size_t n_past, size_t n_q,
+                           size_t q_pos0, uint32_t heads, uint32_t kv_heads, uint32_t hd, int threads) {
+    pthread_once(&f16tab_once, f16tab_init);
+    if (threads < 1) threads = 1;
+    if (threads > 256) threads = 256;
+    if ((size_t)threads > n_q) threads = n_q ? (int)n_q : 1;
+    pthread_t tid[256];
+    pf_job jobs[256];
+    int ok[256];
+    /* interleaved ranges would balance the causal work better; contiguous
+     * ranges of equal length keep it simple */
+    size_t per = (n_q + (size_t)threads - 1) / (size_t)threads;
+    for (int t = 0; t < threads; t++) {
+        size_t a = (size_t)t * per, b = a + per < n_q ? a + per : n_q;
+        if (a > n_q) a = n_q;
+        jobs[t] = (pf_job){out, q, chan_stride, col_stride, k_cache, v_cache, n_past, q_pos0, a, b,
+                           heads, kv_heads, hd};
+        ok[t] = threads > 1 && pthread_create(&tid[t], NULL, pf_thread, &jobs[t]) == 0;
+        if (!ok[t]) pf_thread(&jobs[t]);
+    }
+    for (int t = 0; t < threads; t++)
+        if (ok[t]) pthread_join(tid[t], NULL);
 }
 
 /* cpu.zig:477-483: first index of the maximum (strict >). */
@@ -726,6 +850,64 @@ void orc_model_free(orc_model *m) {
 
 /* load_gguf.loadLinear (load_gguf.zig:358-386) for a tensor whose dims are
  * already [in][out] in ggml order (payload row-major [out][in]). */
+/* orc_read_f16 split into contiguous element ranges across threads.  Every
+ * element is dequantised and rounded on its own, so the result does not depend
+ * on the split; ranges start on multiples of 2048 elements (whole blocks of
+ * every type, the chunking of gguf.zig:554-578). */
+typedef struct {
+    int type;
+    const uint8_t *src;
+    size_t src_len, e0, e1;
+    uint16_t *out;
+    int rc;
+} rf16_job;
+
+static void *rf16_thread(void *arg) {
+    rf16_job *j = (rf16_job *)arg;
+    float buf[2048];
+    j->rc = ORC_OK;
+    for (size_t done = j->e0; done < j->e1;) {
+        size_t k = j->e1 - done < 2048 ? j->e1 - done : 2048;
+        int rc = orc_dequant_range(j->type, j->src, j->src_len, done, buf, k);
+        if (rc) {
+            j->rc = rc;
+            break;
+        }
+        orc_f32_to_f16_n(buf, j->out + done, k);
+        done += k;
+    }
+    return NULL;
+}
+
+static int read_f16_threads(int type, const uint8_t *src, size_t src_len, uint16_t *out, size_t n, int threads) {
+    if (threads <= 1 || type == ORC_F16 || n < (size_t)1 << 20) return orc_read_f16(type, src, src_len, out, n);
+    pthread_once(&f16tab_once, f16tab_init);
+    if (threads > 256) threads = 256;
+    pthread_t tid[256];
+    rf16_job jobs[256];
+    size_t per = (n + (size_t)threads - 1) / (size_t)threads;
+    per = (per + 2047) & ~(size_t)2047;
+    int started = 0, rc = ORC_OK;
+    for (int t = 0; t < threads; t++) {
+        size_t e0 = (size_t)t * per, e1 = e0 + per < n ? e0 + per : n;
+        if (e0 >= n) break;
+        jobs[t] = (rf16_job){type, src, src_len, e0, e1, out, ORC_OK};
+        if (pthread_create(&tid[t], NULL, rf16_thread, &jobs[t]) != 0) {
+            rf16_thread(&jobs[t]);  /* no thread: do it here */
+            if (jobs[t].rc) rc = jobs[t].rc;
+            jobs[t].src = NULL;
+            continue;
+        }
+        started = t + 1;
+    }
+    for (int t = 0; t < started; t++) {
+        if (!jobs[t].src) continue;
+        pthread_join(tid[t], NULL);
+        if (jobs[t].rc) rc = jobs[t].rc;
+    }
+    return rc;
+}
+
 int orc_model_set_linear(orc_model *m, int layer, int role, int type, const uint8_t *raw, size_t nbytes,
                          uint32_t rows, uint32_t cols) {
     const orc_config *c = &m->c;
@@ -765,7 +947,7 @@ int orc_model_set_linear(orc_model *m, int layer, int role, int type, const uint
     default: return ORC_ESHAPE;
     }
     if (!dst) return ORC_ENOMEM;
-    return orc_read_f16(type, raw, nbytes, dst, n);
+    return read_f16_threads(type, raw, nbytes, dst, n, c->threads);
 }
 
 int orc_model_set_f32(orc_model *m, int layer, int role, const float *v, size_t n) {
@@ -830,8 +1012,8 @@ int orc_model_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits)
             L->k_cache[(size_t)pos * kvd + i] = orc_f32_to_f16(k[i]);
             L->v_cache[(size_t)pos * kvd + i] = orc_f32_to_f16(v[i]);
         }
-        orc_attention_decode(m->attn, q, L->k_cache, L->v_cache, (size_t)pos + 1, c->heads, c->kv_heads,
-                             c->head_dim);
+        attention_decode_threads(m->attn, q, L->k_cache, L->v_cache, (size_t)pos + 1, c->heads, c->kv_heads,
+                                 c->head_dim, thr);
         orc_matvec_f16(m->proj, L->o, m->attn, H, qd, thr);
         if (L->o_bias)
             for (size_t i = 0; i < H; i++) m->proj[i] = m->proj[i] + L->o_bias[i];
@@ -846,11 +1028,25 @@ int orc_model_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits)
     orc_rmsnorm(m->h, m->x, m->final_norm, H, c->eps);
     const uint16_t *head = c->tie_embeddings ? m->embed : m->output;
     if (!head) return ORC_ESHAPE;
-    orc_matvec_f16(logits, head, m->h, c->vocab, H, thr);
+    /* logits == NULL: a prompt position whose logits nobody reads (the engine's
+     * prefill computes the head for the last position only, engine.zig:1310-1316) */
+    if (logits) orc_matvec_f16(logits, head, m->h, c->vocab, H, thr);
     return ORC_OK;
 }
 
 const float *orc_model_last_hidden(const orc_model *m) { return m->h; }
+
+/* Overwrite cache rows [pos0, pos0 + n) of `layer` with fp16 rows [n][kv_dim]
+ * (test infrastructure: the GPU engine gets the same rows through cuq_kv_write,
+ * so both continue from one cache state). */
+int orc_model_set_kv(orc_model *m, uint32_t layer, uint32_t pos0, uint32_t n, const uint16_t *k, const uint16_t *v) {
+    const orc_config *c = &m->c;
+    if (layer >= c->layers || (uint64_t)pos0 + n > c->max_seq) return ORC_ESHAPE;
+    size_t kvd = kv_dim(c);
+    memcpy(m->layers[layer].k_cache + (size_t)pos0 * kvd, k, (size_t)n * kvd * 2);
+    memcpy(m->layers[layer].v_cache + (size_t)pos0 * kvd, v, (size_t)n * kvd * 2);
+    return ORC_OK;
+}
 
 int orc_model_kv_row(const orc_model *m, uint32_t layer, uint32_t pos, uint16_t *k, uint16_t *v) {
     const orc_config *c = &m->c;

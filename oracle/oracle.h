@@ -62,6 +62,11 @@ void orc_silu_mul(float *out, const float *g, const float *u, size_t n);        
 float orc_exp_approx(float x);                                                       /* cpu.zig:269-283 */
 void orc_softmax(float *s, size_t n);                                                /* cpu.zig:220-249 */
 /* cpu.zig:323-395 with the default AttnOpts (no softcap, no window). */
+void orc_attention_decode_strided(float *oh, const float *qh, const uint16_t *kh, const uint16_t *vh,
+                                  size_t row_stride, size_t n_past, uint32_t hd);
+void orc_attention_prefill(float *out, const float *q, size_t chan_stride, size_t col_stride,
+                           const uint16_t *k_cache, const uint16_t *v_cache, size_t n_past, size_t n_q,
+                           size_t q_pos0, uint32_t heads, uint32_t kv_heads, uint32_t hd, int threads);
 void orc_attention_decode(float *out, const float *q, const uint16_t *k_cache,
                           const uint16_t *v_cache, size_t n_past, uint32_t heads,
                           uint32_t kv_heads, uint32_t hd);
@@ -101,6 +106,8 @@ int orc_model_forward(orc_model *m, uint32_t token, uint32_t pos, float *logits)
 /* Hidden state after the final RMSNorm of the last forward (for per-stage checks). */
 const float *orc_model_last_hidden(const orc_model *m);
 /* Read back a fp16 KV-cache row: [layer][pos][kv_dim]. */
+int orc_model_set_kv(orc_model *m, uint32_t layer, uint32_t pos0, uint32_t n, const uint16_t *k,
+                     const uint16_t *v);
 int orc_model_kv_row(const orc_model *m, uint32_t layer, uint32_t pos, uint16_t *k, uint16_t *v);
 
 #ifdef __cplusplus

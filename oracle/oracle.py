@@ -79,6 +79,10 @@ def lib():
         L.orc_model_last_hidden.argtypes = [P]
         L.orc_model_last_hidden.restype = ctypes.POINTER(ctypes.c_float)
         L.orc_model_kv_row.argtypes = [P, ctypes.c_uint32, ctypes.c_uint32, P, P]
+        L.orc_model_set_kv.argtypes = [P, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32, P, P]
+        L.orc_attention_prefill.argtypes = [P, P, ctypes.c_size_t, ctypes.c_size_t, P, P, ctypes.c_size_t,
+                                            ctypes.c_size_t, ctypes.c_size_t, ctypes.c_uint32, ctypes.c_uint32,
+                                            ctypes.c_uint32, ctypes.c_int]
         _lib = L
     return _lib
 
@@ -179,6 +183,19 @@ def attention_decode(q, k_cache16, v_cache16, n_past, heads, kv_heads, hd):
     return out
 
 
+def attention_prefill(q, k_cache16, v_cache16, n_past, q_pos0, heads, kv_heads, hd, threads=8):
+    """cpu.attentionPrefill on position-major q [n_q][heads*hd] (float32) and fp16
+    caches [pos][kv_heads*hd] (uint16 bits); returns [n_q][heads*hd]."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    n_q = q.shape[0]
+    k = np.ascontiguousarray(k_cache16, dtype=np.uint16)
+    v = np.ascontiguousarray(v_cache16, dtype=np.uint16)
+    out = np.empty((n_q, heads * hd), dtype=np.float32)
+    lib().orc_attention_prefill(_ptr(out), _ptr(q), 1, heads * hd, _ptr(k), _ptr(v), n_past, n_q, q_pos0, heads,
+                                kv_heads, hd, threads)
+    return out
+
+
 def argmax(v):
     v = np.ascontiguousarray(v, dtype=np.float32)
     return int(lib().orc_argmax(_ptr(v), v.size))
@@ -225,9 +242,11 @@ class Model:
             else:
                 self.set_linear(t.layer, t.role, t.ggml_type, t.data, t.rows, t.cols)
 
-    def forward(self, token, pos):
-        logits = np.empty(self.cfg.vocab, dtype=np.float32)
-        rc = lib().orc_model_forward(self._h, token, pos, _ptr(logits))
+    def forward(self, token, pos, want_logits=True):
+        """One refForward step; without want_logits the lm_head is skipped
+        (returns None) and only the KV cache and hidden state advance."""
+        logits = np.empty(self.cfg.vocab, dtype=np.float32) if want_logits else None
+        rc = lib().orc_model_forward(self._h, token, pos, _ptr(logits) if want_logits else None)
         if rc:
             raise ValueError("orc_model_forward failed: %d" % rc)
         return logits
@@ -235,6 +254,15 @@ class Model:
     def last_hidden(self):
         p = lib().orc_model_last_hidden(self._h)
         return np.ctypeslib.as_array(p, shape=(self.cfg.hidden,)).copy()
+
+    def set_kv(self, layer, pos0, k16, v16):
+        """Overwrite cache rows [pos0, pos0 + n) with fp16 bits [n][kv_dim]."""
+        k = np.ascontiguousarray(k16, dtype=np.uint16)
+        v = np.ascontiguousarray(v16, dtype=np.uint16)
+        n = k.size // (self.cfg.kv_heads * self.cfg.head_dim)
+        rc = lib().orc_model_set_kv(self._h, layer, pos0, n, _ptr(k), _ptr(v))
+        if rc:
+            raise ValueError("set_kv failed: %d" % rc)
 
     def kv_row(self, layer, pos):
         kvd = self.cfg.kv_heads * self.cfg.head_dim

@@ -208,3 +208,59 @@ def test_missing_tensor_is_reported():
     assert L.cuq_model_finalize(h) == rt.EINVAL
     assert "MissingTensor" in rt.last_error()
     L.cuq_model_free(h)
+
+
+def test_profile_decode_table():
+    """cuq_profile_decode (the per-kernel table): every node of every step is
+    timed once per launch, the bytes follow the weights and the cached rows, and
+    the decode state advances as with cuq_forward."""
+    m = synth.model("qwen2.5-0.5b", layers=2, vocab=1024)
+    ref = orc.Model(m.cfg, threads=8, max_seq=32)
+    ref.load(m)
+    eng = E.Engine.from_synth(m, max_seq=32)
+    ids = _prompt(m.cfg, 5)
+    for p, t in enumerate(ids):
+        ref.forward(int(t), p)
+    eng.prefill(ids)
+    n = 3
+    tab = eng.profile_decode(7, len(ids), n)
+    c = m.cfg
+    assert tab["qkv"][0] >= n * c.layers and tab["attention"][0] == n * c.layers
+    assert tab["o"][0] == n * c.layers and tab["down"][0] == n * c.layers and tab["lm_head"][0] == n
+    assert all(v[1] > 0 for k, v in tab.items() if v[0])
+    kvd = c.kv_heads * c.head_dim
+    want_kv = sum(2 * 2 * kvd * c.layers * (len(ids) + i + 1) for i in range(n))
+    assert tab["attention"][2] == want_kv
+    # the three profiled steps decoded tokens 7, then the greedy argmax: the next
+    # forward continues from there like the oracle does
+    tok = 7
+    for i in range(n):
+        tok = orc.argmax(ref.forward(tok, len(ids) + i))
+    got, _ = eng.forward(tok, len(ids) + n)
+    want = ref.forward(tok, len(ids) + n)
+    assert rel_err(got, want) < LOGIT_TOL
+    eng.close()
+
+
+def test_session_reuses_the_kv_prefix_of_a_growing_transcript():
+    """generate.zig:187-192: a second turn whose prompt extends the first turn's
+    prompt and answer prefills only the new suffix, and decodes the same tokens
+    as a fresh engine given the whole second prompt."""
+    m = synth.model("smollm2-135m", layers=2, vocab=1024)
+    eng = E.Engine.from_synth(m, max_seq=96)
+    sess = E.Session(eng, 96)
+    p1 = _prompt(m.cfg, 12, salt=7)
+    t1 = sess.generate(p1, 8)
+    assert sess.last["prefill_reused"] == 0
+    p2 = np.concatenate([p1, t1, _prompt(m.cfg, 5, salt=8)])
+    t2 = sess.generate(p2, 10)
+    assert sess.last["prefill_reused"] == p1.size + t1.size - 1
+    fresh = E.Engine.from_synth(m, max_seq=96)
+    want = E.Session(fresh, 96).generate(p2, 10)
+    assert list(t2) == list(want)
+    # a prompt that does not cover the cache starts over
+    t3 = sess.generate(p2[:10], 4)
+    assert sess.last["prefill_reused"] == 0
+    assert list(t3) == list(E.Session(fresh, 96).generate(p2[:10], 4))
+    eng.close()
+    fresh.close()

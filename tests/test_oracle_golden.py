@@ -223,3 +223,21 @@ def test_matvec_order_is_thread_independent():
     for i in range(257):
         acc = (acc + (wf[:, i] * x[i]).astype(np.float32)).astype(np.float32)
     assert np.array_equal(a.view(np.uint32), acc.view(np.uint32))
+
+
+def test_attention_prefill_is_per_query_decode():
+    """cpu.attentionPrefill (cpu.zig:165-217) runs, for each query, the same dot /
+    softmax / fp16 axpy as attentionDecode (cpu.zig:323-395) over the positions
+    up to its own: the restatement must agree with the decode one bit for bit,
+    threaded or not."""
+    rng = np.random.default_rng(5)
+    heads, kv_heads, hd, n_past, n_q, pos0 = 6, 2, 64, 70, 20, 50
+    q = rng.standard_normal((n_q, heads * hd)).astype(np.float32)
+    k = (rng.standard_normal((n_past, kv_heads * hd)) * 0.5).astype(np.float16).view(np.uint16)
+    v = rng.standard_normal((n_past, kv_heads * hd)).astype(np.float16).view(np.uint16)
+    got1 = orc.attention_prefill(q, k, v, n_past, pos0, heads, kv_heads, hd, threads=1)
+    got4 = orc.attention_prefill(q, k, v, n_past, pos0, heads, kv_heads, hd, threads=4)
+    assert np.array_equal(got1.view(np.uint32), got4.view(np.uint32))
+    for i in range(n_q):
+        want = orc.attention_decode(q[i], k, v, min(n_past, pos0 + i + 1), heads, kv_heads, hd)
+        assert np.array_equal(got1[i].view(np.uint32), want.view(np.uint32)), i
