@@ -221,10 +221,6 @@ static int ensure_xq(cuq_weight *w, size_t halves) {
 int cuq_gemv(const cuq_weight *wc, const float *x_dev, float *y_dev, void *stream) {
     CUQ_CHECK_ARG(wc && x_dev && y_dev, "cuq_gemv: null argument");
     cuq_weight *w = const_cast<cuq_weight *>(wc);
-    if (w->p.raw) {
-        set_error("UnsupportedType: no GEMV for ggml type %d", w->p.type);
-        return CUQ_EUNSUPPORTED;
-    }
     cudaStream_t s = (cudaStream_t)stream;
     int rc = ensure_xq(w, xq_halves(w->p.cols));
     if (rc) return rc;
@@ -249,10 +245,6 @@ int cuq_prepare_x(const float *x_dev, uint32_t n, uint16_t *xq_dev, void *stream
 
 int cuq_gemv_prepared(const cuq_weight *w, const uint16_t *xq_dev, float *y_dev, void *stream) {
     CUQ_CHECK_ARG(w && xq_dev && y_dev, "cuq_gemv_prepared: null argument");
-    if (w->p.raw) {
-        set_error("UnsupportedType: no GEMV for ggml type %d", w->p.type);
-        return CUQ_EUNSUPPORTED;
-    }
     GemvArgs a;
     a.w = &w->p;
     a.xq = (const __half *)xq_dev;
@@ -265,10 +257,6 @@ int cuq_gemv_prepared(const cuq_weight *w, const uint16_t *xq_dev, float *y_dev,
 
 int cuq_weight_dequant_f16(const cuq_weight *w, uint16_t *out_dev, void *stream) {
     CUQ_CHECK_ARG(w && out_dev, "cuq_weight_dequant_f16: null argument");
-    if (w->p.raw) {
-        set_error("UnsupportedType: ggml type %d is kept raw", w->p.type);
-        return CUQ_EUNSUPPORTED;
-    }
     return launch_dequant_planes_f16(w->p, (__half *)out_dev, (cudaStream_t)stream);
 }
 

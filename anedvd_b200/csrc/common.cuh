@@ -86,7 +86,9 @@ __host__ __device__ inline int block_bytes(int t) {
 //          sc  int8  [nsb][rows][16]        d    fp16  [nsb][rows]
 //   F16/BF16 : [rows][cols] 16-bit
 // Other types (F32, Q8_1, Q2_K, Q3_K, Q5_K, Q8_K) keep the raw blocks as-is
-// ("raw" plane only) and are served by the dequantiser, not the GEMV.
+// ("raw": one plane, the GGUF payload unchanged); their GEMV decodes each
+// weight with the element dequantiser, and their prefill GEMM expands the
+// weight to fp16 in a scratch buffer first.
 struct Planes {
     int type = -1;
     uint32_t rows = 0, cols = 0;
@@ -97,13 +99,23 @@ struct Planes {
     bool raw = false;         // true: base holds the GGUF payload unchanged
 };
 
-inline bool gemv_supported(int t) {
+// Types with a field-regrouped planes layout and their own register decoders.
+inline bool planes_fast_type(int t) {
     switch (t) {
     case CUQ_Q8_0: case CUQ_Q4_0: case CUQ_Q4_1: case CUQ_Q5_0: case CUQ_Q5_1:
     case CUQ_Q4_K: case CUQ_Q6_K: case CUQ_F16: case CUQ_BF16: return true;
     default: return false;
     }
 }
+// Types kept as raw GGUF blocks (gguf.zig:842-949, 998-1034, 1061-1071, 751-761).
+inline bool planes_raw_type(int t) {
+    switch (t) {
+    case CUQ_F32: case CUQ_Q8_1: case CUQ_Q2_K: case CUQ_Q3_K: case CUQ_Q5_K: case CUQ_Q8_K: return true;
+    default: return false;
+    }
+}
+// Every type a projection may have: all 15 block types of gguf.zig:30-77.
+inline bool gemv_supported(int t) { return planes_fast_type(t) || planes_raw_type(t); }
 
 // Compute plane offsets for a type/shape; returns false for non-GEMV types.
 bool plan_planes(Planes &p);
@@ -138,6 +150,9 @@ int launch_to_xq(const float *x, uint32_t n, uint32_t n_vec, uint32_t x_stride, 
 // the fp32 result to h_out when non-null.
 int launch_rmsnorm_xq(const float *x, const float *w, uint32_t n, uint32_t n_rows, float eps, __half *xq,
                       float *h_out, cudaStream_t s);
+// One row, one CTA of 1024 threads, launched as a programmatic dependent of the
+// previous kernel (its own dependents may start as soon as it does).
+int launch_rmsnorm_xq_pdl(const float *x, const float *w, uint32_t n, float eps, __half *xq, cudaStream_t s);
 
 // Device-side decode-step state, read and advanced by the step's kernels.
 struct StepState {

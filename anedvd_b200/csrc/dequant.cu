@@ -37,7 +37,7 @@ __global__ void repack_kernel(PlanesView p, const uint8_t *__restrict__ raw, uin
 __global__ void dequant_planes_f16_kernel(PlanesView p, __half *__restrict__ out, int epb, int bpb) {
     uint32_t nb = p.cols / epb;
     size_t total = (size_t)p.rows * nb;
-    uint8_t blk[212];
+    uint8_t blk[296];  // the largest block (Q8_K, 292 bytes)
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < total; i += (size_t)gridDim.x * blockDim.x) {
         uint32_t r = (uint32_t)(i / nb), b = (uint32_t)(i % nb);
         block_move(p, blk, r, b, 1);
@@ -115,7 +115,11 @@ bool plan_planes(Planes &p) {
         p.nbytes = p.off_s2 + nb * rows * 2;
         break;
     case CUQ_F16: case CUQ_BF16: p.nbytes = rows * cols * 2; break;
-    default: return false;
+    default:
+        if (!planes_raw_type(p.type)) return false;
+        p.raw = true;  // the GGUF payload unchanged
+        p.nbytes = rows * nb * (size_t)block_bytes(p.type);
+        break;
     }
     return true;
 }
@@ -144,7 +148,7 @@ int launch_dequant_raw(int type, const uint8_t *raw, size_t raw_bytes, uint64_t 
 }
 
 int launch_repack(const uint8_t *raw, const Planes &p, cudaStream_t s) {
-    if (p.type == CUQ_F16 || p.type == CUQ_BF16) {
+    if (p.raw || p.type == CUQ_F16 || p.type == CUQ_BF16) {
         CUQ_CUDA_TRY(cudaMemcpyAsync(p.base, raw, p.nbytes, cudaMemcpyDeviceToDevice, s));
         return CUQ_OK;
     }
@@ -156,7 +160,7 @@ int launch_repack(const uint8_t *raw, const Planes &p, cudaStream_t s) {
 }
 
 int launch_unpack(const Planes &p, uint8_t *raw, cudaStream_t s) {
-    if (p.type == CUQ_F16 || p.type == CUQ_BF16) {
+    if (p.raw || p.type == CUQ_F16 || p.type == CUQ_BF16) {
         CUQ_CUDA_TRY(cudaMemcpyAsync(raw, p.base, p.nbytes, cudaMemcpyDeviceToDevice, s));
         return CUQ_OK;
     }

@@ -185,7 +185,11 @@ __device__ void block_move(const PlanesView &p, uint8_t *rawblk, uint32_t r, uin
         break;
     case CUQ_F16:
     case CUQ_BF16: mv(B + ((size_t)r * cols + b) * 2, rawblk, 2, dir); break;
-    default: break;
+    default: {  // raw blocks: the payload itself, row-major
+        const int bpb = block_bytes(p.type);
+        mv(B + ((size_t)r * (cols / block_elems(p.type)) + b) * bpb, rawblk, bpb, dir);
+        break;
+    }
     }
 }
 
@@ -197,7 +201,7 @@ __device__ __forceinline__ void embed_row_block(const PlanesView &p, uint32_t r,
     if (r >= p.rows) return;
     const int S = epb >= 256 ? 8 : 1;
     const uint32_t nb = p.cols / epb;
-    uint8_t blk[212];
+    uint8_t blk[296];  // the largest block (Q8_K, 292 bytes)
     for (uint32_t idx = threadIdx.x; idx < nb * S; idx += blockDim.x) {
         const uint32_t b = idx / S;
         const int part = idx % S, per = epb / S;

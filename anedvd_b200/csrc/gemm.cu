@@ -17,16 +17,18 @@ extern "C" int cuq_gemm(const cuq_weight *w, const float *x_dev, uint32_t n, flo
     unsigned int *ctr = nullptr;
     int ksplit = 1;
     const Planes *p = weight_planes(w, &ws, &ctr, &ksplit);
-    if (!p || p->raw) {
+    if (!p) {
         set_error("UnsupportedType: no GEMM for this weight");
         return CUQ_EUNSUPPORTED;
     }
     if (n == 0) return CUQ_OK;
     cudaStream_t s = (cudaStream_t)stream;
     size_t cnt = (size_t)n * p->cols;
+    const size_t scratch = qgemm_scratch_halves(*p, false);
     __half *xh = nullptr;
     int *err = nullptr;
-    CUQ_CUDA_TRY(cudaMallocAsync(&xh, sizeof(__half) * 2 * cnt + 16, s));
+    // x hi | x lo | (raw-block weights) the fp16 expansion
+    CUQ_CUDA_TRY(cudaMallocAsync(&xh, sizeof(__half) * (2 * cnt + scratch) + 16, s));
     CUQ_CUDA_TRY(cudaMallocAsync(&err, sizeof(int), s));
     CUQ_CUDA_TRY(cudaMemsetAsync(err, 0, sizeof(int), s));
     int rc = launch_split_hilo(x_dev, cnt, xh, xh + cnt, s);
@@ -38,6 +40,7 @@ extern "C" int cuq_gemm(const cuq_weight *w, const float *x_dev, uint32_t n, flo
         g.n = n;
         g.y = y_dev;
         g.err = err;
+        if (scratch) g.f16_scratch = xh + 2 * cnt;
         rc = launch_qgemm(g, EPI_STORE, s);
     }
     int herr = 0;

@@ -17,6 +17,8 @@
 //   * 4 warps per CTA split the CTA's K range; split-K across CTAs (ksplit)
 //     reduces deterministically through a workspace: the last CTA of a tile
 //     (atomic ticket) sums the partials in a fixed order and resets the ticket.
+#include <type_traits>
+
 #include "common.cuh"
 #include "gemv_impl.cuh"
 #include "tp.cuh"
@@ -67,6 +69,7 @@ cudaError_t launch_kw(const GemvArgs &a, const KArgs &k, cudaStream_t s) {
 template <class TT, int EPI>
 cudaError_t launch_epi(const GemvArgs &a, const KArgs &k, int kw, cudaStream_t s) {
     if (EPI == EPI_SILU_XQ) return launch_kw<TT, EPI, 2>(a, k, s);  // dual: 2 warps per matrix, one tile per CTA
+    if (std::is_same<TT, TRaw>::value) return launch_kw<TT, EPI, 4>(a, k, s);
     switch (kw) {
     case 1: return launch_kw<TT, EPI, 1>(a, k, s);
     case 2: return launch_kw<TT, EPI, 2>(a, k, s);
@@ -77,7 +80,8 @@ cudaError_t launch_epi(const GemvArgs &a, const KArgs &k, int kw, cudaStream_t s
 template <class TT>
 int launch_t(const GemvArgs &a, int epi, cudaStream_t s) {
     const KArgs k = make_kargs(a);
-    const int kw = gemv_pick_plan(*a.w, 0).kw;
+    // the raw-block decoder runs one shape of CTA (four warps per tile)
+    const int kw = std::is_same<TT, TRaw>::value ? 4 : gemv_pick_plan(*a.w, 0).kw;
     cudaError_t e;
     switch (epi) {
     case EPI_STORE: e = launch_epi<TT, EPI_STORE>(a, k, kw, s); break;
@@ -137,6 +141,16 @@ int launch_to_xq(const float *x, uint32_t n, uint32_t n_vec, uint32_t x_stride, 
     return CUQ_OK;
 }
 
+int launch_rmsnorm_xq_pdl(const float *x, const float *w, uint32_t n, float eps, __half *xq, cudaStream_t s) {
+    cudaError_t e = launch_maybe_pdl(rmsnorm_xq_kernel, dim3(1), dim3(1024), 0, s, true, x, w, n, eps, xq, xq_pad(n),
+                                     xq_halves(n), (float *)nullptr);
+    if (e != cudaSuccess) {
+        set_error("rmsnorm launch: %s", cudaGetErrorString(e));
+        return CUQ_ECUDA;
+    }
+    return CUQ_OK;
+}
+
 int launch_rmsnorm_xq(const float *x, const float *w, uint32_t n, uint32_t n_rows, float eps, __half *xq,
                       float *h_out, cudaStream_t s) {
     rmsnorm_xq_kernel<<<n_rows, 256, 0, s>>>(x, w, n, eps, xq, xq_pad(n), xq_halves(n), h_out);
@@ -153,7 +167,7 @@ GemvPlan gemv_pick_plan(const Planes &w, int sm_count) {
     switch (w.type) {
     case CUQ_Q8_0: case CUQ_F16: case CUQ_BF16: span = 64; break;
     case CUQ_Q4_K: case CUQ_Q6_K: span = 256; break;
-    default: span = 128; break;
+    default: span = planes_raw_type(w.type) ? 64 : 128; break;
     }
     const int ni = (int)((w.cols + span - 1) / span);
     const int tiles = (int)(w.rows / 16);
@@ -224,6 +238,7 @@ int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
     case CUQ_F16: return launch_t<T16<CUQ_F16>>(a, epi, s);
     case CUQ_BF16: return launch_t<T16<CUQ_BF16>>(a, epi, s);
     }
+    if (planes_raw_type(w.type)) return launch_t<TRaw>(a, epi, s);
     return CUQ_EUNSUPPORTED;
 }
 

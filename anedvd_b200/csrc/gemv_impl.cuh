@@ -4,6 +4,7 @@
 #pragma once
 
 #include "common.cuh"
+#include "dequant_impl.cuh"
 #include "tp.cuh"
 
 namespace cuq {
@@ -17,6 +18,7 @@ struct W {
     const uint8_t *q, *q2, *s, *s2;  // plane pointers (see common.cuh)
     uint32_t rows, cols;
     uint32_t qs, q2s;                // bytes per row of the row-major q plane and of Q6_K's qh plane
+    int type;                        // ggml type (the raw-block decoder reads it)
 };
 
 W wview(const Planes &p) {
@@ -33,6 +35,7 @@ W wview(const Planes &p) {
     default: w.qs = p.cols / 2; break;
     }
     w.q2s = p.type == CUQ_Q6_K ? p.cols / 4 : 0;
+    w.type = p.type;
     return w;
 }
 
@@ -424,6 +427,49 @@ struct T16 {
     __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 16 + s * 4; }
 };
 
+// Raw GGUF blocks of any other type (F32, Q8_1, Q2_K, Q3_K, Q5_K, Q8_K): each
+// weight is the element dequantiser's bit-exact fp32 value (dq_elem,
+// gguf.zig:751-1071) rounded to fp16 as readF16 does.  64 columns per
+// iteration; the lane's 32 weights (4 k-steps x rows r0, r0 + 8 x 4 columns)
+// are decoded by load(), so the prefetch ring carries finished fragments.
+// These types have no bandwidth target; this path is for correctness.
+struct TRaw {
+    static constexpr int SPAN = 64, KSTEPS = 4, DEPTH = 1;
+    static constexpr bool HAS_CORR = false;
+    template <class R_>
+    __device__ static void correct(const R_ &, const float *, int, int, float &, float &) {}
+    struct Raw { uint32_t f[4][4]; };
+    struct Prep {};
+    __device__ static void prep(const Raw &, int, Prep &) {}
+    template <class Src = SrcGlobal>
+    __device__ static void load(Raw &R, const W &w, uint32_t r0, int it, int tig) {
+        const int epb = block_elems(w.type), bpb = block_bytes(w.type);
+        const uint32_t nb = w.cols / (uint32_t)epb;
+#pragma unroll
+        for (int s = 0; s < 4; s++) {
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                const uint8_t *row = w.q + (size_t)(r0 + 8 * rr) * nb * bpb;
+                float v[4];
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const uint32_t c = (uint32_t)it * SPAN + tig * 16 + s * 4 + e;
+                    v[e] = c < w.cols ? __half2float(__float2half_rn(dq_elem(w.type, row + (size_t)(c / epb) * bpb,
+                                                                             (int)(c % epb))))
+                                      : 0.f;
+                }
+                R.f[s][rr] = h2u(__floats2half2_rn(v[0], v[2]));      // columns (0, 2) of the group
+                R.f[s][rr + 2] = h2u(__floats2half2_rn(v[1], v[3]));  // columns (1, 3)
+            }
+        }
+    }
+    __device__ static void frag(const Raw &R, const Prep &, int s, uint32_t (&a)[4]) {
+#pragma unroll
+        for (int i = 0; i < 4; i++) a[i] = R.f[s][i];
+    }
+    __device__ static uint32_t koff(int it, int tig, int s) { return it * SPAN + tig * 16 + s * 4; }
+};
+
 // ------------------------------------------------------------------ kernel -
 
 struct KArgs {
@@ -494,7 +540,7 @@ __device__ void finish_step(StepState *st, const uint32_t *forced, uint32_t *out
 // Shared memory of gemv_body, owned by the calling kernel so that the body's
 // instantiations share one copy.
 struct GemvShared {
-    float red[4][16];    // per-warp partial sums
+    float red[8][16];    // per-warp partial sums (up to 8 warps)
     float gu[4][32];     // EPI_SILU_XQ: gate and up values of a tile
     float act16[4][16];  // EPI_SILU_XQ: activations of a tile
     int is_last;
@@ -504,14 +550,27 @@ struct GemvShared {
 // the split-K reduction and the epilogue.  c / k0 / k1: this lane's MMA
 // accumulators and K-quant corrections.  Returns false for a CTA whose split-K
 // partial was not the tile's last.
-template <class TT, int EPI, int KW>
+// Barrier of the threads running a GEMV epilogue: the whole CTA (N = 0), or
+// its first N threads on named barrier 1 (a CTA whose other warps do
+// something else, e.g. a producer warp that streams the weights).
+template <int N>
+__device__ __forceinline__ void cta_sync() {
+    if constexpr (N == 0)
+        __syncthreads();
+    else
+        asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
+}
+
+template <class TT, int EPI, int KW, int NW = 4, int SYNC_N = 0>
 __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_t by, GemvShared &sh, float (&c)[4],
                                             float k0, float k1) {
+    // NW warps per CTA: TPC tiles of KW warps each, or (gate|up) one tile whose
+    // first NW/2 warps hold the gate rows and the others the up rows
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
-    constexpr int TPC = DUAL ? 1 : 4 / KW;
-    constexpr int KWE = DUAL ? 2 : KW;
+    constexpr int TPC = DUAL ? 1 : NW / KW;
+    constexpr int KWE = DUAL ? NW / 2 : KW;
     constexpr int NV = DUAL ? 32 : 16;
-    float(&red)[4][16] = sh.red;
+    float(&red)[8][16] = sh.red;
     int &is_last = sh.is_last;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, tig = lane & 3;
@@ -523,11 +582,12 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
             k1 += __shfl_xor_sync(0xffffffffu, k1, o);
         }
     }
+    if (SYNC_N) cta_sync<SYNC_N>();  // the previous unit's readers of `sh` are done
     if (tig == 0) {
         red[warp][g] = (c[0] + c[1]) - k0;
         red[warp][g + 8] = (c[2] + c[3]) - k1;
     }
-    __syncthreads();
+    cta_sync<SYNC_N>();
     // thread t < TPC * NV owns value vi of local tile tl (dual: vi < 16 gate, >= 16 up)
     const int t = threadIdx.x;
     const int tl = t / NV, vi = t % NV;
@@ -535,7 +595,7 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
     const uint32_t row = (bx * TPC + tl) * 16 + (vi & 15);
     float v = 0.f;
     if (own) {
-        const int w0 = DUAL ? 2 * (vi >> 4) : tl * KW;
+        const int w0 = DUAL ? KWE * (vi >> 4) : tl * KW;
 #pragma unroll
         for (int w = 0; w < KWE; w++) v += red[w0 + w][vi & 15];
     }
@@ -545,12 +605,12 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         // (atomic ticket per tile group) reduces them in a fixed order.
         if (own) p.ws[((size_t)by * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row] = v;
         __threadfence();
-        __syncthreads();
+        cta_sync<SYNC_N>();
         if (t == 0) {
             unsigned int prev = atomicAdd(&p.counters[bx], 1u);
             is_last = (prev == (unsigned)p.ksplit - 1u);
         }
-        __syncthreads();
+        cta_sync<SYNC_N>();
         if (!is_last) return false;
         __threadfence();
         if (own) {
@@ -565,7 +625,7 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         float(&gu)[4][32] = sh.gu;
         float(&act16)[4][16] = sh.act16;
         if (own) gu[tl][vi] = v;
-        __syncthreads();
+        cta_sync<SYNC_N>();
         if (own && vi < 16) {
             float gt = gu[tl][vi], ut = gu[tl][16 + vi];
             // cpu.siluMul (cpu.zig:65-70): g * (1 / (1 + exp(-g))) * u
@@ -579,7 +639,7 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
             p.xq_out[p.kpad_out + pos] = lo;
             act16[tl][vi] = act;
         }
-        __syncthreads();
+        cta_sync<SYNC_N>();
         if (t < TPC && bx * TPC + t < ntiles) {  // a tile's 16 rows are exactly one xq sum group
             float acc = 0.f;
             for (int j = 0; j < 16; j++) acc += act16[t][j];
@@ -590,7 +650,7 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         if (own)
             for (int q = 0; q < p.post.tp.size; q++) tp_slot(p.post.tp, q, p.post.tp_phase, p.post.tp.rank)[row] = v;
         __threadfence_system();
-        __syncthreads();
+        cta_sync<SYNC_N>();
         if (t == 0) tp_signal(p.post.tp, p.post.tp_phase);
     } else {
         if (own) {

@@ -9,7 +9,7 @@
 // launch, as TMA tensor copies into shared memory (up to ~48 KB per CTA, four
 // CTAs per SM), before it even waits for the activation, so the weights of a
 // whole matrix are requested within a few microseconds of the launch.  Each
-// stage of ST iterations lands on its own mbarrier; the four warps decode from
+// stage of ST iterations lands on its own mbarrier; the eight warps decode from
 // shared memory as the stages land, with the same register decoders and
 // tensor-core fragments as the other kernel (gemv_impl.cuh), and the same
 // epilogues, split-K reduction and post-ops.
@@ -96,7 +96,7 @@ __device__ __forceinline__ uint4 lds16(const uint8_t *p) { return *reinterpret_c
 template <class TT> struct TmaGeo;
 
 template <> struct TmaGeo<TQ4K> {
-    static constexpr int ST = 4, NPL = 2;
+    static constexpr int ST = 4;
     static constexpr uint32_t Q = 0, META = 8192, TX = 9216, SLICE = 9216;
     __device__ static void issue(uint32_t dst, const CUtensorMap *m, uint32_t tile, int it, uint64_t *bar) {
         tma_3d(dst + Q, &m[0], 0, (int)tile * 16, it, bar);
@@ -116,7 +116,7 @@ template <> struct TmaGeo<TQ4K> {
 };
 
 template <> struct TmaGeo<TQ6K> {
-    static constexpr int ST = 4, NPL = 4;
+    static constexpr int ST = 4;
     static constexpr uint32_t QL = 0, QH = 8192, SC = 12288, D = 13312, TX = 13440, SLICE = 14336;
     __device__ static void issue(uint32_t dst, const CUtensorMap *m, uint32_t tile, int it, uint64_t *bar) {
         tma_3d(dst + QL, &m[0], 0, (int)tile * 16, it, bar);
@@ -147,7 +147,7 @@ template <> struct TmaGeo<TQ6K> {
 };
 
 template <> struct TmaGeo<TQ8_0> {
-    static constexpr int ST = 8, NPL = 2;  // 8 iterations of 64 columns: 4 lines of 128
+    static constexpr int ST = 8;  // 8 iterations of 64 columns: 4 lines of 128
     static constexpr uint32_t Q = 0, DS = 8192, TX = 8704, SLICE = 9216;
     __device__ static void issue(uint32_t dst, const CUtensorMap *m, uint32_t tile, int it, uint64_t *bar) {
 #pragma unroll
@@ -175,14 +175,18 @@ struct __align__(64) TmaGemvArgs {
 
 // One CTA: 16-row tile blockIdx.x (of both matrices for gate|up), K part
 // blockIdx.y.  Thread 0 requests every stage of the part, then all threads wait
-// for the activation (programmatic dependent launch) and the four warps walk
-// the iterations (warp w takes iterations w, w + 4, ...; gate|up: warps 0-1 the
-// gate rows and 2-3 the up rows, two each).
+// for the activation (programmatic dependent launch) and the eight warps walk
+// the iterations (warp w takes iterations w, w + 8, ...; gate|up: warps 0-3 the
+// gate rows and 4-7 the up rows, four each).  Eight warps rather than four: the
+// decoders are issue-bound and shared memory limits the CTAs per SM; measured,
+// a persistent variant (a producer warp feeding a ring across tiles) was slower.
+constexpr int TMA_WARPS = 8;  // warps per CTA
+
 template <class TT, int EPI>
-__global__ void __launch_bounds__(128) gemv_tma_kernel(const __grid_constant__ TmaGemvArgs P) {
+__global__ void __launch_bounds__(32 * TMA_WARPS, 4) gemv_tma_kernel(const __grid_constant__ TmaGemvArgs P) {
     using G = TmaGeo<TT>;
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
-    constexpr int NMAT = DUAL ? 2 : 1, KWE = DUAL ? 2 : 4;
+    constexpr int NMAT = DUAL ? 2 : 1, KWE = DUAL ? TMA_WARPS / 2 : TMA_WARPS;
     extern __shared__ __align__(1024) uint8_t tma_dyn_raw[];
     // the 128-byte swizzle needs 1024-byte aligned boxes: align the base by hand
     // (the launch adds 1024 bytes of slack)
@@ -215,10 +219,11 @@ __global__ void __launch_bounds__(128) gemv_tma_kernel(const __grid_constant__ T
     griddep_wait();
     griddep_launch();
 
-    const int m = DUAL ? (warp >> 1) : 0, kw = DUAL ? (warp & 1) : warp;
+    const int m = DUAL ? warp / KWE : 0, kw = DUAL ? warp % KWE : warp;
     const __half *xb = p.xq + (g == 1 ? p.kpad : 0);
     const bool bl = g < 2;
-    float c[4] = {0.f, 0.f, 0.f, 0.f};
+    // two accumulators (even and odd k-steps) halve the MMA dependency chain
+    float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     for (int it = it0 + kw; it < it1; it += KWE) {
         const int j = it - it0, s = j / G::ST;
@@ -237,9 +242,14 @@ __global__ void __launch_bounds__(128) gemv_tma_kernel(const __grid_constant__ T
             if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, k));
             uint32_t a[4];
             TT::frag(R, Pp, k, a);
-            mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
+            if (k & 1)
+                mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
+            else
+                mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
         }
     }
+#pragma unroll
+    for (int i = 0; i < 4; i++) c[i] += c2[i];
     if (!ok && P.err) atomicExch(P.err, 1);
     __syncthreads();
     if (abort_flag && threadIdx.x == 0) {
@@ -251,7 +261,7 @@ __global__ void __launch_bounds__(128) gemv_tma_kernel(const __grid_constant__ T
             }
         }
     }
-    if (!gemv_finish<TT, EPI, 4>(p, tile, by, sh, c, 0.f, 0.f)) return;
+    if (!gemv_finish<TT, EPI, TMA_WARPS, TMA_WARPS>(p, tile, by, sh, c, 0.f, 0.f)) return;
     gemv_post_op(p, tma_dyn);
 }
 
@@ -350,7 +360,7 @@ cudaError_t launch_one(const TmaGemvArgs &args, dim3 grid, size_t smem, bool pdl
         cudaFuncSetAttribute(gemv_tma_kernel<TT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
         attr_set = true;
     }
-    return launch_maybe_pdl(gemv_tma_kernel<TT, EPI>, grid, dim3(128), smem, s, pdl, args);
+    return launch_maybe_pdl(gemv_tma_kernel<TT, EPI>, grid, dim3(32 * TMA_WARPS), smem, s, pdl, args);
 }
 
 template <class TT>

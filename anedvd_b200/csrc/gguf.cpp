@@ -13,6 +13,8 @@
 #include <string>
 #include <vector>
 
+#include <cstdint>
+
 #include "../../include/cuq.h"
 
 namespace cuq {
@@ -29,6 +31,7 @@ struct Value {
     std::string s;
     uint64_t arr_len = 0;
     uint32_t arr_type = 0;
+    std::vector<Value> arr;  // array elements
 };
 
 struct TensorInfo {
@@ -108,9 +111,11 @@ struct Gguf {
                 err = "TruncatedFile";
                 return false;
             }
+            v.arr.reserve((size_t)v.arr_len);
             for (uint64_t k = 0; k < v.arr_len; k++) {
                 Value e;
                 if (!value(v.arr_type, e)) return false;
+                v.arr.push_back(std::move(e));
             }
             return true;
         }
@@ -118,7 +123,7 @@ struct Gguf {
     }
     bool parse() {
         uint32_t magic;
-        if (!u32(magic)) return false;
+        if (!u32(magic)) return false;  // empty input: TruncatedFile
         if (magic != 0x46554747u) {
             err = "NotGgufFile";
             return false;
@@ -358,3 +363,234 @@ extern "C" cuq_model *cuq_model_load_gguf(const char *path, const cuq_options *o
     munmap(map, size);
     return m;
 }
+
+// ------------------------------------------------------- inspection API ---
+// The container as Gguf (gguf.zig:328-656) exposes it: header, metadata with
+// the reference's value conversions (gguf.zig:198-291), the tensor table and
+// each tensor's byte range (tensorBytes, gguf.zig:448-460).  Host only.
+
+struct cuq_gguf {
+    Gguf g;
+    std::vector<uint8_t> copy;  // cuq_gguf_open_bytes: the bytes parsed
+    void *map = nullptr;        // cuq_gguf_open: the mapping
+    size_t map_size = 0;
+};
+
+namespace {
+
+// Value as u64 / i64 / f64 / bool (asU64, asI64, asF32, asBool): false when the
+// type does not convert (strings, arrays, floats for the integer forms) or a
+// negative signed value is asked for as unsigned.
+bool value_u64(const Value &v, uint64_t &out) {
+    switch (v.type) {
+    case 0: case 2: case 4: case 10: case 7: out = v.u; return true;
+    case 1: case 3: case 5: case 11:
+        if (v.i < 0) return false;
+        out = (uint64_t)v.i;
+        return true;
+    default: return false;
+    }
+}
+bool value_i64(const Value &v, int64_t &out) {
+    switch (v.type) {
+    case 0: case 2: case 4: case 7: out = (int64_t)v.u; return true;
+    case 10:
+        if (v.u > (uint64_t)INT64_MAX) return false;
+        out = (int64_t)v.u;
+        return true;
+    case 1: case 3: case 5: case 11: out = v.i; return true;
+    default: return false;
+    }
+}
+bool value_f64(const Value &v, double &out) {
+    switch (v.type) {
+    case 6: case 12: out = v.f; return true;
+    case 0: case 2: case 4: case 10: case 7: out = (double)v.u; return true;
+    case 1: case 3: case 5: case 11: out = (double)v.i; return true;
+    default: return false;
+    }
+}
+
+const Value *find_kv(const cuq_gguf *h, const char *key) {
+    if (!h || !key) return nullptr;
+    return h->g.get(key);
+}
+
+cuq_gguf *finish_open(cuq_gguf *h) {
+    if (!h->g.parse()) {
+        cuq::set_error("%s", h->g.err.c_str());
+        cuq_gguf_close(h);
+        return nullptr;
+    }
+    return h;
+}
+
+}  // namespace
+
+extern "C" {
+
+cuq_gguf *cuq_gguf_open(const char *path) {
+    if (!path) {
+        cuq::set_error("cuq_gguf_open: null path");
+        return nullptr;
+    }
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) {
+        cuq::set_error("FileNotFound: %s", path);
+        return nullptr;
+    }
+    struct stat st;
+    if (fstat(fd, &st) != 0) {
+        close(fd);
+        cuq::set_error("cuq_gguf_open: cannot stat %s", path);
+        return nullptr;
+    }
+    cuq_gguf *h = new cuq_gguf();
+    if (st.st_size > 0) {
+        void *map = mmap(nullptr, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+        if (map == MAP_FAILED) {
+            close(fd);
+            delete h;
+            cuq::set_error("cuq_gguf_open: mmap failed");
+            return nullptr;
+        }
+        h->map = map;
+        h->map_size = (size_t)st.st_size;
+        h->g.data = (const uint8_t *)map;
+        h->g.size = (size_t)st.st_size;
+    }
+    close(fd);
+    return finish_open(h);
+}
+
+cuq_gguf *cuq_gguf_open_bytes(const void *data, size_t n) {
+    if (!data && n) {
+        cuq::set_error("cuq_gguf_open_bytes: null data");
+        return nullptr;
+    }
+    cuq_gguf *h = new cuq_gguf();
+    if (n) h->copy.assign((const uint8_t *)data, (const uint8_t *)data + n);
+    h->g.data = h->copy.data();
+    h->g.size = n;
+    return finish_open(h);
+}
+
+void cuq_gguf_close(cuq_gguf *h) {
+    if (!h) return;
+    if (h->map) munmap(h->map, h->map_size);
+    delete h;
+}
+
+uint32_t cuq_gguf_version(const cuq_gguf *h) { return h ? h->g.version : 0; }
+uint64_t cuq_gguf_tensor_count(const cuq_gguf *h) { return h ? (uint64_t)h->g.tensors.size() : 0; }
+
+int cuq_gguf_kv_type(const cuq_gguf *h, const char *key) {
+    const Value *v = find_kv(h, key);
+    return v ? (int)v->type : -1;
+}
+
+int cuq_gguf_get_u64(const cuq_gguf *h, const char *key, uint64_t *out) {
+    const Value *v = find_kv(h, key);
+    uint64_t x;
+    if (!v || !out || !value_u64(*v, x)) return CUQ_EINVAL;
+    *out = x;
+    return CUQ_OK;
+}
+
+int cuq_gguf_get_i64(const cuq_gguf *h, const char *key, int64_t *out) {
+    const Value *v = find_kv(h, key);
+    int64_t x;
+    if (!v || !out || !value_i64(*v, x)) return CUQ_EINVAL;
+    *out = x;
+    return CUQ_OK;
+}
+
+int cuq_gguf_get_f64(const cuq_gguf *h, const char *key, double *out) {
+    const Value *v = find_kv(h, key);
+    double x;
+    if (!v || !out || !value_f64(*v, x)) return CUQ_EINVAL;
+    *out = x;
+    return CUQ_OK;
+}
+
+const char *cuq_gguf_get_string(const cuq_gguf *h, const char *key) {
+    const Value *v = find_kv(h, key);
+    return v && v->type == 8 ? v->s.c_str() : nullptr;
+}
+
+int cuq_gguf_array_info(const cuq_gguf *h, const char *key, uint64_t *len, int *elem_type) {
+    const Value *v = find_kv(h, key);
+    if (!v || v->type != 9) return CUQ_EINVAL;
+    if (len) *len = v->arr_len;
+    if (elem_type) *elem_type = (int)v->arr_type;
+    return CUQ_OK;
+}
+
+int cuq_gguf_array_u64(const cuq_gguf *h, const char *key, uint64_t i, uint64_t *out) {
+    const Value *v = find_kv(h, key);
+    uint64_t x;
+    if (!v || v->type != 9 || i >= v->arr.size() || !out || !value_u64(v->arr[i], x)) return CUQ_EINVAL;
+    *out = x;
+    return CUQ_OK;
+}
+
+const char *cuq_gguf_array_string(const cuq_gguf *h, const char *key, uint64_t i) {
+    const Value *v = find_kv(h, key);
+    if (!v || v->type != 9 || i >= v->arr.size() || v->arr[i].type != 8) return nullptr;
+    return v->arr[i].s.c_str();
+}
+
+int cuq_gguf_tensor_info(const cuq_gguf *h, const char *name, int *ggml_type, uint32_t *n_dims, uint64_t *dims,
+                         uint64_t *offset) {
+    if (!h || !name) return CUQ_EINVAL;
+    auto it = h->g.tensors.find(name);
+    if (it == h->g.tensors.end()) {
+        cuq::set_error("TensorNotFound: %s", name);
+        return CUQ_EINVAL;
+    }
+    const TensorInfo &t = it->second;
+    if (ggml_type) *ggml_type = (int)t.type;
+    if (n_dims) *n_dims = (uint32_t)t.dims.size();
+    if (dims)
+        for (size_t k = 0; k < t.dims.size(); k++) dims[k] = t.dims[k];
+    if (offset) *offset = t.offset;
+    return CUQ_OK;
+}
+
+int cuq_gguf_tensor_bytes(const cuq_gguf *h, const char *name, const void **data, size_t *nbytes) {
+    if (!h || !name || !data || !nbytes) return CUQ_EINVAL;
+    auto it = h->g.tensors.find(name);
+    if (it == h->g.tensors.end()) {
+        cuq::set_error("TensorNotFound: %s", name);
+        return CUQ_EINVAL;
+    }
+    const TensorInfo &t = it->second;
+    const int epb = cuq_block_elems((int)t.type), bpb = cuq_block_bytes((int)t.type);
+    if (!epb || !bpb) {
+        cuq::set_error("UnsupportedType: %s has ggml type %u", name, t.type);
+        return CUQ_EUNSUPPORTED;
+    }
+    uint64_t n = 1;
+    for (auto d : t.dims) {
+        if (d && n > UINT64_MAX / d) {
+            cuq::set_error("TensorDataOutOfRange: %s", name);
+            return CUQ_EFORMAT;
+        }
+        n *= d;
+    }
+    if (n % (uint64_t)epb) {
+        cuq::set_error("InvalidTensorShape: %s (%llu elements, block of %d)", name, (unsigned long long)n, epb);
+        return CUQ_EINVAL;
+    }
+    const uint64_t nb = n / epb * bpb;
+    const uint64_t start = h->g.data_off + t.offset;
+    if (t.offset > UINT64_MAX - h->g.data_off || nb > UINT64_MAX - start || start + nb > h->g.size) {
+        cuq::set_error("TensorDataOutOfRange: %s", name);
+        return CUQ_EFORMAT;
+    }
+    *data = h->g.data + start;
+    *nbytes = (size_t)nb;
+    return CUQ_OK;
+}
+
+}  // extern "C"

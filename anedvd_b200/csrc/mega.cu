@@ -303,7 +303,7 @@ std::string mega_unsupported(const MegaStepSpec &sp) {
         if (p.embed && !p.norm_w) return "embedding phase without a norm";
         for (const MegaSegSpec &g : p.segs) {
             const Planes &w = *g.a.w;
-            if (!gemv_supported(w.type)) return "projection type without a GEMV";
+            if (!planes_fast_type(w.type)) return "projection type without a register decoder";
             if (w.rows == 0 || w.rows % 16) return "projection rows not a multiple of 16";
             if ((w.type == CUQ_F16 || w.type == CUQ_BF16) && w.cols % 16) return "16-bit projection cols";
             if (p.norm_w && w.cols != sp.hidden) return "normed projection input must be the residual";

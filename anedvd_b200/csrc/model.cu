@@ -14,6 +14,7 @@
 // activation (griddepcontrol.wait).  The step reads its token and position from
 // device memory and writes the next ones, so consecutive steps (a prompt fed
 // token by token, then greedy decoding) replay the graph with no host round-trip.
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -165,9 +166,12 @@ static int enqueue_step(cuq_model *m) {
     // CTA of the GEMV that reads it (pre-norm), after its first weight loads are
     // in flight, instead of by the last CTA of the GEMV that wrote the residual.
     // TMA-fed GEMVs request all their weights at launch, before the activation
-    // exists, so the norm stays the producer's post-op (computed once) and runs
-    // while the consumer's weights stream in.
+    // exists, so the norm is computed once instead ...
     const bool pre = m->opt.tp_size == 1 && c.hidden % 16 == 0 && c.hidden <= RN_MAX && !m->all_tma;
+    // ... and is launched as a one-CTA kernel of its own between the residual
+    // GEMV and its consumer: a programmatic dependent launch, so the consumer's
+    // CTAs start streaming their weights while the norm runs.
+    const bool sep_norm = m->opt.tp_size == 1 && m->all_tma;
     auto prenorm = [&](GemvArgs &a, const float *w) {
         if (!pre) return;
         a.pre_x = m->x;
@@ -201,8 +205,13 @@ static int enqueue_step(cuq_model *m) {
             GemvArgs a = gemv(L.o.p, m->xq_attn, nullptr, nullptr);
             int epi;
             residual_out(m, a, epi, L.o_bias, L.ffn_norm, 0);
-            if (pre) a.post.op = POST_NONE;
+            if (pre || sep_norm) a.post.op = POST_NONE;
             TRY(launch_gemv(a, epi, s));
+            // the ffn RMSNorm (main.zig:487) as a kernel of its own
+            if (sep_norm) {
+                m->prof_node = CUQ_NODE_NORM;
+                TRY(launch_rmsnorm_xq_pdl(m->x, L.ffn_norm, c.hidden, c.eps, m->xq_h, s));
+            }
         }
         // gate/up with the SiLU*mul epilogue (engine.zig:645-668 split path)
         m->prof_node = CUQ_NODE_GATE_UP;
@@ -229,9 +238,14 @@ static int enqueue_step(cuq_model *m) {
         {
             GemvArgs a = gemv(L.down.p, m->xq_act, nullptr, nullptr);
             int epi;
-            residual_out(m, a, epi, nullptr, l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm, 1);
-            if (pre) a.post.op = POST_NONE;
+            const float *next_norm = l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm;
+            residual_out(m, a, epi, nullptr, next_norm, 1);
+            if (pre || sep_norm) a.post.op = POST_NONE;
             TRY(launch_gemv(a, epi, s));
+            if (sep_norm) {
+                m->prof_node = CUQ_NODE_NORM;
+                TRY(launch_rmsnorm_xq_pdl(m->x, next_norm, c.hidden, c.eps, m->xq_h, s));
+            }
         }
     }
     // lm_head with the fused argmax (main.zig:534, cpu.zig:477-483); the last CTA
@@ -340,6 +354,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
         PTRY(launch_rmsnorm_hilo(m->pf_x, L.attn_norm, c.hidden, n, c.eps, m->pf_h, m->pf_l, s));
         for (auto &seg : L.qkv) {
             QgemmArgs g;
+            g.f16_scratch = m->pf_wscratch;
             g.w = &seg.p;
             g.xh = m->pf_h;
             g.xl = m->pf_l;
@@ -356,6 +371,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
                                       c.head_dim, m->pf_h, m->pf_l, s));
         {
             QgemmArgs g;
+            g.f16_scratch = m->pf_wscratch;
             g.w = &L.o.p;
             g.xh = m->pf_h;
             g.xl = m->pf_l;
@@ -373,6 +389,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
         PTRY(launch_rmsnorm_hilo(m->pf_x, L.ffn_norm, c.hidden, n, c.eps, m->pf_h, m->pf_l, s));
         if (L.gate_up_dual) {
             QgemmArgs g;
+            g.f16_scratch = m->pf_wscratch;
             g.w = &L.gate.p;
             g.w2 = &L.up.p;
             g.xh = m->pf_h;
@@ -384,6 +401,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
             PTRY(launch_qgemm(g, EPI_SILU_XQ, s));
         } else {
             QgemmArgs g;
+            g.f16_scratch = m->pf_wscratch;
             g.xh = m->pf_h;
             g.xl = m->pf_l;
             g.n = n;
@@ -398,6 +416,7 @@ static int prefill_chunk(cuq_model *m, const uint32_t *ids_dev, uint32_t n, uint
         }
         {
             QgemmArgs g;
+            g.f16_scratch = m->pf_wscratch;
             g.w = &L.down.p;
             g.xh = m->pf_ah;
             g.xl = m->pf_al;
@@ -936,6 +955,18 @@ int cuq_model_finalize(cuq_model *m) {
         }
         m->all_tma = all;
     }
+    {
+        // raw-block weights: fp16 expansion scratch of the largest prefill GEMM
+        size_t need = 0;
+        for (auto &L : m->layers) {
+            for (auto &sg : L.qkv) need = std::max(need, qgemm_scratch_halves(sg.p, false));
+            need = std::max(need, qgemm_scratch_halves(L.o.p, false));
+            need = std::max(need, qgemm_scratch_halves(L.gate.p, L.gate_up_dual));
+            need = std::max(need, qgemm_scratch_halves(L.up.p, false));
+            need = std::max(need, qgemm_scratch_halves(L.down.p, false));
+        }
+        if (need) CUQ_CUDA_TRY(cudaMalloc(&m->pf_wscratch, sizeof(__half) * need));
+    }
     m->ws_floats = ws_need;
     m->n_counters = ctr_need + 1;
     if (ws_need) CUQ_CUDA_TRY(cudaMalloc(&m->ws, sizeof(float) * ws_need));
@@ -1322,7 +1353,7 @@ void cuq_model_free(cuq_model *m) {
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
                     m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets,
                     m->pf_x,       m->pf_qkv, m->pf_q, m->pf_g, m->pf_u, m->pf_h, m->pf_l, m->pf_ah, m->pf_al,
-                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part};
+                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int r = 0; r < m->tpc.size && m->tp_connected; r++)

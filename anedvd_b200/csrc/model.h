@@ -67,6 +67,7 @@ struct cuq_model {
     float *pf_x = nullptr, *pf_qkv = nullptr, *pf_q = nullptr, *pf_g = nullptr, *pf_u = nullptr;
     __half *pf_h = nullptr, *pf_l = nullptr, *pf_ah = nullptr, *pf_al = nullptr;
     uint32_t *pf_ids = nullptr;
+    __half *pf_wscratch = nullptr;               // fp16 expansion of a raw-block weight (its prefill GEMM)
     int *gemm_err = nullptr;
 
     // tensor parallelism (opt.tp_size > 1)

@@ -756,9 +756,43 @@ WPlanes wplanes(const Planes &p) {
 
 }  // namespace
 
+size_t qgemm_scratch_halves(const Planes &w, bool dual) {
+    return w.raw ? (size_t)w.rows * w.cols * (dual ? 2 : 1) : 0;
+}
+
 int launch_qgemm(const QgemmArgs &g, int epi, cudaStream_t s) {
     const Planes &w = *g.w;
-    if (!gemv_supported(w.type)) {
+    if (w.raw) {
+        // expand to fp16 (the reference's own weight values) and run the fp16 GEMM
+        if (!g.f16_scratch) {
+            set_error("qgemm: ggml type %d needs an fp16 scratch buffer", w.type);
+            return CUQ_EINVAL;
+        }
+        const bool dual = epi == EPI_SILU_XQ;
+        const size_t n1 = (size_t)w.rows * w.cols;
+        Planes f[2];
+        for (int i = 0; i < (dual ? 2 : 1); i++) {
+            const Planes &src = i ? *g.w2 : w;
+            if (!src.raw || src.rows != w.rows || src.cols != w.cols) {
+                set_error("qgemm: gate/up must share type and shape");
+                return CUQ_EINVAL;
+            }
+            int rc = launch_dequant_planes_f16(src, g.f16_scratch + i * n1, s);
+            if (rc) return rc;
+            f[i].type = CUQ_F16;
+            f[i].rows = w.rows;
+            f[i].cols = w.cols;
+            f[i].base = reinterpret_cast<uint8_t *>(g.f16_scratch + i * n1);
+            f[i].nbytes = n1 * 2;
+            f[i].off_q = 0;
+        }
+        QgemmArgs g2 = g;
+        g2.w = &f[0];
+        g2.w2 = dual ? &f[1] : nullptr;
+        g2.f16_scratch = nullptr;
+        return launch_qgemm(g2, epi, s);
+    }
+    if (!planes_fast_type(w.type)) {
         set_error("UnsupportedType: no tensor-core GEMM for ggml type %d", w.type);
         return CUQ_EUNSUPPORTED;
     }

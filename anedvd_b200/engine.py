@@ -46,6 +46,20 @@ class Engine:
         return cls(h, cfg)
 
     @classmethod
+    def from_hf(cls, path, max_seq=2048, use_graphs=True, device=0, max_chunk=512, decode_kernel=rt.DECODE_AUTO):
+        """A HuggingFace model directory (config.json + safetensors), uploaded raw."""
+        L = rt.load()
+        rt.init(device)
+        opts = rt.CuqOptions(max_seq=max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs), tp_rank=0, tp_size=1,
+                             decode_kernel=decode_kernel, persistent_ctas=0)
+        h = L.cuq_model_load_hf(path.encode(), ctypes.byref(opts))
+        if not h:
+            raise rt.CuqError(rt.EFORMAT, rt.last_error())
+        cfg = rt.CuqConfig()
+        rt.check(L.cuq_model_get_config(h, ctypes.byref(cfg)))
+        return cls(h, cfg)
+
+    @classmethod
     def from_synth(cls, model, max_seq=None, use_graphs=True, device=0, max_chunk=512, tp_rank=0, tp_size=1,
                    exchange=None, decode_kernel=rt.DECODE_AUTO, persistent_ctas=0):
         """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads).

@@ -52,6 +52,31 @@ SIGNATURES = [
     ("cuq_model_finalize", I32, [P]),
     ("cuq_model_load_gguf", P, [ctypes.c_char_p, P]),
     ("cuq_model_get_config", I32, [P, P]),
+    ("cuq_gguf_open", P, [ctypes.c_char_p]),
+    ("cuq_gguf_open_bytes", P, [P, SZ]),
+    ("cuq_gguf_close", None, [P]),
+    ("cuq_gguf_version", U32, [P]),
+    ("cuq_gguf_tensor_count", U64, [P]),
+    ("cuq_gguf_kv_type", I32, [P, ctypes.c_char_p]),
+    ("cuq_gguf_get_u64", I32, [P, ctypes.c_char_p, ctypes.POINTER(U64)]),
+    ("cuq_gguf_get_i64", I32, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_int64)]),
+    ("cuq_gguf_get_f64", I32, [P, ctypes.c_char_p, ctypes.POINTER(ctypes.c_double)]),
+    ("cuq_gguf_get_string", ctypes.c_char_p, [P, ctypes.c_char_p]),
+    ("cuq_gguf_array_info", I32, [P, ctypes.c_char_p, ctypes.POINTER(U64), ctypes.POINTER(I32)]),
+    ("cuq_gguf_array_u64", I32, [P, ctypes.c_char_p, U64, ctypes.POINTER(U64)]),
+    ("cuq_gguf_array_string", ctypes.c_char_p, [P, ctypes.c_char_p, U64]),
+    ("cuq_gguf_tensor_info", I32, [P, ctypes.c_char_p, ctypes.POINTER(I32), ctypes.POINTER(U32),
+                                   ctypes.POINTER(U64), ctypes.POINTER(U64)]),
+    ("cuq_gguf_tensor_bytes", I32, [P, ctypes.c_char_p, ctypes.POINTER(P), ctypes.POINTER(SZ)]),
+    ("cuq_safetensors_open", P, [ctypes.c_char_p]),
+    ("cuq_safetensors_open_bytes", P, [P, SZ]),
+    ("cuq_safetensors_close", None, [P]),
+    ("cuq_safetensors_count", U64, [P]),
+    ("cuq_safetensors_name", ctypes.c_char_p, [P, U64]),
+    ("cuq_safetensors_tensor", I32, [P, ctypes.c_char_p, ctypes.c_char_p, ctypes.POINTER(U32),
+                                     ctypes.POINTER(U64), ctypes.POINTER(P), ctypes.POINTER(SZ)]),
+    ("cuq_hf_read_config", I32, [ctypes.c_char_p, P]),
+    ("cuq_model_load_hf", P, [ctypes.c_char_p, P]),
     ("cuq_tp_comm_handle", I32, [P, P]),
     ("cuq_tp_connect", I32, [P, P]),
     ("cuq_shard_rows", I32, [I32, U32, U32, U32, U32, P, P]),
@@ -92,7 +117,7 @@ class CuqStats(ctypes.Structure):
                 ("kernel_launches", U64), ("persistent_ctas", U64)]
 
 
-NODE_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "lm_head"]
+NODE_NAMES = ["embed", "qkv", "attention", "o", "gate_up", "down", "lm_head", "norm"]
 
 
 class CuqNodeTime(ctypes.Structure):
@@ -136,3 +161,122 @@ def check(rc):
 
 def init(device=0):
     return check(load().cuq_init(device))
+
+
+class GgufFile:
+    """The library's GGUF parser (cuq_gguf_*), as gguf.zig's Gguf: metadata
+    getters with the reference's conversions, the tensor table and raw bytes.
+    Host only; raises CuqError with the parser's error name."""
+
+    def __init__(self, path=None, data=None):
+        L = load()
+        if data is not None:
+            self._buf = ctypes.create_string_buffer(bytes(data), len(data))
+            self._h = L.cuq_gguf_open_bytes(self._buf, len(data))
+        else:
+            self._h = L.cuq_gguf_open(path.encode())
+        if not self._h:
+            raise CuqError(EFORMAT, last_error())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load().cuq_gguf_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    @property
+    def version(self):
+        return load().cuq_gguf_version(self._h)
+
+    @property
+    def tensor_count(self):
+        return load().cuq_gguf_tensor_count(self._h)
+
+    def kv_type(self, key):
+        return load().cuq_gguf_kv_type(self._h, key.encode())
+
+    def _get(self, fn, ctype, key):
+        v = ctype()
+        return v.value if fn(self._h, key.encode(), ctypes.byref(v)) == OK else None
+
+    def u64(self, key):
+        return self._get(load().cuq_gguf_get_u64, U64, key)
+
+    def i64(self, key):
+        return self._get(load().cuq_gguf_get_i64, ctypes.c_int64, key)
+
+    def f64(self, key):
+        return self._get(load().cuq_gguf_get_f64, ctypes.c_double, key)
+
+    def string(self, key):
+        s = load().cuq_gguf_get_string(self._h, key.encode())
+        return None if s is None else s.decode()
+
+    def array(self, key):
+        L = load()
+        n, et = U64(), I32()
+        if L.cuq_gguf_array_info(self._h, key.encode(), ctypes.byref(n), ctypes.byref(et)) != OK:
+            return None
+        out = []
+        for i in range(n.value):
+            if et.value == 8:
+                out.append(L.cuq_gguf_array_string(self._h, key.encode(), i).decode())
+            else:
+                v = U64()
+                check(L.cuq_gguf_array_u64(self._h, key.encode(), i, ctypes.byref(v)))
+                out.append(v.value)
+        return out
+
+    def tensor_info(self, name):
+        t, nd, dims, off = I32(), U32(), (U64 * 8)(), U64()
+        check(load().cuq_gguf_tensor_info(self._h, name.encode(), ctypes.byref(t), ctypes.byref(nd), dims,
+                                          ctypes.byref(off)))
+        return t.value, list(dims[:nd.value]), off.value
+
+    def tensor_bytes(self, name):
+        p, n = P(), SZ()
+        check(load().cuq_gguf_tensor_bytes(self._h, name.encode(), ctypes.byref(p), ctypes.byref(n)))
+        return ctypes.string_at(p, n.value)
+
+
+class SafetensorsFile:
+    """The library's safetensors reader (cuq_safetensors_*), host only."""
+
+    def __init__(self, path=None, data=None):
+        L = load()
+        if data is not None:
+            self._buf = ctypes.create_string_buffer(bytes(data), len(data))
+            self._h = L.cuq_safetensors_open_bytes(self._buf, len(data))
+        else:
+            self._h = L.cuq_safetensors_open(path.encode())
+        if not self._h:
+            raise CuqError(EFORMAT, last_error())
+
+    def close(self):
+        if getattr(self, "_h", None):
+            load().cuq_safetensors_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        self.close()
+
+    def names(self):
+        L = load()
+        return [L.cuq_safetensors_name(self._h, i).decode() for i in range(L.cuq_safetensors_count(self._h))]
+
+    def tensor(self, name):
+        """(dtype, shape, bytes)"""
+        dt = ctypes.create_string_buffer(8)
+        rank, shape, p, n = U32(), (U64 * 8)(), P(), SZ()
+        check(load().cuq_safetensors_tensor(self._h, name.encode(), dt, ctypes.byref(rank), shape, ctypes.byref(p),
+                                            ctypes.byref(n)))
+        return dt.value.decode(), list(shape[:rank.value]), ctypes.string_at(p, n.value)
+
+
+def hf_config(path):
+    """config.json of a HuggingFace model directory as a CuqConfig (cuq_hf_read_config)."""
+    c = CuqConfig()
+    check(load().cuq_hf_read_config(path.encode(), ctypes.byref(c)))
+    return c

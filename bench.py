@@ -313,10 +313,11 @@ def gemv_roofline(ttype, raw, rows, cols, stream_ptr, pk, label, reps=64):
 
 
 # the kernel behind each node of the per-op decode step
-NODE_KERNEL = {"embed": "embed_row_kernel", "qkv": "gemv_kernel, RMSNorm per CTA + q||k||v",
-               "attention": "attn_step_kernel", "o": "gemv_kernel + residual",
-               "gate_up": "dual gemv_kernel, RMSNorm per CTA + gate|up + SiLU*mul",
-               "down": "gemv_kernel + residual", "lm_head": "gemv_kernel + argmax"}
+NODE_KERNEL = {"embed": "embed_norm_kernel", "qkv": "gemv_tma_kernel, q||k||v (+ v when its type differs)",
+               "attention": "attn_step_kernel", "o": "gemv_tma_kernel + residual",
+               "gate_up": "gemv_tma_kernel, gate|up + SiLU*mul",
+               "down": "gemv_tma_kernel + residual", "lm_head": "gemv_tma_kernel + argmax",
+               "norm": "rmsnorm_xq_kernel"}
 
 
 def run_ours(args, world, rank, local):

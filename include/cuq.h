@@ -247,6 +247,64 @@ int cuq_model_finalize(cuq_model *m);
  * cuq_model_finalize. */
 cuq_model *cuq_model_load_gguf(const char *path, const cuq_options *opts);
 
+/* ----------------------------------------------------- GGUF container --- */
+/* The file format the loader reads, as gguf.zig's Gguf exposes it (host only,
+ * no GPU needed).  Open errors (cuq_last_error): NotGgufFile,
+ * UnsupportedVersion, TruncatedFile, TooManyTensors, TooManyMetadataEntries,
+ * InvalidMetadata, InvalidTensorShape (gguf.zig:589-656). */
+typedef struct cuq_gguf cuq_gguf;
+cuq_gguf *cuq_gguf_open(const char *path);                  /* Gguf.load: maps the file */
+cuq_gguf *cuq_gguf_open_bytes(const void *data, size_t n);  /* Gguf.fromBytes: parses a copy */
+void cuq_gguf_close(cuq_gguf *g);
+uint32_t cuq_gguf_version(const cuq_gguf *g);
+uint64_t cuq_gguf_tensor_count(const cuq_gguf *g);
+/* Metadata (gguf.zig:198-291): the value type id of `key` (0-12) or -1 when
+ * absent; integer, float and bool values converted as the reference's
+ * asU64 / asI64 / asF32 do (CUQ_EINVAL when absent or not convertible). */
+int cuq_gguf_kv_type(const cuq_gguf *g, const char *key);
+int cuq_gguf_get_u64(const cuq_gguf *g, const char *key, uint64_t *out);
+int cuq_gguf_get_i64(const cuq_gguf *g, const char *key, int64_t *out);
+int cuq_gguf_get_f64(const cuq_gguf *g, const char *key, double *out);
+const char *cuq_gguf_get_string(const cuq_gguf *g, const char *key);  /* NULL unless a string */
+int cuq_gguf_array_info(const cuq_gguf *g, const char *key, uint64_t *len, int *elem_type);
+int cuq_gguf_array_u64(const cuq_gguf *g, const char *key, uint64_t i, uint64_t *out);
+const char *cuq_gguf_array_string(const cuq_gguf *g, const char *key, uint64_t i);
+/* Tensor table: type, dims in ggml order (dims[0] = row length; up to 8) and
+ * offset inside the data section; CUQ_EINVAL (TensorNotFound) when absent. */
+int cuq_gguf_tensor_info(const cuq_gguf *g, const char *name, int *ggml_type, uint32_t *n_dims, uint64_t *dims,
+                         uint64_t *offset);
+/* Gguf.tensorBytes (gguf.zig:448-460): the tensor's payload inside the file
+ * (valid until cuq_gguf_close).  CUQ_EUNSUPPORTED (UnsupportedType),
+ * CUQ_EINVAL (InvalidTensorShape, TensorNotFound), CUQ_EFORMAT
+ * (TensorDataOutOfRange). */
+int cuq_gguf_tensor_bytes(const cuq_gguf *g, const char *name, const void **data, size_t *nbytes);
+
+/* ------------------------------------------- HuggingFace directories --- */
+/* safetensors files (safetensors.zig): open errors HeaderTooSmall,
+ * InvalidHeaderLength, InvalidHeader, InvalidTensorEntry, UnsupportedDtype,
+ * DataSizeMismatch (safetensors.zig:104-121).  Host only. */
+typedef struct cuq_safetensors cuq_safetensors;
+cuq_safetensors *cuq_safetensors_open(const char *path);
+cuq_safetensors *cuq_safetensors_open_bytes(const void *data, size_t n);
+void cuq_safetensors_close(cuq_safetensors *s);
+uint64_t cuq_safetensors_count(const cuq_safetensors *s);                /* tensors, __metadata__ excluded */
+const char *cuq_safetensors_name(const cuq_safetensors *s, uint64_t i);   /* in header order */
+/* dtype_out: 8 bytes ("F16", "BF16", ...), shape: up to 8 dims; data valid until close. */
+int cuq_safetensors_tensor(const cuq_safetensors *s, const char *name, char *dtype_out, uint32_t *rank,
+                           uint64_t *shape, const void **data, size_t *nbytes);
+/* config.json of a model directory (hf.zig Config -> load_hf.zig toModelConfig):
+ * hidden_size, num_hidden_layers, num_attention_heads, num_key_value_heads,
+ * head_dim, intermediate_size, vocab_size, rms_norm_eps, rope_theta,
+ * tie_word_embeddings; rope_adjacent is 0 (HF's half-split RoPE).  Host only. */
+int cuq_hf_read_config(const char *dir, cuq_config *out);
+/* load_hf.zig (loadRuntime / loadLayer / loadHead, load_hf.zig:143-230): a
+ * model directory (config.json + model*.safetensors shards, or the files of
+ * model.safetensors.index.json) uploaded raw: F16 / BF16 / F32 weights as on
+ * disk, norms and biases as f32; the head is tied when lm_head.weight is
+ * absent.  Returns a finalized model, except with opts->tp_size > 1 (as
+ * cuq_model_load_gguf). */
+cuq_model *cuq_model_load_hf(const char *dir, const cuq_options *opts);
+
 /* Tensor parallelism (Megatron split of BASELINE config 5; the reference engine
  * is single-device, so these have no counterpart there).  One process per GPU,
  * each creating its model with the same config and tp_size and its own tp_rank,
@@ -320,7 +378,8 @@ int cuq_model_stats(const cuq_model *m, cuq_stats *out);
 #define CUQ_NODE_GATE_UP 4  /* gate|up projections + SiLU*mul (+ RMSNorm) */
 #define CUQ_NODE_DOWN 5     /* down projection + residual */
 #define CUQ_NODE_HEAD 6     /* final RMSNorm + lm_head + argmax */
-#define CUQ_NODES 7
+#define CUQ_NODE_NORM 7     /* RMSNorms launched as kernels of their own */
+#define CUQ_NODES 8
 typedef struct {
     uint64_t launches;  /* kernel launches of this node over the steps */
     double ms;          /* summed launch times */

@@ -53,8 +53,42 @@ def test_dequant_range_offsets_and_errors():
 
 
 def _weights(ttype, rows, cols, seed):
+    if ttype in RAW_TYPES and ttype != 0:
+        return golden_blocks(ttype, rows * cols, seed)
     w = synth.seeded_normal("test/%d/%d/%d/%d" % (ttype, rows, cols, seed), rows * cols)
     return quant.quantize(ttype, w).tobytes()
+
+
+# types kept as raw GGUF blocks on the device (no quantiser here: their test
+# tensors are drawn from the reference-pinned golden blocks)
+RAW_TYPES = [0, 9, 10, 11, 13, 15]
+
+
+# the block's scale fields (byte offset, fp16 or fp32) and the power of two
+# that brings the golden blocks' weights (std 11-550) to a model's scale (~0.02)
+SCALE_FIELDS = {9: ([(0, 2)], 12), 10: ([(80, 2), (82, 2)], 9), 11: ([(108, 2)], 11),
+                13: ([(0, 2), (2, 2)], 14), 15: ([(0, 4)], 11)}
+
+
+def golden_blocks(ttype, n, seed, model_scale=False):
+    """A payload of n weights whose blocks are drawn (seeded) from the 64 golden
+    blocks of the type -- valid blocks the reference's own vectors pin.  With
+    model_scale the blocks' d (and dmin) are divided by a power of two so the
+    weights have a transformer's magnitude (the golden blocks exercise extreme
+    scales, which would overflow a model's fp16 activations)."""
+    be, bb = orc.block_elems(ttype), orc.block_bytes(ttype)
+    blocks = np.frombuffer(open(os.path.join(GOLD, "dequant_wide", TYPES[ttype] + ".bin"), "rb").read(),
+                           dtype=np.uint8).reshape(-1, bb)
+    idx = np.random.default_rng(seed).integers(0, blocks.shape[0], size=n // be)
+    out = blocks[idx].copy()
+    if model_scale and ttype in SCALE_FIELDS:
+        fields, shift = SCALE_FIELDS[ttype]
+        f = np.float32(2.0 ** -shift)
+        for off, size in fields:
+            dt = np.float16 if size == 2 else np.float32
+            v = (out[:, off:off + size].copy().view(dt).astype(np.float32) * f).astype(dt)
+            out[:, off:off + size] = v.view(np.uint8).reshape(-1, size)
+    return out.tobytes()
 
 
 @pytest.mark.parametrize("ttype", GEMV_TYPES)
@@ -112,12 +146,38 @@ def test_gemm_matches_gemv():
         assert rel_err(Y[i], _ref_gemv(12, raw, rows, cols, X[i])) < KERNEL_TOL
 
 
-def test_gemv_rejects_unsupported_types():
-    raw = open(os.path.join(GOLD, "dequant_wide", "q2_k.bin"), "rb").read()
-    W = Weight(10, raw, 16, 256 * 4)
-    x = dev(np.zeros(1024, np.float32))
-    y = empty(16)
-    assert lib().cuq_gemv(W.h, ptr(x), ptr(y), None) == rt.EUNSUPPORTED
+def test_weight_rejects_unknown_types():
+    raw = np.zeros(16 * 34, np.uint8)
+    L = lib()
+    for t in (4, 5, 16, 31):  # ids gguf.zig:30-46 does not define
+        assert not L.cuq_weight_create(t, raw.ctypes.data_as(ctypes.c_void_p), raw.size, 16, 32)
+
+
+@pytest.mark.parametrize("ttype", RAW_TYPES)
+@pytest.mark.parametrize("shape", [(16, 256), (48, 1024), (256, 4096)])
+def test_gemv_raw_block_types(ttype, shape):
+    """The remaining block types (Q8_1, Q2_K, Q3_K, Q5_K, Q8_K, F32;
+    gguf.zig:842-949, 998-1034, 1061-1071, 751-761) through the GEMV: every
+    weight is the reference's readF16 value."""
+    rows, cols = shape
+    raw = _weights(ttype, rows, cols, 7)
+    x = synth.seeded_normal("test/x/raw/%d" % cols, cols, std=1.0)
+    W = Weight(ttype, raw, rows, cols)
+    assert W.export_raw().tobytes() == raw
+    assert np.array_equal(W.dequant_f16(), orc.read_f16(ttype, raw, rows * cols).reshape(rows, cols))
+    assert rel_err(W.gemv(x), _ref_gemv(ttype, raw, rows, cols, x)) < KERNEL_TOL
+
+
+@pytest.mark.parametrize("ttype", RAW_TYPES)
+def test_gemm_raw_block_types(ttype):
+    """Their prefill GEMM: the weight expanded to fp16 (readF16 values) in a
+    scratch buffer, then the tcgen05 fp16 GEMM."""
+    rows, cols, n = 128, 1024, 37
+    raw = _weights(ttype, rows, cols, 8)
+    X = np.stack([synth.seeded_normal("test/X/raw/%d" % i, cols, std=1.0) for i in range(n)])
+    Y = Weight(ttype, raw, rows, cols).gemm(X)
+    for i in (0, 17, n - 1):
+        assert rel_err(Y[i], _ref_gemv(ttype, raw, rows, cols, X[i])) < KERNEL_TOL
 
 
 def test_rmsnorm():

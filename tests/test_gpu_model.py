@@ -5,6 +5,8 @@ Bars: logits within 2e-3 relative error
 (rel = max|a-b| / max|b|, main.zig:1920-1930); greedy tokens identical wherever
 the oracle's top-2 margin exceeds that tolerance.
 """
+import zlib
+
 import numpy as np
 import pytest
 
@@ -227,6 +229,7 @@ def test_profile_decode_table():
     c = m.cfg
     assert tab["qkv"][0] >= n * c.layers and tab["attention"][0] == n * c.layers
     assert tab["o"][0] == n * c.layers and tab["down"][0] == n * c.layers and tab["lm_head"][0] == n
+    assert tab["norm"][0] in (0, 2 * n * c.layers)  # the two norms of a layer, when they run on their own
     assert all(v[1] > 0 for k, v in tab.items() if v[0])
     kvd = c.kv_heads * c.head_dim
     want_kv = sum(2 * 2 * kvd * c.layers * (len(ids) + i + 1) for i in range(n))
@@ -264,3 +267,40 @@ def test_session_reuses_the_kv_prefix_of_a_growing_transcript():
     assert list(t3) == list(E.Session(fresh, 96).generate(p2[:10], 4))
     eng.close()
     fresh.close()
+
+
+def test_model_with_raw_block_types_matches_reference():
+    """A Llama-shaped model whose projections use the block types kept raw on
+    the device (Q5_K, Q3_K, Q2_K, Q8_K, Q8_1): decode GEMVs through the element
+    dequantiser, prefill GEMMs through the fp16 expansion, against refForward."""
+    from .test_gpu_kernels import golden_blocks
+    m = synth.model("llama3-8b", layers=2, vocab=1024, hidden=512, heads=4, kv_heads=2, inter=1024)
+    mix = {"q": 13, "k": 11, "v": 10, "o": 15, "gate": 9, "up": 9, "down": 13}
+    for t in m.tensors():
+        if t.role in mix:
+            t.ggml_type = mix[t.role]
+            t.data = golden_blocks(t.ggml_type, t.rows * t.cols, zlib.crc32(t.name.encode()) % 1000, model_scale=True)
+    e = _compare(m, n_prompt=9, n_decode=5)
+    assert e < LOGIT_TOL, e
+
+
+@pytest.mark.parametrize("linear_type", [1, 30], ids=["f16", "bf16"])
+def test_hf_directory_matches_reference(linear_type, tmp_path):
+    """load_hf.zig's path (config.json + sharded safetensors + index) uploaded raw:
+    F16 / BF16 weights as on disk, rounded by the kernels as readF16 does,
+    against refForward on the same weights."""
+    from .hf_util import to_hf_types, write_hf_dir
+    m = to_hf_types(synth.model("qwen2.5-0.5b", layers=2, vocab=1024), linear_type)
+    path = write_hf_dir(m, str(tmp_path / "hf"), shards=3)
+    ref = orc.Model(m.cfg, threads=8, max_seq=32)
+    ref.load(m)
+    eng = E.Engine.from_hf(path, max_seq=32)
+    assert eng.cfg.rope_adjacent == 0 and eng.cfg.tie_embeddings == 1
+    ids = _prompt(m.cfg, 7)
+    for p, t in enumerate(ids):
+        want = ref.forward(int(t), p)
+    got, _ = eng.prefill(ids)
+    assert rel_err(got, want) < LOGIT_TOL
+    got, _ = eng.forward(3, len(ids))
+    assert rel_err(got, ref.forward(3, len(ids))) < LOGIT_TOL
+    eng.close()
