@@ -15,6 +15,7 @@
 // device memory and writes the next ones, so consecutive steps (a prompt fed
 // token by token, then greedy decoding) replay the graph with no host round-trip.
 #include <algorithm>
+#include <cstddef>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -289,6 +290,58 @@ static int run_steps(cuq_model *m, uint32_t n) {
         } else {
             int rc = enqueue_step(m);
             if (rc) return rc;
+        }
+    }
+    return CUQ_OK;
+}
+
+// A draw right after the step's lm_head: replaces the step's greedy token
+// (out_tokens[step], the next token) with one sampled from the logits with the
+// call's parameters, LCG state and window, all read from device memory.
+static int enqueue_sample(cuq_model *m) {
+    SampleArgs a;
+    a.logits = m->logits;
+    a.vocab = m->lc.vocab;
+    a.prm = &m->smp->prm;
+    a.rng = &m->smp->rng;
+    a.st = m->state;
+    a.out_tokens = m->out_tokens;
+    a.ring = &m->smp->ring;
+    a.ring_ids = m->smp->ids;
+    return launch_sample(a, true, m->stream);
+}
+
+// n sampled decode steps: the decode step and its draw, replayed as one CUDA
+// graph (captured at the first sampled call) when the model uses graphs.
+static int run_steps_sampled(cuq_model *m, uint32_t n) {
+    if (n == 0) return CUQ_OK;
+    if (m->opt.use_graphs && !m->graph_exec_smp) {
+        CUQ_CUDA_TRY(cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal));
+        int rc = enqueue_step(m);
+        if (rc == CUQ_OK) rc = enqueue_sample(m);
+        cudaGraph_t g = nullptr;
+        cudaError_t e = cudaStreamEndCapture(m->stream, &g);
+        if (rc != CUQ_OK) {
+            if (g) cudaGraphDestroy(g);
+            return rc;
+        }
+        if (e != cudaSuccess) {
+            set_error("graph capture: %s", cudaGetErrorString(e));
+            return CUQ_ECUDA;
+        }
+        m->graph_smp = g;
+        CUQ_CUDA_TRY(cudaGraphInstantiate(&m->graph_exec_smp, g, 0));
+    }
+    for (uint32_t i = 0; i < n; i++) {
+        if (m->graph_exec_smp) {
+            CUQ_CUDA_TRY(cudaGraphLaunch(m->graph_exec_smp, m->stream));
+            m->stats.graph_replays++;
+            m->stats.kernel_launches += m->stats.kernels_per_step + 1;
+        } else {
+            int rc = enqueue_step(m);
+            if (rc == CUQ_OK) rc = enqueue_sample(m);
+            if (rc) return rc;
+            m->stats.kernel_launches += 1;
         }
     }
     return CUQ_OK;
@@ -611,6 +664,8 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
             t.err = m->tp_err;
             t.peer[t.rank] = m->tp_buf;
         }
+        if (cudaMalloc(&m->smp, sizeof(SampleState)) != cudaSuccess) break;
+        if (cudaMallocHost(&m->smp_host, sizeof(SampleState)) != cudaSuccess) break;
         if (cudaEventCreate(&m->ev0) != cudaSuccess || cudaEventCreate(&m->ev1) != cudaSuccess) break;
         ok = true;
     } while (0);
@@ -1181,6 +1236,75 @@ int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t 
     return check_gemm_err(m);
 }
 
+int cuq_generate_sampled(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_cached, uint32_t n_decode,
+                         const cuq_sampler_params *params, uint32_t seed, uint32_t penalty_window,
+                         uint32_t *out_tokens) {
+    CUQ_CHECK_ARG(m && ids && n_prompt > 0 && n_cached < n_prompt && params && (out_tokens || n_decode == 0),
+                  "cuq_generate_sampled: bad argument");
+    CUQ_CHECK_ARG(penalty_window <= CUQ_SAMPLE_MAX_WINDOW, "cuq_generate_sampled: penalty window %u exceeds %u",
+                  penalty_window, (unsigned)CUQ_SAMPLE_MAX_WINDOW);
+    if (!m->finalized) {
+        set_error("cuq_generate_sampled: model not finalized");
+        return CUQ_ENOTREADY;
+    }
+    const cuq_sampler_params &P = *params;
+    const bool pen = !(P.repetition_penalty == 1.0f && P.presence_penalty == 0.0f && P.frequency_penalty == 0.0f);
+    const bool draw = P.temperature > 0.0f || pen;  // otherwise the step's own argmax is the reference's choice
+    if (draw && m->opt.tp_size > 1) {
+        set_error("cuq_generate_sampled: sampling under tensor parallelism is not supported (greedy only)");
+        return CUQ_EUNSUPPORTED;
+    }
+    if (draw && m->lc.vocab > CUQ_SAMPLE_MAX_VOCAB) {
+        set_error("cuq_generate_sampled: vocab %u exceeds %u", m->lc.vocab, (unsigned)CUQ_SAMPLE_MAX_VOCAB);
+        return CUQ_EINVAL;
+    }
+    const uint32_t n_new = n_prompt - n_cached;
+    if (n_decode == 0) return cuq_prefill(m, ids + n_cached, n_new, n_cached, nullptr, nullptr);
+    if (n_prompt + n_decode - 1 > m->opt.max_seq) {
+        set_error("ContextOverflow: %u prompt + %u decode > max_seq %u", n_prompt, n_decode, m->opt.max_seq);
+        return CUQ_ECONTEXT;
+    }
+    int rc;
+    for (uint32_t i = n_cached; i < n_prompt; i++)
+        if ((rc = check_token(m, ids[i]))) return rc;
+    if (draw) {
+        // parameters, the LCG seed (generate.zig:169) and the window: the last
+        // `penalty_window` prompt ids (generate.zig:205-211)
+        SampleState &h = *m->smp_host;
+        h.prm = P;
+        h.rng = seed;
+        const uint32_t nw = n_prompt < penalty_window ? n_prompt : penalty_window;
+        memcpy(h.ids, ids + (n_prompt - nw), sizeof(uint32_t) * nw);
+        h.ring.len = nw;
+        h.ring.head = 0;
+        h.ring.cap = penalty_window;
+        CUQ_CUDA_TRY(cudaMemcpyAsync(m->smp, m->smp_host, offsetof(SampleState, ids) + sizeof(uint32_t) * nw,
+                                     cudaMemcpyHostToDevice, m->stream));
+    }
+    CUQ_CUDA_TRY(cudaEventRecord(m->ev0, m->stream));
+    if (n_new == 1) {
+        CUQ_CUDA_TRY(cudaMemcpyAsync(m->forced, ids + n_cached, sizeof(uint32_t), cudaMemcpyHostToDevice,
+                                     m->stream));
+        if ((rc = set_state(m, (int)ids[n_cached], (int)n_cached, 1))) return rc;
+        if ((rc = run_steps(m, 1))) return rc;
+    } else if ((rc = prefill_batched(m, ids + n_cached, n_new, n_cached))) {
+        return rc;
+    }
+    if (draw) {
+        // the first token is drawn from the prompt's last logits, the rest after each step
+        if ((rc = enqueue_sample(m))) return rc;
+        m->stats.kernel_launches += 1;
+        if ((rc = run_steps_sampled(m, n_decode - 1))) return rc;
+    } else if ((rc = run_steps(m, n_decode - 1))) {
+        return rc;
+    }
+    m->stats.prefill_tokens += n_new;
+    m->stats.tokens += n_decode;
+    if ((rc = finish_call(m, n_decode, nullptr, nullptr, &m->stats.decode_ms))) return rc;
+    memcpy(out_tokens, m->out_host, sizeof(uint32_t) * n_decode);
+    return check_gemm_err(m);
+}
+
 int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps, uint32_t *out_tokens) {
     CUQ_CHECK_ARG(m && (out_tokens || n_steps == 0), "cuq_decode_greedy: bad argument");
     if (!m->finalized) {
@@ -1331,6 +1455,9 @@ void cuq_model_free(cuq_model *m) {
     if (m->stream) cudaStreamSynchronize(m->stream);
     if (m->graph_exec) cudaGraphExecDestroy(m->graph_exec);
     if (m->graph) cudaGraphDestroy(m->graph);
+    if (m->graph_exec_smp) cudaGraphExecDestroy(m->graph_exec_smp);
+    if (m->graph_smp) cudaGraphDestroy(m->graph_smp);
+    if (m->smp_host) cudaFreeHost(m->smp_host);
     for (auto &L : m->layers) {
         for (int r = 0; r < 7; r++) free_pending(L.pend[r]);
         for (auto &seg : L.qkv) free_planes(seg.p);
@@ -1353,7 +1480,7 @@ void cuq_model_free(cuq_model *m) {
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
                     m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets,
                     m->pf_x,       m->pf_qkv, m->pf_q, m->pf_g, m->pf_u, m->pf_h, m->pf_l, m->pf_ah, m->pf_al,
-                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch};
+                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch, m->smp};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int r = 0; r < m->tpc.size && m->tp_connected; r++)

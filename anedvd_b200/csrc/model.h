@@ -5,6 +5,7 @@
 
 #include "common.cuh"
 #include "mega.h"
+#include "sample.cuh"
 
 namespace cuq {
 
@@ -89,6 +90,13 @@ struct cuq_model {
     std::vector<cudaEvent_t> prof_ev;
     std::vector<int> prof_tag;
     size_t prof_n = 0;
+
+    // sampled decoding (cuq_generate_sampled): parameters, LCG state and the
+    // penalty window on the device, staged from pinned memory once per call
+    cuq::SampleState *smp = nullptr;             // device
+    cuq::SampleState *smp_host = nullptr;        // pinned
+    cudaGraph_t graph_smp = nullptr;             // decode step + draw
+    cudaGraphExec_t graph_exec_smp = nullptr;
 
     cudaGraph_t graph = nullptr;
     cudaGraphExec_t graph_exec = nullptr;

@@ -196,7 +196,8 @@ def reuse_length(cached, prompt):
 
 
 class Session:
-    """Session.generate (generate.zig:166-250), greedy: the decode loop runs on the device.
+    """Session.generate (generate.zig:166-250): the decode loop runs on the device,
+    greedy by default or with a sampler (cuq_sampler_params, drawn on the device).
 
     Like the reference's session it remembers which token ids the engine's KV
     cache holds, and a prompt that extends them (a multi-turn transcript) only
@@ -212,7 +213,9 @@ class Session:
         self.engine.reset()
         self.cached = []
 
-    def generate(self, ids, n_decode):
+    def generate(self, ids, n_decode, sampler=None, seed=0x12345678, penalty_window=256):
+        """`sampler`: None for greedy decoding, else rt.CuqSamplerParams (the
+        reference's Params.sampler; seed and penalty_window as Params)."""
         ids = np.ascontiguousarray(ids, dtype=np.uint32)
         sent = int(ids.size)
         # generate.zig:171-185: keep the newest tokens of a prompt that does not
@@ -233,7 +236,14 @@ class Session:
                      "prompt_tokens_dropped": sent - int(ids.size), "prefill_reused": int(reuse)}
         out = np.empty(n_decode, dtype=np.uint32)
         L = rt.load()
-        if reuse == 0:
+        if sampler is not None:
+            if n_decode > 0:
+                rt.check(L.cuq_generate_sampled(self.engine._h, _ptr(ids), ids.size, reuse, n_decode,
+                                                ctypes.byref(sampler), seed, penalty_window, _ptr(out)))
+            else:
+                tail = np.ascontiguousarray(ids[reuse:])
+                rt.check(L.cuq_prefill(self.engine._h, _ptr(tail), tail.size, reuse, None, None))
+        elif reuse == 0:
             # prefill from position 0 and decode on the device in one call
             rt.check(L.cuq_generate(self.engine._h, _ptr(ids), ids.size, n_decode, _ptr(out)))
         else:

@@ -1,8 +1,8 @@
 """ctypes binding of libcuq.so, the C ABI in include/cuq.h.
 
-This is the same binding a Zig maintainer writes as `extern fn` declarations
-(INTEGRATION.md); Python uses it for the tests and the benchmark.  Loading
-fails loudly when the library is missing: there is no CPU fallback.
+This is the same binding a Zig maintainer writes as `extern fn`
+declarations; Python uses it for the tests and the benchmark.  Loading fails
+loudly when the library is missing: there is no CPU fallback.
 """
 
 import ctypes
@@ -46,6 +46,7 @@ SIGNATURES = [
     ("cuq_attention_decode_noalloc", I32, [P, P, P, P, U32, U32, U32, U32, U32, P]),
     ("cuq_attention_prefill", I32, [P, P, P, P, U32, U32, U32, U32, U32, U32, P]),
     ("cuq_argmax", I32, [P, U32, P, P]),
+    ("cuq_sample", I32, [P, U32, P, P, U32, P, P, P]),
     ("cuq_model_create", P, [P, P]),
     ("cuq_upload_tensor", I32, [P, I32, I32, I32, P, SZ, U32, U32]),
     ("cuq_upload_f32", I32, [P, I32, I32, P, SZ]),
@@ -84,6 +85,7 @@ SIGNATURES = [
     ("cuq_forward", I32, [P, U32, U32, P, P]),
     ("cuq_prefill", I32, [P, P, U32, U32, P, P]),
     ("cuq_generate", I32, [P, P, U32, U32, P]),
+    ("cuq_generate_sampled", I32, [P, P, U32, U32, U32, P, U32, U32, P]),
     ("cuq_decode_greedy", I32, [P, U32, U32, U32, P]),
     ("cuq_kv_write", I32, [P, U32, U32, U32, P, P]),
     ("cuq_kv_read", I32, [P, U32, U32, U32, P, P]),
@@ -108,6 +110,19 @@ class CuqOptions(ctypes.Structure):
 
 
 DECODE_AUTO, DECODE_PER_OP, DECODE_PERSISTENT = 0, 1, 2
+
+SAMPLE_MAX_VOCAB, SAMPLE_MAX_WINDOW = 327680, 8192
+
+
+class CuqSamplerParams(ctypes.Structure):
+    """cuq_sampler_params = cpu.SamplerParams (cpu.zig:502-518); defaults are the reference's."""
+    _fields_ = [("temperature", F32), ("top_k", U32), ("top_p", F32), ("repetition_penalty", F32),
+                ("presence_penalty", F32), ("frequency_penalty", F32), ("min_keep_delta", F32)]
+
+    def __init__(self, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, presence_penalty=0.0,
+                 frequency_penalty=0.0, min_keep_delta=20.0):
+        super().__init__(temperature, top_k, top_p, repetition_penalty, presence_penalty, frequency_penalty,
+                         min_keep_delta)
 
 
 class CuqStats(ctypes.Structure):

@@ -97,7 +97,7 @@ def seeded_normal(key, n, std=0.02):
 
 
 def tensor_type(cfg, role, layer):
-    """The Q4_K_M mix of BASELINE configs 3/4: Q6_K for attn_v, ffn_down of even
+    """The Q4_K_M mix of the Qwen2.5-1.5B and Llama-3-8B benchmark models: Q6_K for attn_v, ffn_down of even
     layers and the output matrix (token_embd when tied); Q4_K elsewhere."""
     if role in ("attn_norm", "ffn_norm", "final_norm", "q_bias", "k_bias", "v_bias"):
         return F32
@@ -261,7 +261,7 @@ def cached_gguf(m, directory=None):
 
 
 def c1_matrices():
-    """the eight Q8_0 matrices and their fp32 N(0,1) inputs."""
+    """The SmolLM2-135M layer op set: the eight Q8_0 matrices and their fp32 N(0,1) inputs."""
     out = []
     for name, rows, cols in C1_MATRICES:
         w = seeded_normal("c1/" + name, rows * cols)

@@ -89,6 +89,8 @@ def parse():
     ap.add_argument("--persistent-ctas", type=int, default=0, help="CTAs per SM of the persistent kernel (0 = max)")
     ap.add_argument("--profile", choices=["gemv", "qgemm", "prefill", "decode"], default=None,
                     help="run only the roofline kernel (a few launches) for an ncu capture, print nothing")
+    ap.add_argument("--layers", type=int, default=0,
+                    help="--profile prefill/decode: a model of this many layers (same shapes; 0 = the config's)")
     return ap.parse_args()
 
 
@@ -479,7 +481,8 @@ def profile_case(args):
     torch.cuda.set_device(0)
     name = args.config or "c5"
     C = CONFIGS[name]
-    model = synth.model(C["model"], payload=C["payload"], cache=False)
+    extra = {"layers": args.layers} if args.layers else {}
+    model = synth.model(C["model"], payload=C["payload"], cache=False, **extra)
     if args.profile == "gemv":
         s = torch.cuda.Stream()
         ttype, raw, rows, cols = head_shard(model, C, 0, 1)

@@ -163,6 +163,30 @@ int cuq_attention_decode_noalloc(float *out_dev, const float *q_dev, const uint1
 /* cpu.argmax (cpu.zig:477-483): first index of the maximum, written to *out_dev (u32). */
 int cuq_argmax(const float *v_dev, uint32_t n, uint32_t *out_dev, void *stream);
 
+/* cpu.SamplerParams (cpu.zig:502-518), field for field.  The reference's
+ * defaults: temperature 1, top_k 0 (off), top_p 1 (off), repetition_penalty 1,
+ * presence/frequency 0, min_keep_delta 20; Session.generate's default sampler
+ * is temperature 0.7, top_k 40 (generate.zig:36-43). */
+typedef struct {
+    float temperature;         /* <= 0: greedy (after the penalties) */
+    uint32_t top_k;            /* 0: off */
+    float top_p;               /* 1: off; <= 0 is treated as 1 */
+    float repetition_penalty;  /* 1: off; <= 0 is treated as 1 */
+    float presence_penalty;
+    float frequency_penalty;
+    float min_keep_delta;      /* logits below max - delta * temperature are never drawn */
+} cuq_sampler_params;
+#define CUQ_SAMPLE_MAX_VOCAB 327680u  /* logits one draw holds on chip */
+#define CUQ_SAMPLE_MAX_WINDOW 8192u   /* penalty window ids */
+/* cpu.sampleProfiled (cpu.zig:621-721) with cpu.applyPenalties (cpu.zig:529-547)
+ * on the device: logits_dev [vocab] f32 is penalised in place, like the
+ * reference's slice; recent_dev holds the n_recent window ids; rng_dev is the
+ * LCG state (u32, advanced only when a draw happens, as the reference's *rng);
+ * the token goes to *token_dev.  One cluster of 8 CTAs.  params is host
+ * memory, read at the call. */
+int cuq_sample(float *logits_dev, uint32_t vocab, const cuq_sampler_params *params, const uint32_t *recent_dev,
+               uint32_t n_recent, uint32_t *rng_dev, uint32_t *token_dev, void *stream);
+
 /* ------------------------------------------------------------ engine ---- */
 
 /* Model geometry: the fields of model.Config (model.zig:10-244) this path uses. */
@@ -190,7 +214,7 @@ typedef struct {
  * between the phases (single GPU, gate/up of one type, hidden <= 8192;
  * cuq_model_finalize fails when the model does not allow it).  On B200 the
  * per-op path with programmatic dependent launch is the faster of the two for
- * the BASELINE configs, so AUTO picks it. */
+ * benchmark models (SmolLM2-135M to Llama-3-8B), so AUTO picks it. */
 #define CUQ_DECODE_AUTO 0
 #define CUQ_DECODE_PER_OP 1
 #define CUQ_DECODE_PERSISTENT 2
@@ -305,7 +329,7 @@ int cuq_hf_read_config(const char *dir, cuq_config *out);
  * cuq_model_load_gguf). */
 cuq_model *cuq_model_load_hf(const char *dir, const cuq_options *opts);
 
-/* Tensor parallelism (Megatron split of BASELINE config 5; the reference engine
+/* Tensor parallelism (Megatron split, used for the Llama-3-8B shape; the reference engine
  * is single-device, so these have no counterpart there).  One process per GPU,
  * each creating its model with the same config and tp_size and its own tp_rank,
  * uploading the FULL tensors (each rank keeps its shard: q/k/v/gate/up and the
@@ -342,6 +366,21 @@ int cuq_prefill(cuq_model *m, const uint32_t *ids, uint32_t n, uint32_t start_po
  * no host round-trip).  out_tokens (host, n_decode u32) gets the generated ids. */
 int cuq_generate(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_decode,
                  uint32_t *out_tokens);
+/* Session.generate (generate.zig:166-250) with its Params: prefill the prompt
+ * `ids`, then draw `n_decode` tokens with `params`, the LCG seeded with `seed`
+ * (generate.zig:169) and the penalties looking at the last `penalty_window`
+ * ids of prompt and output (generate.zig:205-211, 231-233; at most
+ * CUQ_SAMPLE_MAX_WINDOW).  Positions [0, n_cached) of the KV cache already
+ * hold ids[0..n_cached) (a session's reused prefix, generate.zig:187-192;
+ * 0 = none): only ids[n_cached..n_prompt) are prefilled.  Every draw runs on
+ * the device right after its step's lm_head (cuq_sample's kernel, reading the
+ * parameters, the LCG state and the window from device memory), so the loop
+ * stays on the device.  With temperature <= 0 and no penalty the step's own
+ * argmax is used, as in cuq_generate.  Drawing needs a single GPU
+ * (CUQ_EUNSUPPORTED under tensor parallelism) and vocab <= CUQ_SAMPLE_MAX_VOCAB. */
+int cuq_generate_sampled(cuq_model *m, const uint32_t *ids, uint32_t n_prompt, uint32_t n_cached, uint32_t n_decode,
+                         const cuq_sampler_params *params, uint32_t seed, uint32_t penalty_window,
+                         uint32_t *out_tokens);
 /* Decode `n_steps` greedy tokens from the device-resident state left by a
  * prefill/forward at position `pos` with next token `token` (no prefill). */
 int cuq_decode_greedy(cuq_model *m, uint32_t token, uint32_t pos, uint32_t n_steps,

@@ -776,6 +776,165 @@ uint32_t orc_argmax(const float *v, size_t n) {
     return (uint32_t)best;
 }
 
+/* ------------------------------------------------------------- sampler --- */
+
+/* cpu.zig:529-547: each occurrence in the window (in window order) divides a
+ * positive logit by the repetition penalty or multiplies a non-positive one,
+ * then subtracts the frequency penalty; the presence penalty is subtracted at
+ * a token's first occurrence only. */
+void orc_apply_penalties(float *logits, size_t n, const orc_sampler_params *p, const uint32_t *recent,
+                         size_t n_recent) {
+    if (p->repetition_penalty == 1.0f && p->presence_penalty == 0.0f && p->frequency_penalty == 0.0f) return;
+    const float rep = p->repetition_penalty > 0.0f ? p->repetition_penalty : 1.0f;
+    for (size_t i = 0; i < n_recent; i++) {
+        const uint32_t id = recent[i];
+        if (id >= n) continue;
+        float v = logits[id];
+        if (rep != 1.0f) v = v > 0 ? v / rep : v * rep;
+        if (p->frequency_penalty != 0) v -= p->frequency_penalty;
+        if (p->presence_penalty != 0) {
+            int seen = 0;
+            for (size_t j = 0; j < i; j++)
+                if (recent[j] == id) { seen = 1; break; }
+            if (!seen) v -= p->presence_penalty;
+        }
+        logits[id] = v;
+    }
+}
+
+typedef struct { float logit; uint32_t index; } orc_cand;
+
+/* cpu.zig:573-604 selectTopK: the k largest in items[0..k), descending, by an
+ * insertion scan that moves an item only past strictly smaller ones, so equal
+ * logits keep their scan (index) order. */
+static void select_top_k(orc_cand *items, size_t n, size_t k) {
+    size_t held = 0;
+    for (size_t i = 0; i < n; i++) {
+        const orc_cand c = items[i];
+        if (held < k) {
+            size_t j = held;
+            while (j > 0 && items[j - 1].logit < c.logit) { items[j] = items[j - 1]; j--; }
+            items[j] = c;
+            held++;
+        } else {
+            if (c.logit <= items[k - 1].logit) continue;
+            const orc_cand victim = items[k - 1];
+            size_t j = k - 1;
+            while (j > 0 && items[j - 1].logit < c.logit) { items[j] = items[j - 1]; j--; }
+            items[j] = c;
+            items[i] = victim;
+        }
+    }
+}
+
+/* std.mem.sort is stable: with the candidates in index order, "value
+ * descending, then index ascending" is the same order. */
+static int cand_desc(const void *a, const void *b) {
+    const orc_cand *x = (const orc_cand *)a, *y = (const orc_cand *)b;
+    if (x->logit != y->logit) return x->logit > y->logit ? -1 : 1;
+    return x->index < y->index ? -1 : (x->index > y->index);
+}
+
+uint32_t orc_sample(float *logits, size_t n, const orc_sampler_params *p, const uint32_t *recent, size_t n_recent,
+                    uint32_t *rng, orc_sampler_info *info) {
+    orc_sampler_info tmp;
+    if (!info) info = &tmp;
+    memset(info, 0, sizeof(*info));
+    info->top_p_margin = 1.0f;
+    info->topk_gap = INFINITY;
+    orc_apply_penalties(logits, n, p, recent, n_recent);
+    const float top_p = p->top_p > 0.0f ? (p->top_p < 1.0f ? p->top_p : 1.0f) : 1.0f;
+    float max_v = -INFINITY;
+    for (size_t i = 0; i < n; i++) max_v = logits[i] > max_v ? logits[i] : max_v;  /* @max */
+    info->max_logit = max_v;
+    if (p->temperature <= 0) return orc_argmax(logits, n);
+    const float cut = max_v - p->min_keep_delta * p->temperature;
+    orc_cand *c = (orc_cand *)malloc(sizeof(orc_cand) * (n ? n : 1));
+    size_t nc = 0;
+    for (size_t i = 0; i < n; i++)
+        if (logits[i] >= cut) { c[nc].logit = logits[i]; c[nc].index = (uint32_t)i; nc++; }
+    info->candidates = (uint32_t)nc;
+    uint32_t out;
+    if (nc == 0) {
+        info->path = 1;
+        out = orc_argmax(logits, n);
+        free(c);
+        return out;
+    }
+    size_t keep = nc;
+    const int topk = p->top_k > 0 && p->top_k < nc;
+    if (topk) {
+        select_top_k(c, nc, p->top_k);
+        keep = p->top_k;
+        /* the k-th kept logit against the best one left out (ties resolve by index on both sides) */
+        float next = -INFINITY;
+        for (size_t i = keep; i < nc; i++) next = c[i].logit > next ? c[i].logit : next;
+        info->topk_gap = c[keep - 1].logit - next;
+    }
+    /* probabilities replace the logits in place (cpu.zig:677-681), so the
+     * top-p sort below orders by probability */
+    float sum = 0;
+    for (size_t i = 0; i < keep; i++) {
+        c[i].logit = expf((c[i].logit - max_v) / p->temperature);
+        sum += c[i].logit;
+    }
+    if (sum <= 0) {
+        info->path = 2;
+        out = orc_argmax(logits, n);
+        goto done;
+    }
+    if (top_p < 1.0f) {
+        info->sorted_for_top_p = 1;
+        if (!topk && keep > 1) qsort(c, keep, sizeof(orc_cand), cand_desc);
+        float acc = 0, prev = 0;
+        size_t cut_n = keep;
+        info->top_p_margin = INFINITY;
+        for (size_t i = 0; i < keep; i++) {
+            prev = acc;
+            acc += c[i].logit / sum;
+            if (acc >= top_p) {
+                cut_n = i + 1;
+                float a = acc - top_p, b = top_p - prev;
+                info->top_p_margin = a < b ? a : b;
+                break;
+            }
+        }
+        keep = cut_n;
+        sum = 0;
+        for (size_t i = 0; i < keep; i++) sum += c[i].logit;
+        if (sum <= 0) {
+            info->path = 2;
+            out = orc_argmax(logits, n);
+            goto done;
+        }
+    }
+    info->kept = (uint32_t)keep;
+    info->sum = sum;
+    *rng = *rng * 1664525u + 1013904223u;
+    {
+        const float r = (float)(*rng >> 8) / 16777216.0f;
+        float target = r * sum;
+        info->target = target;
+        info->path = 3;
+        out = c[0].index;
+        double cum = 0;
+        for (size_t i = 0; i < keep; i++) {
+            const double lo = cum;
+            cum += c[i].logit;
+            target -= c[i].logit;
+            if (target <= 0) {
+                out = c[i].index;
+                const double a = (double)info->target - lo, b = cum - (double)info->target;
+                info->draw_margin = (float)((a < b ? a : b) / sum);
+                break;
+            }
+        }
+    }
+done:
+    free(c);
+    return out;
+}
+
 /* --------------------------------------------------------------- model --- */
 
 typedef struct {

@@ -72,6 +72,43 @@ void orc_attention_decode(float *out, const float *q, const uint16_t *k_cache,
                           uint32_t kv_heads, uint32_t hd);
 uint32_t orc_argmax(const float *v, size_t n);                                       /* cpu.zig:477-483 */
 
+/* cpu.SamplerParams (cpu.zig:502-518), field for field. */
+typedef struct {
+    float temperature;          /* <= 0: greedy */
+    uint32_t top_k;             /* 0: off */
+    float top_p;                /* 1: off; <= 0 treated as 1 */
+    float repetition_penalty;   /* 1: off; <= 0 treated as 1 */
+    float presence_penalty;
+    float frequency_penalty;
+    float min_keep_delta;       /* logits below max - delta * temperature are dropped */
+} orc_sampler_params;
+
+/* What one draw did: cpu.SamplerInfo (cpu.zig:491-500) plus the distances the
+ * parity tests use to tell a genuine mismatch from one forced by rounding. */
+typedef struct {
+    uint32_t candidates;        /* entries >= the min_keep_delta cut */
+    uint32_t kept;              /* entries drawn from */
+    int32_t sorted_for_top_p;
+    int32_t path;               /* 0 greedy, 1 no candidates, 2 sum <= 0, 3 drawn */
+    float max_logit;            /* after the penalties */
+    float sum;                  /* probability mass of the kept set */
+    float target;               /* r * sum before the walk */
+    float draw_margin;          /* distance of target from the nearest cumulative edge, / sum */
+    float top_p_margin;         /* distance of the nucleus cut from top_p (1 when top_p is off) */
+    float topk_gap;             /* logit of the k-th kept minus the next one (inf when top-k is off) */
+} orc_sampler_info;
+
+/* cpu.applyPenalties (cpu.zig:529-547), in place. */
+void orc_apply_penalties(float *logits, size_t n, const orc_sampler_params *p, const uint32_t *recent,
+                         size_t n_recent);
+/* cpu.sampleProfiled (cpu.zig:621-721): penalties (in place), greedy for a
+ * non-positive temperature, the min_keep_delta cut, top-k by selectTopK
+ * (cpu.zig:573-604), probabilities by exp, top-p over the descending order
+ * (stable sort), then the LCG draw (rng = rng * 1664525 + 1013904223).
+ * info may be NULL. */
+uint32_t orc_sample(float *logits, size_t n, const orc_sampler_params *p, const uint32_t *recent, size_t n_recent,
+                    uint32_t *rng, orc_sampler_info *info);
+
 /* ------------------------------------------------------------ model ----- */
 
 typedef struct {

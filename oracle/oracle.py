@@ -39,6 +39,25 @@ class OrcConfig(ctypes.Structure):
     ]
 
 
+class SamplerParams(ctypes.Structure):
+    """cpu.SamplerParams (cpu.zig:502-518); the defaults are the reference's."""
+    _fields_ = [("temperature", ctypes.c_float), ("top_k", ctypes.c_uint32), ("top_p", ctypes.c_float),
+                ("repetition_penalty", ctypes.c_float), ("presence_penalty", ctypes.c_float),
+                ("frequency_penalty", ctypes.c_float), ("min_keep_delta", ctypes.c_float)]
+
+    def __init__(self, temperature=1.0, top_k=0, top_p=1.0, repetition_penalty=1.0, presence_penalty=0.0,
+                 frequency_penalty=0.0, min_keep_delta=20.0):
+        super().__init__(temperature, top_k, top_p, repetition_penalty, presence_penalty, frequency_penalty,
+                         min_keep_delta)
+
+
+class SamplerInfo(ctypes.Structure):
+    _fields_ = [("candidates", ctypes.c_uint32), ("kept", ctypes.c_uint32), ("sorted_for_top_p", ctypes.c_int32),
+                ("path", ctypes.c_int32), ("max_logit", ctypes.c_float), ("sum", ctypes.c_float),
+                ("target", ctypes.c_float), ("draw_margin", ctypes.c_float), ("top_p_margin", ctypes.c_float),
+                ("topk_gap", ctypes.c_float)]
+
+
 _lib = None
 
 
@@ -69,6 +88,10 @@ def lib():
                                            ctypes.c_uint32]
         L.orc_argmax.argtypes = [P, ctypes.c_size_t]
         L.orc_argmax.restype = ctypes.c_uint32
+        L.orc_apply_penalties.argtypes = [P, ctypes.c_size_t, ctypes.POINTER(SamplerParams), P, ctypes.c_size_t]
+        L.orc_sample.argtypes = [P, ctypes.c_size_t, ctypes.POINTER(SamplerParams), P, ctypes.c_size_t,
+                                 ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(SamplerInfo)]
+        L.orc_sample.restype = ctypes.c_uint32
         L.orc_model_create.argtypes = [ctypes.POINTER(OrcConfig)]
         L.orc_model_create.restype = P
         L.orc_model_free.argtypes = [P]
@@ -199,6 +222,26 @@ def attention_prefill(q, k_cache16, v_cache16, n_past, q_pos0, heads, kv_heads, 
 def argmax(v):
     v = np.ascontiguousarray(v, dtype=np.float32)
     return int(lib().orc_argmax(_ptr(v), v.size))
+
+
+def apply_penalties(logits, params, recent):
+    """cpu.applyPenalties on a copy of `logits`."""
+    v = np.array(logits, dtype=np.float32, copy=True)
+    r = np.ascontiguousarray(recent, dtype=np.uint32)
+    lib().orc_apply_penalties(_ptr(v), v.size, ctypes.byref(params), _ptr(r) if r.size else None, r.size)
+    return v
+
+
+def sample(logits, params, recent, rng):
+    """cpu.sampleProfiled on a copy of `logits`: (token, rng after, SamplerInfo,
+    the penalised logits)."""
+    v = np.array(logits, dtype=np.float32, copy=True)
+    r = np.ascontiguousarray(recent, dtype=np.uint32)
+    st = ctypes.c_uint32(rng)
+    info = SamplerInfo()
+    tok = lib().orc_sample(_ptr(v), v.size, ctypes.byref(params), _ptr(r) if r.size else None, r.size,
+                           ctypes.byref(st), ctypes.byref(info))
+    return int(tok), int(st.value), info, v
 
 
 class Model:

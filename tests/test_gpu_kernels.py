@@ -1,6 +1,6 @@
 """Per-kernel parity on the GPU: each CUDA entry point against the CPU oracle.
 
-Bars (BASELINE north star): dequantised weights bit-exact in fp32; per-kernel
+Bars: dequantised weights bit-exact in fp32; per-kernel
 outputs within 1e-3 relative error, rel = max|a-b| / max|b| as in the
 reference's compareLogits (main.zig:1920-1930).
 """
@@ -129,7 +129,7 @@ def test_gemv_partial_last_iteration(ttype):
 
 
 def test_gemv_c1_op_set():
-    """the eight Q8_0 matrices of a SmolLM2-135M layer + lm_head."""
+    """The Q8_0 op set of one SmolLM2-135M layer: its eight matrices + the lm_head."""
     for name, rows, cols, raw, x in synth.c1_matrices():
         got = Weight(8, raw, rows, cols).gemv(x)
         e = rel_err(got, _ref_gemv(8, raw, rows, cols, x))

@@ -1,7 +1,7 @@
 """Whole-model parity on the GPU: the device-resident engine against the CPU
 oracle's refForward (teacher-forced, every position compared).
 
-Bars (BASELINE north star): logits within 2e-3 relative error
+Bars: logits within 2e-3 relative error
 (rel = max|a-b| / max|b|, main.zig:1920-1930); greedy tokens identical wherever
 the oracle's top-2 margin exceeds that tolerance.
 """
@@ -96,12 +96,12 @@ def test_persistent_generate_equals_single_steps(name, kw):
 
 
 def test_smollm2_full_size_matches_reference():
-    """BASELINE config 2 at full size (30 layers, vocab 49152), 16-token prompt."""
+    """SmolLM2-135M Q8_0 at full size (30 layers, vocab 49152), 16-token prompt."""
     e = _compare(synth.model("smollm2-135m"), n_prompt=16, n_decode=8)
     assert e < LOGIT_TOL, e
 
 
-# BASELINE configs 3-5 at their full depth and vocabulary (config 5 with 8 of
+# Qwen2.5-0.5B Q8_0, Qwen2.5-1.5B and Llama-3-8B Q4_K_M at their full depth and vocabulary (Llama with 8 of
 # its 32 layers, to keep the CPU oracle within a few GB of host memory).  The
 # weights are "tiled" payloads: every block a real quantised block, the same
 # bytes for the GPU and the oracle.

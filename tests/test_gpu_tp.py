@@ -1,4 +1,4 @@
-"""Tensor parallelism on 2 GPUs (BASELINE config 5's split) against the CPU
+"""Tensor parallelism on 2 GPUs (the Llama-3-8B Megatron split) against the CPU
 oracle: one spawned process per GPU, each with its shard of the same synthetic
 model; the ranks exchange IPC handles over a `gloo` group and the partial sums
 inside the CUDA step kernels.  Rank 0 gathers the logit slices and checks them

@@ -1,5 +1,5 @@
 """Tensor-parallel host logic on CPU (no GPU): the raw-tensor shard helpers of
-the C ABI, and the Megatron split arithmetic of BASELINE config 5 checked with
+the C ABI, and the Megatron split arithmetic of the Llama-3-8B shape checked with
 two `gloo` ranks against the oracle's full-matrix results.
 
 Column-parallel (q/k/v/gate/up/lm_head rows) must reassemble bit-exactly;
