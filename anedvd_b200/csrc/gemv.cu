@@ -226,7 +226,7 @@ int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
         set_error("gemv: split-K needs a workspace");
         return CUQ_EINVAL;
     }
-    if (!a.pre_w && gemv_tma_supported(w.type)) return launch_gemv_tma(a, epi, s);
+    if ((!a.pre_w || a.ss_in) && gemv_tma_supported(w.type)) return launch_gemv_tma(a, epi, s);
     switch (w.type) {
     case CUQ_Q8_0: return launch_t<TQ8_0>(a, epi, s);
     case CUQ_Q4_0: return launch_t<TQ4L<CUQ_Q4_0>>(a, epi, s);

@@ -489,6 +489,8 @@ struct KArgs {
     const float *pre_x, *pre_w;  // GemvArgs::pre_* (pre_w null: input is xq)
     uint32_t pre_n;
     float pre_eps;
+    const float *ss_in;          // GemvArgs::ss_in / ss_out
+    float *ss_out;
     GemvPost post;
 };
 
@@ -513,6 +515,8 @@ inline KArgs make_kargs(const GemvArgs &a) {
     k.pre_w = a.pre_w;
     k.pre_n = a.pre_n;
     k.pre_eps = a.pre_eps;
+    k.ss_in = a.ss_in;
+    k.ss_out = a.ss_out;
     k.post = a.post;
     return k;
 }
@@ -561,9 +565,11 @@ __device__ __forceinline__ void cta_sync() {
         asm volatile("bar.sync 1, %0;" ::"n"(N) : "memory");
 }
 
+// nparts: CTAs contributing partial sums to this tile (0: p.ksplit); by is this
+// CTA's slot among them.
 template <class TT, int EPI, int KW, int NW = 4, int SYNC_N = 0>
 __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_t by, GemvShared &sh, float (&c)[4],
-                                            float k0, float k1) {
+                                            float k0, float k1, int nparts = 0) {
     // NW warps per CTA: TPC tiles of KW warps each, or (gate|up) one tile whose
     // first NW/2 warps hold the gate rows and the others the up rows
     constexpr bool DUAL = (EPI == EPI_SILU_XQ);
@@ -600,7 +606,8 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         for (int w = 0; w < KWE; w++) v += red[w0 + w][vi & 15];
     }
     const uint32_t rows = p.w.rows;
-    if (p.ksplit > 1) {
+    const int np = nparts > 0 ? nparts : p.ksplit;
+    if (np > 1) {
         // split-K: publish the partials, the last CTA of this column of the grid
         // (atomic ticket per tile group) reduces them in a fixed order.
         if (own) p.ws[((size_t)by * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row] = v;
@@ -608,14 +615,14 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         cta_sync<SYNC_N>();
         if (t == 0) {
             unsigned int prev = atomicAdd(&p.counters[bx], 1u);
-            is_last = (prev == (unsigned)p.ksplit - 1u);
+            is_last = (prev == (unsigned)np - 1u);
         }
         cta_sync<SYNC_N>();
         if (!is_last) return false;
         __threadfence();
         if (own) {
             float acc = 0.f;
-            for (int ky = 0; ky < p.ksplit; ky++)
+            for (int ky = 0; ky < np; ky++)
                 acc += __ldcg(&p.ws[((size_t)ky * (DUAL ? 2 : 1) + (vi >> 4)) * rows + row]);
             v = acc;
         }
@@ -659,8 +666,17 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
                 p.y[row] = v;
             } else if (EPI == EPI_ADD) {
                 if (p.bias) v = v + p.bias[row];
-                p.y[row] = p.y[row] + v;
+                v = p.y[row] + v;
+                p.y[row] = v;
             }
+        }
+        if (EPI == EPI_ADD && p.ss_out && t < TPC * 16) {
+            // the tile's sum of squares of the updated rows (16 lanes, fixed order)
+            float q = own ? v * v : 0.f;
+            const unsigned mask = 0xFFFFu << (t & 16);
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) q += __shfl_xor_sync(mask, q, o);
+            if (own && (t & 15) == 0) p.ss_out[bx * TPC + tl] = q;
         }
         if (EPI == EPI_ARGMAX) {
             // first index of the maximum (cpu.zig:477-483) as a packed 64-bit max

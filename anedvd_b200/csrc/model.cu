@@ -156,6 +156,7 @@ static int enqueue_step(cuq_model *m) {
         a.y = y;
         a.bias = bias;
         a.ws = m->ws;
+        a.ws_floats = m->ws_floats;
         a.counters = m->counters;
         a.ksplit = gemv_pick_ksplit(w, m->sm_count);
         a.pdl = pdl;
@@ -166,20 +167,23 @@ static int enqueue_step(cuq_model *m) {
     // Single GPU with register-prefetch GEMVs: each RMSNorm is computed by every
     // CTA of the GEMV that reads it (pre-norm), after its first weight loads are
     // in flight, instead of by the last CTA of the GEMV that wrote the residual.
-    // TMA-fed GEMVs request all their weights at launch, before the activation
-    // exists, so the norm is computed once instead ...
     const bool pre = m->opt.tp_size == 1 && c.hidden % 16 == 0 && c.hidden <= RN_MAX && !m->all_tma;
-    // ... and is launched as a one-CTA kernel of its own between the residual
-    // GEMV and its consumer: a programmatic dependent launch, so the consumer's
-    // CTAs start streaming their weights while the norm runs.
-    const bool sep_norm = m->opt.tp_size == 1 && m->all_tma;
-    auto prenorm = [&](GemvArgs &a, const float *w) {
-        if (!pre) return;
+    // TMA-fed GEMVs request all their weights at launch, before the activation
+    // exists.  There the GEMV that updates the residual (o, down) also writes the
+    // sum of squares of each 16-row tile it produced, and every CTA of the
+    // consumer normalises only its own K range with the mean square summed from
+    // those partials: no norm kernel, no serial tail.  ss[0]: after o, ss[1]:
+    // after down.
+    const bool tnorm = m->opt.tp_size == 1 && m->all_tma;
+    auto prenorm = [&](GemvArgs &a, const float *w, const float *ss) {
+        if (!pre && !(tnorm && ss)) return;
         a.pre_x = m->x;
         a.pre_w = w;
         a.pre_n = c.hidden;
         a.pre_eps = c.eps;
+        if (tnorm) a.ss_in = ss;
     };
+    float *const ss_o = m->ss, *const ss_down = m->ss + c.hidden / 16;
     // engine.zig:561-564 embedding (then layer 0's attention RMSNorm)
     m->prof_node = CUQ_NODE_EMBED;
     if (pre)
@@ -192,7 +196,7 @@ static int enqueue_step(cuq_model *m) {
         m->prof_node = CUQ_NODE_QKV;
         for (auto &seg : L.qkv) {
             GemvArgs a = gemv(seg.p, m->xq_h, m->qkv + seg.row_off, L.qkv_bias ? L.qkv_bias + seg.row_off : nullptr);
-            prenorm(a, L.attn_norm);
+            prenorm(a, L.attn_norm, l > 0 ? ss_down : nullptr);  // layer 0: the embedding kernel's xq
             TRY(launch_gemv(a, EPI_STORE, s));
         }
         // RoPE + fp16 KV write + attention (main.zig:457-472), this rank's heads
@@ -206,13 +210,9 @@ static int enqueue_step(cuq_model *m) {
             GemvArgs a = gemv(L.o.p, m->xq_attn, nullptr, nullptr);
             int epi;
             residual_out(m, a, epi, L.o_bias, L.ffn_norm, 0);
-            if (pre || sep_norm) a.post.op = POST_NONE;
+            if (pre || tnorm) a.post.op = POST_NONE;
+            if (tnorm) a.ss_out = ss_o;  // for the ffn RMSNorm (main.zig:487) in gate|up
             TRY(launch_gemv(a, epi, s));
-            // the ffn RMSNorm (main.zig:487) as a kernel of its own
-            if (sep_norm) {
-                m->prof_node = CUQ_NODE_NORM;
-                TRY(launch_rmsnorm_xq_pdl(m->x, L.ffn_norm, c.hidden, c.eps, m->xq_h, s));
-            }
         }
         // gate/up with the SiLU*mul epilogue (engine.zig:645-668 split path)
         m->prof_node = CUQ_NODE_GATE_UP;
@@ -221,14 +221,14 @@ static int enqueue_step(cuq_model *m) {
             a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count, 2);
             a.w2 = &L.up.p;
             a.xq_out = m->xq_act;
-            prenorm(a, L.ffn_norm);
+            prenorm(a, L.ffn_norm, ss_o);
             TRY(launch_gemv(a, EPI_SILU_XQ, s));
         } else {
             GemvArgs a = gemv(L.gate.p, m->xq_h, m->gate_buf, nullptr);
-            prenorm(a, L.ffn_norm);
+            prenorm(a, L.ffn_norm, ss_o);
             TRY(launch_gemv(a, EPI_STORE, s));
             a = gemv(L.up.p, m->xq_h, m->up_buf, nullptr);
-            prenorm(a, L.ffn_norm);
+            prenorm(a, L.ffn_norm, ss_o);
             TRY(launch_gemv(a, EPI_STORE, s));
             TRY(launch_silu_mul(m->act, m->gate_buf, m->up_buf, lc.inter, s));
             TRY(launch_to_xq(m->act, lc.inter, 1, lc.inter, m->xq_act, s));
@@ -241,12 +241,9 @@ static int enqueue_step(cuq_model *m) {
             int epi;
             const float *next_norm = l + 1 < c.layers ? m->layers[l + 1].attn_norm : m->final_norm;
             residual_out(m, a, epi, nullptr, next_norm, 1);
-            if (pre || sep_norm) a.post.op = POST_NONE;
+            if (pre || tnorm) a.post.op = POST_NONE;
+            if (tnorm) a.ss_out = ss_down;  // for the next attention RMSNorm or the final norm
             TRY(launch_gemv(a, epi, s));
-            if (sep_norm) {
-                m->prof_node = CUQ_NODE_NORM;
-                TRY(launch_rmsnorm_xq_pdl(m->x, next_norm, c.hidden, c.eps, m->xq_h, s));
-            }
         }
     }
     // lm_head with the fused argmax (main.zig:534, cpu.zig:477-483); the last CTA
@@ -254,8 +251,15 @@ static int enqueue_step(cuq_model *m) {
     // the cross-rank argmax under tensor parallelism.
     m->prof_node = CUQ_NODE_HEAD;
     {
+        // the final RMSNorm (main.zig:532): the lm_head's many waves of CTAs
+        // would each repeat a per-CTA norm, so it runs once, as its own kernel
+        if (tnorm) {
+            m->prof_node = CUQ_NODE_NORM;
+            TRY(launch_rmsnorm_xq_pdl(m->x, m->final_norm, c.hidden, c.eps, m->xq_h, s));
+            m->prof_node = CUQ_NODE_HEAD;
+        }
         GemvArgs a = gemv(head_proj(m).p, m->xq_h, m->logits, nullptr);
-        prenorm(a, m->final_norm);
+        prenorm(a, m->final_norm, nullptr);
         a.argmax64 = &m->state->argmax64;
         a.row_base = m->vocab_base;
         a.post.op = m->opt.tp_size > 1 ? POST_TP_FINISH : POST_FINISH;
@@ -613,6 +617,8 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
         build_rope_table(cs.data(), o.max_seq, c.head_dim, c.rope_theta);
         if (cudaMalloc(&m->rope_cs, sizeof(float) * cs.size()) != cudaSuccess) break;
         if (cudaMemcpy(m->rope_cs, cs.data(), sizeof(float) * cs.size(), cudaMemcpyHostToDevice) != cudaSuccess) break;
+        if (cudaMalloc(&m->ss, sizeof(float) * 2 * (c.hidden / 16)) != cudaSuccess) break;
+        cudaMemset(m->ss, 0, sizeof(float) * 2 * (c.hidden / 16));
         if (cudaMalloc(&m->done, sizeof(unsigned int)) != cudaSuccess) break;
         if (cudaMalloc(&m->tickets, sizeof(unsigned int) * lc.kv_heads) != cudaSuccess) break;
         cudaMemset(m->done, 0, sizeof(unsigned int));
@@ -931,6 +937,7 @@ int cuq_model_finalize(cuq_model *m) {
             size_t need = (size_t)k * p.rows * (dual ? 2 : 1);
             if (need > ws_need) ws_need = need;
         }
+        ws_need = std::max(ws_need, gemv_stream_ws_floats(p, dual ? 2 : 1, m->sm_count));
         if (p.rows / 16 > ctr_need) ctr_need = p.rows / 16;
     };
     for (uint32_t l = 0; l < c.layers; l++) {
@@ -1480,7 +1487,7 @@ void cuq_model_free(cuq_model *m) {
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
                     m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets,
                     m->pf_x,       m->pf_qkv, m->pf_q, m->pf_g, m->pf_u, m->pf_h, m->pf_l, m->pf_ah, m->pf_al,
-                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch, m->smp};
+                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch, m->smp, m->ss};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int r = 0; r < m->tpc.size && m->tp_connected; r++)

@@ -56,6 +56,7 @@ struct cuq_model {
     float *ws = nullptr;                         // split-K partials
     unsigned int *counters = nullptr;
     unsigned int *done = nullptr;                // GEMV grid-completion counter (post-ops)
+    float *ss = nullptr;                         // [2][hidden/16] per-tile sums of squares of the residual
     unsigned int *tickets = nullptr;             // attention combine tickets, one per KV head
     size_t ws_floats = 0, n_counters = 0;
     int attn_nsplit = 1;
