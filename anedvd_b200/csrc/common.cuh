@@ -204,6 +204,7 @@ struct TpComm {
     size_t off_am = 0;            // byte offset of the argmax keys
     size_t off_ctr = 0;           // byte offset of the counters
     int *err = nullptr;           // this rank's error flag: set when a wait gives up
+    unsigned long long wait_ns = 10000000000ull;  // a wait for the peers gives up after this long
 };
 
 // Work the CTA that completes a GEMV's last tile does after the whole output is
@@ -267,6 +268,7 @@ struct GemvArgs {
     // (the residual) into ss_out[tile], for the next GEMV's ss_in.
     float *ss_out = nullptr;
     size_t ws_floats = 0;         // capacity of ws (0: sized for ksplit partials only)
+    bool tma = true;              // the TMA-fed kernels may run it (else the register-prefetch kernel)
     int *err = nullptr;           // set to 1 when a bounded wait of the TMA GEMV gave up (may be null)
     GemvPost post;
 };
@@ -326,7 +328,8 @@ __device__ __forceinline__ void rmsnorm_xq_block(const float *x, const float *w,
 int launch_gemv(const GemvArgs &a, int epilogue, cudaStream_t s);
 // K parts (CTAs along K) of a GEMV of this weight; nmat 2 for a gate|up pair.
 // Callers size the split-K workspace with the same value they launch with.
-int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat = 1);
+// tma: the caller lets the TMA-fed kernels run this weight (GemvArgs::tma).
+int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat = 1, bool tma = true);
 // The TMA-fed GEMV (gemv_tma.cu): the types it covers, its K split, and its
 // launcher (CUQ_EUNSUPPORTED for a type or form it does not cover; then the
 // register-prefetch kernel runs).

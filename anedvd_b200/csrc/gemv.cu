@@ -195,8 +195,8 @@ GemvPlan gemv_pick_plan(const Planes &w, int sm_count) {
     return pl;
 }
 
-int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat) {
-    if (gemv_tma_supported(w.type)) return gemv_tma_ksplit(w, nmat, sm_count);
+int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat, bool tma) {
+    if (tma && gemv_tma_supported(w.type)) return gemv_tma_ksplit(w, nmat, sm_count);
     return gemv_pick_plan(w, sm_count).ksplit;
 }
 
@@ -226,7 +226,7 @@ int launch_gemv(const GemvArgs &a, int epi, cudaStream_t s) {
         set_error("gemv: split-K needs a workspace");
         return CUQ_EINVAL;
     }
-    if ((!a.pre_w || a.ss_in) && gemv_tma_supported(w.type)) return launch_gemv_tma(a, epi, s);
+    if (a.tma && (!a.pre_w || a.ss_in) && gemv_tma_supported(w.type)) return launch_gemv_tma(a, epi, s);
     switch (w.type) {
     case CUQ_Q8_0: return launch_t<TQ8_0>(a, epi, s);
     case CUQ_Q4_0: return launch_t<TQ4L<CUQ_Q4_0>>(a, epi, s);

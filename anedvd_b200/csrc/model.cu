@@ -158,7 +158,8 @@ static int enqueue_step(cuq_model *m) {
         a.ws = m->ws;
         a.ws_floats = m->ws_floats;
         a.counters = m->counters;
-        a.ksplit = gemv_pick_ksplit(w, m->sm_count);
+        a.tma = m->use_tma;
+        a.ksplit = gemv_pick_ksplit(w, m->sm_count, 1, m->use_tma);
         a.pdl = pdl;
         a.err = m->gemm_err;
         a.post.done = m->done;
@@ -218,7 +219,7 @@ static int enqueue_step(cuq_model *m) {
         m->prof_node = CUQ_NODE_GATE_UP;
         if (L.gate_up_dual) {
             GemvArgs a = gemv(L.gate.p, m->xq_h, nullptr, nullptr);
-            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count, 2);
+            a.ksplit = gemv_pick_ksplit(L.gate.p, m->sm_count, 2, m->use_tma);
             a.w2 = &L.up.p;
             a.xq_out = m->xq_act;
             prenorm(a, L.ffn_norm, ss_o);
@@ -366,7 +367,8 @@ static int enqueue_head(cuq_model *m, const float *x_row, bool pdl) {
     a.row_base = m->vocab_base;
     a.ws = m->ws;
     a.counters = m->counters;
-    a.ksplit = gemv_pick_ksplit(head.p, m->sm_count);
+    a.tma = m->use_tma;
+    a.ksplit = gemv_pick_ksplit(head.p, m->sm_count, 1, m->use_tma);
     a.pdl = pdl;
     a.err = m->gemm_err;
     a.post.done = m->done;
@@ -668,6 +670,7 @@ cuq_model *cuq_model_create(const cuq_config *cfg, const cuq_options *opts) {
             cudaMemset(m->tp_err, 0, sizeof(int));
             cudaMemset(m->tp_done, 0, sizeof(unsigned int));
             t.err = m->tp_err;
+            if (o.wait_limit_ms) t.wait_ns = (unsigned long long)o.wait_limit_ms * 1000000ull;
             t.peer[t.rank] = m->tp_buf;
         }
         if (cudaMalloc(&m->smp, sizeof(SampleState)) != cudaSuccess) break;
@@ -930,14 +933,26 @@ int cuq_model_finalize(cuq_model *m) {
         set_error("MissingTensor: output_norm.weight");
         return CUQ_EINVAL;
     }
+    {
+        // Decode GEMV kernel.  The TMA-fed kernels (a CTA requests a whole tile's
+        // weights at once) pay off when a rank streams gigabytes per token; on
+        // smaller models the register-prefetch kernel is faster (measured on
+        // B200: SmolLM2-135M 1393 against 1111 tok/s, Qwen2.5-1.5B 551 against
+        // 485, Llama-3-8B 234 against 265).
+        size_t wb = 0;
+        for (auto &L : m->layers)
+            for (int r = 0; r < 7; r++) wb += L.pend[r].nbytes;
+        wb += c.tie_embeddings ? m->pend_embed.nbytes : m->pend_output.nbytes;
+        m->use_tma = wb >= (size_t(2) << 30);  // this rank's bytes (uploads keep only the shard)
+    }
     size_t ws_need = 0, ctr_need = 0;
-    auto account = [&](const Planes &p, int dual) {
-        int k = gemv_pick_ksplit(p, m->sm_count, dual ? 2 : 1);
+    auto account = [&](const Planes &p, int dual, bool tma) {
+        int k = gemv_pick_ksplit(p, m->sm_count, dual ? 2 : 1, tma);
         if (k > 1) {
             size_t need = (size_t)k * p.rows * (dual ? 2 : 1);
             if (need > ws_need) ws_need = need;
         }
-        ws_need = std::max(ws_need, gemv_stream_ws_floats(p, dual ? 2 : 1, m->sm_count));
+        if (tma) ws_need = std::max(ws_need, gemv_stream_ws_floats(p, dual ? 2 : 1, m->sm_count));
         if (p.rows / 16 > ctr_need) ctr_need = p.rows / 16;
     };
     for (uint32_t l = 0; l < c.layers; l++) {
@@ -977,17 +992,17 @@ int cuq_model_finalize(cuq_model *m) {
         for (size_t gi = 0; gi < groups.size(); gi++) {
             if ((rc = build_proj(L.qkv[gi], groups[gi], s))) return rc;
             L.qkv[gi].row_off = offs[gi];
-            account(L.qkv[gi].p, 0);
+            account(L.qkv[gi].p, 0, m->use_tma);
         }
         if ((rc = build_proj(L.o, {&L.pend[R_O]}, s))) return rc;
         if ((rc = build_proj(L.gate, {&L.pend[R_GATE]}, s))) return rc;
         if ((rc = build_proj(L.up, {&L.pend[R_UP]}, s))) return rc;
         if ((rc = build_proj(L.down, {&L.pend[R_DOWN]}, s))) return rc;
         L.gate_up_dual = L.gate.p.type == L.up.p.type;
-        account(L.o.p, 0);
-        account(L.gate.p, L.gate_up_dual);
-        account(L.up.p, 0);
-        account(L.down.p, 0);
+        account(L.o.p, 0, m->use_tma);
+        account(L.gate.p, L.gate_up_dual, m->use_tma);
+        account(L.up.p, 0, m->use_tma);
+        account(L.down.p, 0, m->use_tma);
         for (int r = 0; r < 7; r++) free_pending(L.pend[r]);
     }
     if (c.tie_embeddings && m->opt.tp_size > 1) {
@@ -1006,10 +1021,10 @@ int cuq_model_finalize(cuq_model *m) {
         if ((rc = build_proj(m->output, {&m->pend_output}, s))) return rc;
         free_pending(m->pend_output);
     }
-    account(head_proj(m).p, 0);
+    account(head_proj(m).p, 0, m->use_tma);
     {
         // every decode GEMV on the TMA-fed kernel: the norms stay post-ops
-        bool all = gemv_tma_supported(head_proj(m).p.type);
+        bool all = m->use_tma && gemv_tma_supported(head_proj(m).p.type);
         for (auto &L : m->layers) {
             for (auto &sg : L.qkv) all = all && gemv_tma_supported(sg.p.type);
             all = all && gemv_tma_supported(L.o.p.type) && gemv_tma_supported(L.gate.p.type) &&
@@ -1088,11 +1103,23 @@ int cuq_tp_connect(cuq_model *m, const void *handles) {
         if (r == m->tpc.rank) continue;
         cudaIpcMemHandle_t h;
         memcpy(&h, hb + (size_t)r * CUQ_TP_HANDLE_BYTES, sizeof(h));
+        bool absent = true;
+        for (int i = 0; i < CUQ_TP_HANDLE_BYTES; i++) absent = absent && hb[(size_t)r * CUQ_TP_HANDLE_BYTES + i] == 0;
+        if (absent) {
+            // a rank that never joins: what this rank sends it lands in a local
+            // sink, and every wait for its arrivals runs out (CUQ_ETIMEOUT)
+            if (!m->tp_sink) {
+                CUQ_CUDA_TRY(cudaMalloc(&m->tp_sink, m->tp_bytes));
+                CUQ_CUDA_TRY(cudaMemset(m->tp_sink, 0, m->tp_bytes));
+            }
+            m->tpc.peer[r] = m->tp_sink;
+            continue;
+        }
         void *p = nullptr;
         cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
         if (e != cudaSuccess) {
             for (int q = 0; q < r; q++)
-                if (q != m->tpc.rank && m->tpc.peer[q]) {
+                if (q != m->tpc.rank && m->tpc.peer[q] && m->tpc.peer[q] != m->tp_sink) {
                     cudaIpcCloseMemHandle(m->tpc.peer[q]);
                     m->tpc.peer[q] = nullptr;
                 }
@@ -1383,6 +1410,14 @@ int cuq_reset(cuq_model *m) {
         CUQ_CUDA_TRY(cudaMemsetAsync(L.k_cache, 0, kv_bytes, m->stream));
         CUQ_CUDA_TRY(cudaMemsetAsync(L.v_cache, 0, kv_bytes, m->stream));
     }
+    if (m->tp_buf) {
+        // after a call that gave up on a peer: this rank's arrival counters and
+        // error flag start from zero again (every rank resets before the next call)
+        CUQ_CUDA_TRY(cudaMemsetAsync(m->tp_buf + m->tpc.off_ctr, 0, m->tp_bytes - m->tpc.off_ctr, m->stream));
+        CUQ_CUDA_TRY(cudaMemsetAsync(m->tp_err, 0, sizeof(int), m->stream));
+        CUQ_CUDA_TRY(cudaMemsetAsync(m->counters, 0, sizeof(unsigned) * m->n_counters, m->stream));
+        CUQ_CUDA_TRY(cudaMemsetAsync(m->done, 0, sizeof(unsigned), m->stream));
+    }
     CUQ_CUDA_TRY(cudaStreamSynchronize(m->stream));
     return CUQ_OK;
 }
@@ -1487,11 +1522,11 @@ void cuq_model_free(cuq_model *m) {
                     m->gate_buf,   m->up_buf, m->xq_h, m->xq_attn, m->xq_act,     m->rope_cs,   m->ws,
                     m->counters,   m->state,  m->forced, m->out_tokens, m->done, m->tickets,
                     m->pf_x,       m->pf_qkv, m->pf_q, m->pf_g, m->pf_u, m->pf_h, m->pf_l, m->pf_ah, m->pf_al,
-                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch, m->smp, m->ss};
+                    m->pf_ids,     m->gemm_err, m->tp_err, m->tp_done, m->pf_part, m->pf_wscratch, m->smp, m->ss, m->tp_sink};
     for (void *b : bufs)
         if (b) cudaFree(b);
     for (int r = 0; r < m->tpc.size && m->tp_connected; r++)
-        if (r != m->tpc.rank && m->tpc.peer[r]) cudaIpcCloseMemHandle(m->tpc.peer[r]);
+        if (r != m->tpc.rank && m->tpc.peer[r] && m->tpc.peer[r] != m->tp_sink) cudaIpcCloseMemHandle(m->tpc.peer[r]);
     if (m->tp_buf) cudaFree(m->tp_buf);
     if (m->state_host) cudaFreeHost(m->state_host);
     if (m->out_host) cudaFreeHost(m->out_host);

@@ -40,6 +40,7 @@ struct cuq_model {
     uint32_t vocab_base = 0;     // first lm_head row (global token id) held by this rank
     cuq_options opt{};
     bool finalized = false;
+    bool use_tma = false;        // the decode GEMVs may run the TMA-fed kernels (large models)
     bool all_tma = false;        // every decode GEMV runs the TMA-fed kernel
     int sm_count = 148;
     cudaStream_t stream = nullptr;
@@ -74,6 +75,7 @@ struct cuq_model {
 
     // tensor parallelism (opt.tp_size > 1)
     uint8_t *tp_buf = nullptr;                   // this rank's communication buffer (IPC-exported)
+    uint8_t *tp_sink = nullptr;                  // stands in for the buffer of a rank that never joins
     size_t tp_bytes = 0;
     cuq::TpComm tpc;                             // peers mapped by cuq_tp_connect
     bool tp_connected = false;

@@ -49,13 +49,14 @@ __device__ __forceinline__ void tp_signal(const TpComm &t, int c) {
 }
 
 // One thread: wait until this rank's counter c reaches `expected`; false (and
-// the error flag set) if it does not within TP_TIMEOUT_NS.
+// the error flag set) if it does not within t.wait_ns (TP_TIMEOUT_NS unless the
+// model's options set a limit).
 __device__ __forceinline__ bool tp_wait(const TpComm &t, int c, unsigned int expected) {
     const unsigned int *ctr = tp_ctr(t, t.rank, c);
     if (ld_acquire_sys(ctr) >= expected) return true;
     const unsigned long long t0 = globaltimer_ns();
     while (ld_acquire_sys(ctr) < expected) {
-        if (globaltimer_ns() - t0 > TP_TIMEOUT_NS) {
+        if (globaltimer_ns() - t0 > t.wait_ns) {
             atomicExch(t.err, 1);
             return false;
         }

@@ -61,7 +61,7 @@ class Engine:
 
     @classmethod
     def from_synth(cls, model, max_seq=None, use_graphs=True, device=0, max_chunk=512, tp_rank=0, tp_size=1,
-                   exchange=None, decode_kernel=rt.DECODE_AUTO, persistent_ctas=0):
+                   exchange=None, decode_kernel=rt.DECODE_AUTO, persistent_ctas=0, wait_limit_ms=0):
         """Upload an anedvd_b200.synth.SynthModel tensor by tensor (raw GGUF payloads).
 
         Tensor parallel (tp_size > 1, one process per GPU): every rank uploads
@@ -76,7 +76,7 @@ class Engine:
                            rope_adjacent=int(c.rope_adjacent), tie_embeddings=int(c.tie_embeddings))
         opts = rt.CuqOptions(max_seq=max_seq or c.max_seq, max_chunk=max_chunk, use_graphs=int(use_graphs),
                              tp_rank=tp_rank, tp_size=tp_size, decode_kernel=decode_kernel,
-                             persistent_ctas=persistent_ctas)
+                             persistent_ctas=persistent_ctas, wait_limit_ms=wait_limit_ms)
         h = L.cuq_model_create(ctypes.byref(cfg), ctypes.byref(opts))
         if not h:
             raise rt.CuqError(rt.EINVAL, rt.last_error())

@@ -106,7 +106,7 @@ class CuqConfig(ctypes.Structure):
 class CuqOptions(ctypes.Structure):
     _fields_ = [("max_seq", U32), ("max_chunk", U32), ("use_graphs", ctypes.c_int32),
                 ("tp_rank", ctypes.c_int32), ("tp_size", ctypes.c_int32),
-                ("decode_kernel", ctypes.c_int32), ("persistent_ctas", ctypes.c_int32)]
+                ("decode_kernel", ctypes.c_int32), ("persistent_ctas", ctypes.c_int32), ("wait_limit_ms", U32)]
 
 
 DECODE_AUTO, DECODE_PER_OP, DECODE_PERSISTENT = 0, 1, 2

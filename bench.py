@@ -322,6 +322,50 @@ NODE_KERNEL = {"embed": "embed_norm_kernel", "qkv": "gemv_tma_kernel, q||k||v (+
                "norm": "rmsnorm_xq_kernel"}
 
 
+def tp_check(world, rank, local, exchange):
+    """Correctness of the tensor-parallel path on this launch, outside the timed
+    region: a 2-layer Llama-3-8B-shaped model (full width, vocab 4096) runs a
+    12-token prompt and 4 decode steps across the ranks; rank 0 gathers the
+    logit slices and compares them with the same model on one GPU, whose path
+    the GPU test suite checks against the CPU oracle.  Returns the largest
+    relative logits difference (max|a-b|/max|b|) and whether every greedy token
+    agrees (rank 0; None elsewhere)."""
+    import torch.distributed as dist
+    from anedvd_b200 import engine as E
+    from anedvd_b200 import synth
+    m = synth.model("llama3-8b", layers=2, vocab=4096, payload="tiled", cache=False)
+    ids = prompt_ids(m.cfg.vocab, 12, seed=3)
+    n_dec = 4
+    eng = E.Engine.from_synth(m, max_seq=32, device=local, max_chunk=64, tp_rank=rank, tp_size=world,
+                              exchange=exchange)
+    got = []
+    barrier(world)
+    lg, am = eng.prefill(ids, 0)
+    got.append((lg, am))
+    for s in range(n_dec):
+        lg, am = eng.forward(got[-1][1], ids.size + s)
+        got.append((lg, am))
+    eng.close()
+    parts = [None] * world
+    dist.all_gather_object(parts, got)
+    res = None
+    if rank == 0:
+        one = E.Engine.from_synth(m, max_seq=32, device=local, max_chunk=64)
+        rel, same = 0.0, True
+        want, wam = one.prefill(ids, 0)
+        for s in range(n_dec + 1):
+            if s:
+                want, wam = one.forward(got[s - 1][1], ids.size + s - 1)
+            full = np.concatenate([parts[r][s][0] for r in range(world)])
+            rel = max(rel, float(np.max(np.abs(full - want)) / np.max(np.abs(want))))
+            same = same and all(parts[r][s][1] == wam for r in range(world))
+        one.close()
+        res = {"model": "llama3-8b shape, 2 layers, vocab 4096", "prompt": int(ids.size), "decode_steps": n_dec,
+               "reference": "the same model on one GPU", "max_rel_logits_diff": rel, "greedy_tokens_equal": same}
+    barrier(world)
+    return res
+
+
 def run_ours(args, world, rank, local):
     import torch
     from anedvd_b200 import engine as E
@@ -441,6 +485,7 @@ def run_ours(args, world, rank, local):
                "sample": ref.sample_desc(n_tok, "bounded sample")}
         del ref
     wbytes = model.weight_bytes_per_token()
+    tpc = tp_check(world, rank, local, exchange) if tp else None
     if rank == 0:
         line = {
             "metric": "decode_tok_per_s", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -460,6 +505,7 @@ def run_ours(args, world, rank, local):
             "kernels": kernels, "step_hbm": step_hbm,
             "roofline": roof, "peak_kind": pk_kind, "cpu_baseline": cpu,
             "gpu_launches": int(launches),
+            "tp_check": tpc,
             "kernels_per_token": (1.0 / n_decode) if persistent else int(kps),
             "clocks": clk,
         }

@@ -206,6 +206,8 @@ typedef struct {
                               * process per GPU; see cuq_tp_connect) */
     int32_t decode_kernel;   /* CUQ_DECODE_*: how decode steps run (default AUTO) */
     int32_t persistent_ctas; /* CTAs per SM of the persistent decode kernel; 0 = as many as fit */
+    uint32_t wait_limit_ms;  /* tensor parallel: a wait for the peers gives up after this long
+                              * (CUQ_ETIMEOUT); 0 = 10 s */
 } cuq_options;
 
 /* decode_kernel: PER_OP (and AUTO, the default) runs one kernel per op,
@@ -339,10 +341,14 @@ cuq_model *cuq_model_load_hf(const char *dir, const cuq_options *opts);
  * all ranks' handles, in rank order, to cuq_tp_connect.  The ranks then exchange
  * partial sums over NVLink inside the step's kernels (no library collective);
  * every rank must make the same calls with the same arguments, in the same
- * order.  cuq_forward/cuq_prefill return this rank's slice of the logits
+ * order.  A handle of CUQ_TP_HANDLE_BYTES zero bytes stands for a rank that
+ * never joins (fault tests on one GPU): every exchange then waits for it until
+ * options.wait_limit_ms and the call returns CUQ_ETIMEOUT.  cuq_reset clears
+ * this rank's arrival counters, so that after a time-out every rank can reset
+ * and carry on.  cuq_forward/cuq_prefill return this rank's slice of the logits
  * (vocab / tp_size values starting at token id tp_rank * vocab / tp_size); the
  * argmax and generated tokens are global.  A peer that does not arrive within
- * 10 s ends the call with CUQ_ETIMEOUT. */
+ * options.wait_limit_ms (10 s by default) ends the call with CUQ_ETIMEOUT. */
 #define CUQ_TP_HANDLE_BYTES 64
 int cuq_tp_comm_handle(cuq_model *m, void *handle_out);
 int cuq_tp_connect(cuq_model *m, const void *handles);
