@@ -267,7 +267,6 @@ struct GemvArgs {
     // EPI_ADD: the sum of squares of each 16-row tile of the updated output
     // (the residual) into ss_out[tile], for the next GEMV's ss_in.
     float *ss_out = nullptr;
-    size_t ws_floats = 0;         // capacity of ws (0: sized for ksplit partials only)
     bool tma = true;              // the TMA-fed kernels may run it (else the register-prefetch kernel)
     int *err = nullptr;           // set to 1 when a bounded wait of the TMA GEMV gave up (may be null)
     GemvPost post;
@@ -335,9 +334,6 @@ int gemv_pick_ksplit(const Planes &w, int sm_count, int nmat = 1, bool tma = tru
 // register-prefetch kernel runs).
 bool gemv_tma_supported(int type);
 int gemv_tma_ksplit(const Planes &w, int nmat, int sm_count);
-// Split-K workspace (floats) the stream-K form of the TMA GEMV needs for this
-// weight (nmat 2: a gate|up pair); 0 when it does not run that form.
-size_t gemv_stream_ws_floats(const Planes &w, int nmat, int sm_count);
 int launch_gemv_tma(const GemvArgs &a, int epilogue, cudaStream_t s);
 struct GemvPlan {
     int kw = 4;      // warps per 16-row tile

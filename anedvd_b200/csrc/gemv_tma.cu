@@ -35,8 +35,6 @@
 
 namespace cuq {
 
-int sm_count_current();
-
 namespace {
 
 constexpr int TMA_MAX_STAGES = 24;
@@ -338,251 +336,6 @@ __global__ void __launch_bounds__(32 * TMA_WARPS, 4) gemv_tma_kernel(const __gri
     gemv_post_op(p, tma_dyn);
 }
 
-// ------------------------------------------------------- stream-K kernel ---
-// The same GEMV as one wave of persistent CTAs (STR_CPS per SM).  The work is
-// the list of stages (16-row tile, SIT iterations of K) in tile-major order;
-// CTA c takes the contiguous range [c*S/N, (c+1)*S/N), so every CTA streams
-// the same number of bytes.  A producer warp keeps a ring of stages in flight
-// by TMA (full / empty mbarrier pairs); eight consumer warps decode each stage
-// as it lands and accumulate a tile across its stages in registers.  A tile
-// that lies wholly inside one CTA's range finishes there; one shared by
-// neighbouring CTAs combines their partial sums in a fixed order (the last to
-// arrive, by ticket).  Loads therefore overlap decoding across tiles, which the
-// one-tile-per-CTA kernel can only do across its few resident CTAs.
-constexpr int STR_CW = 8;                      // consumer warps
-constexpr int STR_THREADS = 32 * (STR_CW + 1);  // + one producer warp
-constexpr int STR_CPS = 3;                     // CTAs per SM
-constexpr int STR_MAX_RING = 8;
-
-struct __align__(64) StreamArgs {
-    CUtensorMap map[2][4];
-    KArgs k;
-    int ni;                 // iterations per tile (per matrix)
-    int spt;                // stages per tile
-    int nstage;             // tiles * spt
-    int ring;               // ring slots
-    uint32_t stage_bytes;   // shared memory of one stage (every matrix and box)
-    uint32_t xs_off;        // k.ss_in: the staged input (hi then lo, all of K)
-    int *err;
-};
-
-// owner of stage s when S stages are split into N contiguous ranges
-__host__ __device__ __forceinline__ uint32_t str_owner(uint32_t s, uint32_t S, uint32_t N) {
-    return (uint32_t)((((unsigned long long)s + 1ull) * N + S - 1ull) / S) - 1u;
-}
-
-__device__ __forceinline__ void sbar_init(uint64_t *bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
-}
-__device__ __forceinline__ void sbar_arrive(uint64_t *bar) {
-    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-__device__ __forceinline__ bool sbar_try(uint64_t *bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 10000;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_addr(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-// Bounded wait for phase `parity` of a ring barrier; false (and the abort flag
-// set) after TMA_WAIT_NS, or at once when another warp already gave up.
-__device__ __forceinline__ bool sbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
-    if (sbar_try(bar, parity)) return true;
-    const unsigned long long t0 = globaltimer_ns();
-    while (!sbar_try(bar, parity)) {
-        if (*abort_flag) return false;
-        if (globaltimer_ns() - t0 > TMA_WAIT_NS) {
-            *abort_flag = 1;
-            return false;
-        }
-    }
-    return true;
-}
-// OR of `v` over the consumer warps (named barrier 1): the same answer in every thread
-__device__ __forceinline__ bool consumers_any(bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 p, %1, 0;\n\t"
-        "bar.red.or.pred q, 1, %2, p;\n\t"
-        "selp.u32 %0, 1, 0, q;\n\t}"
-        : "=r"(r)
-        : "r"((uint32_t)v), "n"(32 * STR_CW)
-        : "memory");
-    return r != 0;
-}
-
-template <class TT, int EPI>
-__global__ void __launch_bounds__(STR_THREADS, STR_CPS) gemv_stream_kernel(const __grid_constant__ StreamArgs P) {
-    using G = TmaGeo<TT>;
-    constexpr bool DUAL = (EPI == EPI_SILU_XQ);
-    constexpr int NMAT = DUAL ? 2 : 1;
-    constexpr int NBX = (DUAL || G::ST >= 8) ? 1 : 2;  // geometry boxes per matrix per stage
-    constexpr int SIT = NBX * G::ST;                  // iterations per matrix per stage
-    constexpr int WPM = STR_CW / NMAT;                // consumer warps per matrix
-    constexpr int IPW = SIT / WPM;                    // iterations per warp per stage
-    static_assert(IPW >= 1 && IPW * WPM == SIT, "stage shape");
-    extern __shared__ __align__(1024) uint8_t str_dyn_raw[];
-    uint8_t *str_dyn = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(str_dyn_raw) + 1023) & ~(uintptr_t)1023);
-    __shared__ GemvShared sh;
-    __shared__ __align__(8) uint64_t full[STR_MAX_RING], empty[STR_MAX_RING];
-    __shared__ int abort_flag;
-    __shared__ uint32_t s_issued;  // stages the producer issued (for the drain after a timeout)
-    const KArgs &p = P.k;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int g = lane >> 2, tig = lane & 3;
-    const uint32_t N = gridDim.x, cta = blockIdx.x, S = (uint32_t)P.nstage;
-    const uint32_t s0 = (uint32_t)((unsigned long long)cta * S / N);
-    const uint32_t s1 = (uint32_t)((unsigned long long)(cta + 1) * S / N);
-    const uint32_t R = (uint32_t)P.ring, spt = (uint32_t)P.spt;
-    if (threadIdx.x == 0) {
-        for (uint32_t r = 0; r < R; r++) {
-            sbar_init(&full[r], 1);
-            sbar_init(&empty[r], STR_CW);
-        }
-        abort_flag = 0;
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    }
-    __syncthreads();
-    const uint32_t base = smem_addr(str_dyn);
-    auto issue = [&](uint32_t j) {  // stage s0 + j into its ring slot
-        const uint32_t s = s0 + j, slot = j % R, tile = s / spt, ks = s % spt;
-        tbar_expect_tx(&full[slot], NMAT * NBX * G::TX);
-#pragma unroll
-        for (int m = 0; m < NMAT; m++)
-#pragma unroll
-            for (int b = 0; b < NBX; b++)
-                G::issue(base + slot * P.stage_bytes + (uint32_t)(m * NBX + b) * G::SLICE, P.map[m], tile,
-                         (int)(ks * SIT + b * G::ST), &full[slot]);
-    };
-    // the weights do not depend on the previous kernel: fill the ring now
-    const uint32_t nmine = s1 - s0;
-    uint32_t issued = 0;
-    if (warp == STR_CW && lane == 0)
-        for (; issued < nmine && issued < R; issued++) issue(issued);
-    griddep_wait();
-    griddep_launch();
-
-    // the input from the residual (k.ss_in): all of K, normalised, in shared memory
-    __half *xs = reinterpret_cast<__half *>(str_dyn + P.xs_off);
-    const uint32_t klen = (uint32_t)P.ni * TT::SPAN;
-    if (p.ss_in) {
-        __shared__ float s_inv;
-        if (warp == 0) {
-            float sum = 0.f;
-            for (uint32_t i = lane; i < p.pre_n / 16; i += 32) sum += __ldcg(p.ss_in + i);
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-            if (lane == 0) s_inv = 1.0f / sqrtf(sum / (float)p.pre_n + p.pre_eps);
-        }
-        __syncthreads();
-        const float inv = s_inv;
-        for (uint32_t i = threadIdx.x * 8u; i < klen; i += blockDim.x * 8u) {
-            const bool in = i < p.pre_n;
-            const float4 z = make_float4(0.f, 0.f, 0.f, 0.f);
-            const float4 *xp = reinterpret_cast<const float4 *>(p.pre_x + i);
-            const float4 *wp = reinterpret_cast<const float4 *>(p.pre_w + i);
-            const float4 x0 = in ? __ldcg(xp) : z, x1 = in ? __ldcg(xp + 1) : z;
-            const float4 w0 = in ? __ldg(wp) : z, w1 = in ? __ldg(wp + 1) : z;
-            const float f[8] = {(x0.x * inv) * w0.x, (x0.y * inv) * w0.y, (x0.z * inv) * w0.z, (x0.w * inv) * w0.w,
-                                (x1.x * inv) * w1.x, (x1.y * inv) * w1.y, (x1.z * inv) * w1.z, (x1.w * inv) * w1.w};
-            uint32_t hw[4], lw[4];
-#pragma unroll
-            for (int q = 0; q < 4; q++) {  // fragment order (0, 2, 1, 3) of each group of 4
-                const int a = (q >> 1) * 4 + (q & 1), b = a + 2;
-                const __half ha = __float2half_rn(f[a]), hb = __float2half_rn(f[b]);
-                hw[q] = h2u(__halves2half2(ha, hb));
-                lw[q] = h2u(__halves2half2(__float2half_rn(f[a] - __half2float(ha)),
-                                           __float2half_rn(f[b] - __half2float(hb))));
-            }
-            *reinterpret_cast<uint4 *>(xs + i) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-            *reinterpret_cast<uint4 *>(xs + klen + i) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
-        }
-        __syncthreads();
-    }
-
-    if (warp == STR_CW) {
-        // producer: refill each slot once its consumers have released it
-        if (lane == 0) {
-            for (; issued < nmine; issued++) {
-                if (!sbar_wait(&empty[issued % R], ((issued / R) - 1u) & 1u, &abort_flag) || abort_flag) break;
-                issue(issued);
-            }
-            s_issued = issued;
-        }
-    } else {
-        const int m = DUAL ? warp / WPM : 0, jb = warp % WPM;
-        const __half *xb = p.ss_in ? xs + (g == 1 ? klen : 0u) : p.xq + (g == 1 ? p.kpad : 0);
-        const bool bl = g < 2;
-        float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
-        bool ok = true, dead = false;
-        for (uint32_t j = 0; j < nmine && !dead; j++) {
-            const uint32_t s = s0 + j, slot = j % R, tile = s / spt, ks = s % spt;
-            if (ok && !sbar_wait(&full[slot], (j / R) & 1u, &abort_flag)) ok = false;
-            if (ok) {
-                const uint8_t *st = str_dyn + slot * P.stage_bytes;
-#pragma unroll
-                for (int i = 0; i < IPW; i++) {
-                    const int jj = jb + i * WPM;           // iteration inside the stage
-                    const int it = (int)(ks * SIT) + jj;   // iteration inside the tile
-                    if (it >= P.ni) continue;
-                    const uint8_t *sb = st + (size_t)(m * NBX + jj / G::ST) * G::SLICE;
-                    typename TT::Raw Rw;
-                    G::load(Rw, sb, jj % G::ST, g, tig);
-                    typename TT::Prep Pp;
-                    TT::prep(Rw, tig, Pp);
-#pragma unroll
-                    for (int k = 0; k < TT::KSTEPS; k++) {
-                        uint2 b = make_uint2(0u, 0u);
-                        if (bl) b = *reinterpret_cast<const uint2 *>(xb + TT::koff(it, tig, k));
-                        uint32_t a[4];
-                        TT::frag(Rw, Pp, k, a);
-                        if (k & 1)
-                            mma16816(c2, a[0], a[1], a[2], a[3], b.x, b.y);
-                        else
-                            mma16816(c, a[0], a[1], a[2], a[3], b.x, b.y);
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) sbar_arrive(&empty[slot]);  // the slot may be refilled
-            if (ks == spt - 1u || j == nmine - 1u) {
-                // this CTA's last stage of the tile: every consumer decides alike
-                if (consumers_any(!ok)) {
-                    dead = true;
-                    break;
-                }
-                const uint32_t ca = str_owner(tile * spt, S, N), cb = str_owner(tile * spt + spt - 1u, S, N);
-#pragma unroll
-                for (int i = 0; i < 4; i++) c[i] += c2[i];
-                gemv_finish<TT, EPI, STR_CW, STR_CW, 32 * STR_CW>(p, tile, cta - ca, sh, c, 0.f, 0.f,
-                                                                   (int)(cb - ca + 1u));
-#pragma unroll
-                for (int i = 0; i < 4; i++) c[i] = c2[i] = 0.f;
-            }
-        }
-        if (dead && P.err && threadIdx.x == 0) atomicExch(P.err, 1);
-    }
-    __syncthreads();
-    if (abort_flag && threadIdx.x == 0) {
-        // a wait gave up: let the copies still in flight land (bounded) before
-        // the CTA's shared memory is released
-        const unsigned long long t0 = globaltimer_ns();
-        const uint32_t n_iss = s_issued;
-        for (uint32_t r = 0; r < R && r < n_iss; r++) {
-            const uint32_t jl = n_iss - 1u - r;  // the last R stages issued
-            while (!sbar_try(&full[jl % R], (jl / R) & 1u) && globaltimer_ns() - t0 < TMA_WAIT_NS) {
-            }
-        }
-        if (P.err) atomicExch(P.err, 1);
-    }
-    gemv_post_op(p, str_dyn);
-}
-
 // ----------------------------------------------------------------- host ---
 
 typedef CUresult (*EncodeFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
@@ -693,149 +446,7 @@ cudaError_t launch_epi_tma(int epi, const TmaGemvArgs &args, dim3 grid, size_t s
     return cudaErrorInvalidValue;
 }
 
-// ------------------------------------------------------- stream-K host ---
-
-// Geometry of the stream-K form for a weight: iterations per tile, boxes and
-// iterations per stage, shared memory of a stage.
-struct StreamGeo {
-    int ni, nbx, sit, spt;
-    uint32_t slice, stage_bytes;
-    int span;
-};
-
-StreamGeo stream_geo(const Planes &w, int nmat) {
-    StreamGeo g{};
-    int st;
-    switch (w.type) {
-    case CUQ_Q4_K: st = TmaGeo<TQ4K>::ST; g.slice = TmaGeo<TQ4K>::SLICE; g.span = 256; break;
-    case CUQ_Q6_K: st = TmaGeo<TQ6K>::ST; g.slice = TmaGeo<TQ6K>::SLICE; g.span = 256; break;
-    default: st = TmaGeo<TQ8_0>::ST; g.slice = TmaGeo<TQ8_0>::SLICE; g.span = 64; break;
-    }
-    g.ni = (int)((w.cols + g.span - 1) / g.span);
-    g.nbx = (nmat == 2 || st >= 8) ? 1 : 2;
-    g.sit = g.nbx * st;
-    g.spt = (g.ni + g.sit - 1) / g.sit;
-    g.stage_bytes = (uint32_t)nmat * g.nbx * g.slice;
-    return g;
-}
-
-// The launch of the stream-K form: CTAs, ring slots, dynamic shared memory and
-// the most CTAs that share one tile.  False when the form does not fit.
-bool stream_plan(const Planes &w, int nmat, int sm_count, bool staged_x, uint32_t post_n, int &nctas, int &ring,
-                 size_t &smem, uint32_t &xs_off, int &maxc) {
-    const StreamGeo g = stream_geo(w, nmat);
-    const uint32_t tiles = w.rows / 16;
-    const uint32_t S = tiles * (uint32_t)g.spt;
-    const int sm = sm_count > 0 ? sm_count : 148;
-    nctas = (int)std::min<uint32_t>(S, (uint32_t)(STR_CPS * sm));
-    // per-CTA budget: the SM's shared memory over STR_CPS CTAs, less the static
-    // part and the 1 KB the runtime reserves per CTA
-    const size_t budget = 232448 / STR_CPS - 4096;
-    const size_t xs = staged_x ? 4u * (size_t)g.ni * g.span : 0u;
-    if (budget < 1024 + xs + 2 * (size_t)g.stage_bytes) return false;
-    ring = (int)std::min<size_t>(STR_MAX_RING, (budget - 1024 - xs) / g.stage_bytes);
-    xs_off = (uint32_t)ring * g.stage_bytes;
-    smem = 1024 + (size_t)xs_off + xs;
-    if (smem < 1024 + sizeof(float) * (size_t)post_n) smem = 1024 + sizeof(float) * (size_t)post_n;
-    maxc = 1;
-    for (uint32_t t = 0; t < tiles; t++) {
-        const uint32_t ca = str_owner(t * g.spt, S, nctas), cb = str_owner(t * g.spt + g.spt - 1, S, nctas);
-        maxc = std::max(maxc, (int)(cb - ca + 1));
-    }
-    return true;
-}
-
-// Which GEMVs take the stream-K form.  The decoders are bound by instruction
-// issue, and the per-tile kernel runs all 32 warps an SM's registers allow as
-// decoders, while the stream form spends one warp per CTA on the ring; the
-// stream form only wins when the per-tile grid runs many waves of short CTAs
-// (the lm_heads: 8016-9496 tiles), where it saves the CTAs' fixed costs.
-// CUQ_GEMV_STREAM=0 / 1 forces it off / on for every weight.
-bool stream_wanted(const Planes &w, int sm_count) {
-    static int mode = -2;
-    if (mode == -2) {
-        const char *e = getenv("CUQ_GEMV_STREAM");
-        mode = e ? (atoi(e) != 0 ? 1 : 0) : -1;
-    }
-    if (mode >= 0) return mode == 1;
-    return w.rows / 16 > 16u * (uint32_t)(sm_count > 0 ? sm_count : 148);
-}
-
-template <class TT, int EPI>
-cudaError_t launch_stream_one(const StreamArgs &args, int nctas, size_t smem, bool pdl, cudaStream_t s) {
-    static bool attr_set = false;
-    if (!attr_set) {
-        cudaFuncSetAttribute(gemv_stream_kernel<TT, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             232448 / STR_CPS);
-        attr_set = true;
-    }
-    return launch_maybe_pdl(gemv_stream_kernel<TT, EPI>, dim3(nctas), dim3(STR_THREADS), smem, s, pdl, args);
-}
-
-template <class TT>
-cudaError_t launch_stream_epi(int epi, const StreamArgs &args, int nctas, size_t smem, bool pdl, cudaStream_t s) {
-    switch (epi) {
-    case EPI_STORE: return launch_stream_one<TT, EPI_STORE>(args, nctas, smem, pdl, s);
-    case EPI_ADD: return launch_stream_one<TT, EPI_ADD>(args, nctas, smem, pdl, s);
-    case EPI_SILU_XQ: return launch_stream_one<TT, EPI_SILU_XQ>(args, nctas, smem, pdl, s);
-    case EPI_ARGMAX: return launch_stream_one<TT, EPI_ARGMAX>(args, nctas, smem, pdl, s);
-    case EPI_TP_PUSH: return launch_stream_one<TT, EPI_TP_PUSH>(args, nctas, smem, pdl, s);
-    }
-    return cudaErrorInvalidValue;
-}
-
-// CUQ_EUNSUPPORTED when this weight or call does not take the stream-K form.
-int launch_gemv_stream(const GemvArgs &a, int epi, cudaStream_t s) {
-    const Planes &w = *a.w;
-    const bool dual = epi == EPI_SILU_XQ;
-    const int nmat = dual ? 2 : 1;
-    const bool norm = a.post.op == POST_RMSNORM || a.post.op == POST_TP_REDUCE;
-    const uint32_t post_n = norm && a.post.n % 16 == 0 && a.post.n <= RN_MAX ? a.post.n : 0u;
-    int nctas, ring, maxc;
-    size_t smem;
-    uint32_t xs_off;
-    if (!stream_plan(w, nmat, sm_count_current(), a.ss_in != nullptr, post_n, nctas, ring, smem, xs_off, maxc))
-        return CUQ_EUNSUPPORTED;
-    if (maxc > 1 && (!a.ws || !a.counters || (size_t)maxc * nmat * w.rows > a.ws_floats)) return CUQ_EUNSUPPORTED;
-    const StreamGeo g = stream_geo(w, nmat);
-    StreamArgs args;
-    memset(&args, 0, sizeof(args));
-    int rc = make_maps(w, args.map[0]);
-    if (rc) return rc;
-    if (dual && (rc = make_maps(*a.w2, args.map[1]))) return rc;
-    args.k = make_kargs(a);
-    args.k.ksplit = 1;
-    args.ni = g.ni;
-    args.spt = g.spt;
-    args.nstage = (int)(w.rows / 16) * g.spt;
-    args.ring = ring;
-    args.stage_bytes = g.stage_bytes;
-    args.xs_off = xs_off;
-    args.err = a.err;
-    cudaError_t e;
-    switch (w.type) {
-    case CUQ_Q4_K: e = launch_stream_epi<TQ4K>(epi, args, nctas, smem, a.pdl, s); break;
-    case CUQ_Q6_K: e = launch_stream_epi<TQ6K>(epi, args, nctas, smem, a.pdl, s); break;
-    default: e = launch_stream_epi<TQ8_0>(epi, args, nctas, smem, a.pdl, s); break;
-    }
-    if (e != cudaSuccess) {
-        set_error("gemv (stream-K) launch: %s", cudaGetErrorString(e));
-        return CUQ_ECUDA;
-    }
-    return CUQ_OK;
-}
-
 }  // namespace
-
-size_t gemv_stream_ws_floats(const Planes &w, int nmat, int sm_count) {
-    if (!gemv_tma_supported(w.type) || !stream_wanted(w, sm_count)) return 0;
-    int nctas, ring, maxc;
-    size_t smem;
-    uint32_t xs_off;
-    // the largest form: staged input and a norm post-op
-    if (!stream_plan(w, nmat, sm_count, true, 0, nctas, ring, smem, xs_off, maxc)) return 0;
-    return maxc > 1 ? (size_t)maxc * nmat * w.rows : 0;
-}
 
 // The block types the TMA-fed kernels decode.  CUQ_GEMV_TMA is a bit mask of
 // the types that use them (bit 0 Q4_K, bit 1 Q6_K, bit 2 Q8_0; default all);
@@ -882,10 +493,6 @@ int launch_gemv_tma(const GemvArgs &a, int epi, cudaStream_t s) {
     if (a.ss_in && (!a.pre_x || !a.pre_w || a.pre_n != w.cols || a.pre_n % 16)) {
         set_error("gemv: the input norm needs x and its weight of cols (%u) floats", w.cols);
         return CUQ_EINVAL;
-    }
-    if (stream_wanted(w, sm_count_current())) {
-        const int rc = launch_gemv_stream(a, epi, s);
-        if (rc != CUQ_EUNSUPPORTED) return rc;
     }
     const bool dual = epi == EPI_SILU_XQ;
     TmaGemvArgs args;
