@@ -656,7 +656,9 @@ __device__ __forceinline__ bool gemv_finish(const KArgs &p, uint32_t bx, uint32_
         // this rank's partial of rows [row] into slot [rank] of every rank's buffer
         if (own)
             for (int q = 0; q < p.post.tp.size; q++) tp_slot(p.post.tp, q, p.post.tp_phase, p.post.tp.rank)[row] = v;
-        __threadfence_system();
+        // the barrier orders every thread's stores before thread 0's system fence
+        // in tp_signal (a cumulative release), which publishes them to the peers
+        // before its arrival is counted
         cta_sync<SYNC_N>();
         if (t == 0) tp_signal(p.post.tp, p.post.tp_phase);
     } else {
