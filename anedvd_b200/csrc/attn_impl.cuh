@@ -20,7 +20,7 @@ namespace {
 // Splits cover at least ATT_MIN_CHUNK positions, so a short context uses few
 // splits and the merge reads few partials.
 constexpr uint32_t ATT_MIN_CHUNK = 32;
-constexpr int ATT_MAX_SPLIT = 64;
+constexpr int ATT_MAX_SPLIT = 128;
 // Contexts up to this many positions are walked by one CTA per KV group, which
 // then writes the result directly (no partials, no merge).
 constexpr uint32_t ATT_DIRECT_MAX = 128;
@@ -138,6 +138,10 @@ constexpr int attn_step_floats(int HD, int G) {
                                                            : attn_merge_floats(G) + G * HD;
 }
 
+template <int HD, int G>
+__device__ __forceinline__ void attn_store_cta(float *part, uint32_t split, int nsplit, uint32_t heads, uint32_t kvh,
+                                               float *scr, float *direct);
+
 // Merge the lanes of each warp and the CTA's 4 warps; write the split's partial
 // (o, m, l) for query heads kvh*G .. kvh*G+G-1, or, when `direct` is set (the
 // split is the whole context), the final o / l into direct[0 .. G*HD).
@@ -179,6 +183,18 @@ __device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], f
             for (int e = 0; e < E; e++) sm_o[warp][g][lp * E + e] = o[g][e];
         }
     }
+    attn_store_cta<HD, G>(part, split, nsplit, heads, kvh, scr, direct);
+}
+
+// Combine the 4 warps' (m, l, o) of each head from shared memory (scr: per warp
+// m[G], then l[G], then o[G][HD]) into the split's partial, or, with `direct`,
+// the final result.
+template <int HD, int G>
+__device__ __forceinline__ void attn_store_cta(float *part, uint32_t split, int nsplit, uint32_t heads, uint32_t kvh,
+                                               float *scr, float *direct) {
+    float(*sm_m)[G] = reinterpret_cast<float(*)[G]>(scr);
+    float(*sm_l)[G] = reinterpret_cast<float(*)[G]>(scr + 4 * G);
+    float(*sm_o)[G][HD] = reinterpret_cast<float(*)[G][HD]>(scr + 8 * G);
     __syncthreads();
     float *po = part + ((size_t)split * heads + kvh * G) * HD;
     float *pml = part + (size_t)nsplit * heads * HD + ((size_t)split * heads + kvh * G) * 2;
@@ -204,24 +220,202 @@ __device__ __forceinline__ void attn_store_split(float (&m)[G], float (&l)[G], f
     }
 }
 
+// ------------------------------------------------ tensor-core decode walk ---
+// The online softmax of attn_walk with both contractions on mma.sync m16n8k16
+// (fp16 operands, fp32 accumulation), 16 positions per warp at a time.
+//   Scores: S (16 rows x 8 positions, two tiles) = Q . K^T.  Row g < G holds
+//   query head g's fp32 q rounded to fp16 (hi), row 8 + g the remainder q - hi
+//   (lo), so S[g] + S[8 + g] is the fp32 dot product to about 2^-22 |q||k| (K is
+//   fp16 in the cache; the tensor core multiplies fp16 exactly and adds in fp32).
+//   Output: O (16 rows x HD) += P . V with P split the same way (row g: fp16(p),
+//   row 8 + g: p - fp16(p)); the head's result is O[g] + O[8 + g].
+// A lane loads 16 contiguous bytes of each K row it needs: the dims of one
+// k-step are permuted accordingly (the dot product does not depend on their
+// order), k-step 2b + h taking dims 32b + 8*q4 + 4h + {0,1} (A cols 2*q4 +
+// {0,1}) and + {2,3} (cols 2*q4 + 8 + {0,1}).  For V it loads 16 bytes of four
+// position rows and packs the two positions of each dim with byte_perm; column
+// n of output tile T is dim 64*(T/8) + 8n + T%8.
+__device__ __forceinline__ void attn_mma(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// fp16 hi / lo halves of two floats, packed (first value in the low half)
+__device__ __forceinline__ void attn_split2(float x, float y, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __floats2half2_rn(x, y);
+    const float2 hf = __half22float2(h);
+    const __half2 r = __floats2half2_rn(x - hf.x, y - hf.y);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&r);
+}
+
+__host__ __device__ constexpr int attn_tc_dim(int T, int n) { return 64 * (T / 8) + 8 * n + (T % 8); }
+
+// Walk positions [p0, p1) of one KV head: warp `warp` of the CTA's 4 takes the
+// 16-position tiles p0 + 16*(warp + 4i).  qs: the G rotated query heads (fp32,
+// G * HD in shared memory).  Returns the lane's row max m (shared by the 4
+// lanes of a row), its partial row sum l and the O fragments.
+template <int HD, int G>
+__device__ __forceinline__ void attn_walk_tc(const float *qs, const __half *kh, const __half *vh, uint32_t p0,
+                                             uint32_t p1, int warp, float &m, float &l, float (&o)[HD / 8][4]) {
+    static_assert(HD == 64 || HD == 128, "head_dim 64 or 128");
+    static_assert(G >= 1 && G <= 8, "1 to 8 query heads per KV head");
+    constexpr int NKB = HD / 32, NT = HD / 8, NH = HD / 64;
+    const int lane = threadIdx.x & 31, g4 = lane >> 2, q4 = lane & 3;
+    const float scale = 1.0f / sqrtf((float)HD);
+    uint32_t qa[NKB][2][4];  // A fragments of Q, constant over the walk
+#pragma unroll
+    for (int b = 0; b < NKB; b++) {
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (g4 < G) {
+#pragma unroll
+                for (int e = 0; e < 4; e++) v[e] = qs[g4 * HD + 32 * b + 8 * q4 + 4 * h + e];
+            }
+            attn_split2(v[0], v[1], qa[b][h][0], qa[b][h][1]);
+            attn_split2(v[2], v[3], qa[b][h][2], qa[b][h][3]);
+        }
+    }
+    m = -INFINITY;
+    l = 0.f;
+#pragma unroll
+    for (int t = 0; t < NT; t++) o[t][0] = o[t][1] = o[t][2] = o[t][3] = 0.f;
+    const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+    // K rows t0 + 8j + g4 (dims 32b + 8*q4 ..); V rows t0 + 8*(r/2) + 2*q4 + r%2
+    // (dims 64h + 8*g4 ..).  The next tile's rows are requested before this
+    // tile's math, so a warp keeps one tile in flight while it computes.
+    uint4 kn[2][NKB], vn[4][NH];
+    auto fetch = [&](uint32_t t0) {
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            const uint32_t p = t0 + 8u * j + g4;
+#pragma unroll
+            for (int b = 0; b < NKB; b++)
+                kn[j][b] = p < p1 ? *reinterpret_cast<const uint4 *>(kh + (size_t)p * HD + 32 * b + 8 * q4) : z;
+        }
+#pragma unroll
+        for (int r = 0; r < 4; r++) {
+            const uint32_t p = t0 + 8u * (r >> 1) + 2u * q4 + (r & 1);
+#pragma unroll
+            for (int h = 0; h < NH; h++)
+                vn[r][h] = p < p1 ? *reinterpret_cast<const uint4 *>(vh + (size_t)p * HD + 64 * h + 8 * g4) : z;
+        }
+    };
+    if (p0 + 16u * (uint32_t)warp < p1) fetch(p0 + 16u * (uint32_t)warp);
+    for (uint32_t t0 = p0 + 16u * (uint32_t)warp; t0 < p1; t0 += 64u) {
+        uint4 kx[2][NKB], vx[4][NH];
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int b = 0; b < NKB; b++) kx[j][b] = kn[j][b];
+#pragma unroll
+        for (int r = 0; r < 4; r++)
+#pragma unroll
+            for (int h = 0; h < NH; h++) vx[r][h] = vn[r][h];
+        if (t0 + 64u < p1) fetch(t0 + 64u);
+        float s[2][4];
+#pragma unroll
+        for (int j = 0; j < 2; j++) {
+            s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+            for (int b = 0; b < NKB; b++) {
+                const uint32_t *kw = reinterpret_cast<const uint32_t *>(&kx[j][b]);
+                attn_mma(s[j], qa[b][0], kw[0], kw[1]);
+                attn_mma(s[j], qa[b][1], kw[2], kw[3]);
+            }
+        }
+        // the lane's positions: t0 + 2*q4 + {0,1} (tile 0) and t0 + 8 + 2*q4 + {0,1} (tile 1)
+        float sc[4];
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int e = 0; e < 2; e++)
+                sc[2 * j + e] = t0 + 8u * j + 2u * q4 + e < p1 ? (s[j][e] + s[j][2 + e]) * scale : -INFINITY;
+        float mx = fmaxf(fmaxf(sc[0], sc[1]), fmaxf(sc[2], sc[3]));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float mn = fmaxf(m, mx);  // finite: position t0 is valid
+        const float corr = expf(m - mn);
+        float pr[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) pr[i] = expf(sc[i] - mn);
+        l = l * corr + ((pr[0] + pr[1]) + (pr[2] + pr[3]));
+        m = mn;
+        uint32_t pa[4];
+        attn_split2(pr[0], pr[1], pa[0], pa[1]);
+        attn_split2(pr[2], pr[3], pa[2], pa[3]);
+#pragma unroll
+        for (int t = 0; t < NT; t++) {
+            const int h = t / 8, e = t % 8;
+            const uint32_t sel = (e & 1) ? 0x7632u : 0x5410u;
+            const uint32_t b0 = __byte_perm(reinterpret_cast<const uint32_t *>(&vx[0][h])[e >> 1],
+                                            reinterpret_cast<const uint32_t *>(&vx[1][h])[e >> 1], sel);
+            const uint32_t b1 = __byte_perm(reinterpret_cast<const uint32_t *>(&vx[2][h])[e >> 1],
+                                            reinterpret_cast<const uint32_t *>(&vx[3][h])[e >> 1], sel);
+#pragma unroll
+            for (int i = 0; i < 4; i++) o[t][i] *= corr;
+            attn_mma(o[t], pa, b0, b1);
+        }
+    }
+}
+
+// The walk's state into the shared-memory layout of attn_store_split (per warp
+// m, l and o of each of the G heads), then the CTA's combine.
+template <int HD, int G>
+__device__ __forceinline__ void attn_store_split_tc(float m, float l, const float (&o)[HD / 8][4], int warp,
+                                                    float *part, uint32_t split, int nsplit, uint32_t heads,
+                                                    uint32_t kvh, float *scr, float *direct = nullptr) {
+    const int lane = threadIdx.x & 31, g4 = lane >> 2, q4 = lane & 3;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    float(*sm_m)[G] = reinterpret_cast<float(*)[G]>(scr);
+    float(*sm_l)[G] = reinterpret_cast<float(*)[G]>(scr + 4 * G);
+    float(*sm_o)[G][HD] = reinterpret_cast<float(*)[G][HD]>(scr + 8 * G);
+    if (g4 < G) {
+        if (q4 == 0) {
+            sm_m[warp][g4] = m;
+            sm_l[warp][g4] = l;
+        }
+#pragma unroll
+        for (int t = 0; t < HD / 8; t++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) sm_o[warp][g4][attn_tc_dim(t, 2 * q4 + e)] = o[t][e] + o[t][2 + e];
+    }
+    attn_store_cta<HD, G>(part, split, nsplit, heads, kvh, scr, direct);
+}
+
 // Merge the nact splits of query heads h0 .. h0+NH-1 (one CTA, any size):
 // out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.  Every split's weight is
-// computed once into shared memory, then each thread sums float4 columns with
-// independent loads.  `res` receives the NH*HD results; scr:
-// attn_merge_floats(NH), not overlapping res.
-template <int HD, int NH>
+// computed once into shared memory, then each thread sums float4 columns in
+// split order, MB splits' loads in flight at a time; the first MB of its first
+// column are requested before the weights are computed.  `res` receives the
+// NH*HD results; scr: attn_merge_floats(NH), not overlapping res.
+template <int HD, int NH, int MB = 8>
 __device__ __forceinline__ void attn_merge(const float *part, int nsplit, uint32_t nact, uint32_t heads, uint32_t h0,
                                            float *res, float *scr) {
     float(*cw)[NH] = reinterpret_cast<float(*)[NH]>(scr);
     float *inv_l = scr + ATT_MAX_SPLIT * NH;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const float *pml = part + (size_t)nsplit * heads * HD;
+    const int ncol = NH * HD / 4;
+    const size_t sstride = (size_t)heads * HD / 4;
+    auto column = [&](int t) { return reinterpret_cast<const float4 *>(part + (size_t)(h0 + t / (HD / 4)) * HD) + t % (HD / 4); };
+    float4 v[MB];
+    auto load = [&](const float4 *src, uint32_t s0) {
+#pragma unroll
+        for (int j = 0; j < MB; j++)
+            v[j] = s0 + j < nact ? __ldcg(src + (s0 + j) * sstride) : make_float4(0.f, 0.f, 0.f, 0.f);
+    };
+    if ((int)threadIdx.x < ncol) load(column(threadIdx.x), 0);
     for (int g = warp; g < NH; g += nw) {
         const uint32_t h = h0 + g;
-        float ms[2], ls[2];
+        constexpr int J = ATT_MAX_SPLIT / 32;
+        float ms[J], ls[J];
         float M = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
+        for (int j = 0; j < J; j++) {
             const uint32_t s = lane + 32 * j;
             ms[j] = s < nact ? __ldcg(pml + ((size_t)s * heads + h) * 2) : -INFINITY;
             ls[j] = s < nact ? __ldcg(pml + ((size_t)s * heads + h) * 2 + 1) : 0.f;
@@ -231,7 +425,7 @@ __device__ __forceinline__ void attn_merge(const float *part, int nsplit, uint32
         for (int sh = 16; sh > 0; sh >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, sh));
         float L = 0.f;
 #pragma unroll
-        for (int j = 0; j < 2; j++) {
+        for (int j = 0; j < J; j++) {
             const uint32_t s = lane + 32 * j;
             const float c = ms[j] == -INFINITY ? 0.f : expf(ms[j] - M);
             if (s < nact) cw[s][g] = c;
@@ -242,19 +436,21 @@ __device__ __forceinline__ void attn_merge(const float *part, int nsplit, uint32
         if (lane == 0) inv_l[g] = 1.0f / L;
     }
     __syncthreads();
-    for (int t = threadIdx.x; t < NH * HD / 4; t += blockDim.x) {
-        const int g = t / (HD / 4), d4 = t % (HD / 4);
-        const float4 *src = reinterpret_cast<const float4 *>(part + (size_t)(h0 + g) * HD) + d4;
-        const size_t sstride = (size_t)heads * HD / 4;
+    for (int t = threadIdx.x; t < ncol; t += blockDim.x) {
+        const int g = t / (HD / 4);
+        const float4 *src = column(t);
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-        for (uint32_t s = 0; s < nact; s++) {
-            const float4 v = __ldcg(src + s * sstride);
-            const float c = cw[s][g];
-            acc.x = fmaf(v.x, c, acc.x);
-            acc.y = fmaf(v.y, c, acc.y);
-            acc.z = fmaf(v.z, c, acc.z);
-            acc.w = fmaf(v.w, c, acc.w);
+        for (uint32_t s0 = 0; s0 < nact; s0 += MB) {
+            if (t != (int)threadIdx.x || s0 != 0) load(src, s0);
+#pragma unroll
+            for (int j = 0; j < MB; j++) {
+                if (s0 + j >= nact) break;
+                const float c = cw[s0 + j][g];
+                acc.x = fmaf(v[j].x, c, acc.x);
+                acc.y = fmaf(v[j].y, c, acc.y);
+                acc.z = fmaf(v[j].z, c, acc.z);
+                acc.w = fmaf(v[j].w, c, acc.w);
+            }
         }
         const float il = inv_l[g];
         res[4 * t] = acc.x * il;
@@ -325,8 +521,10 @@ __device__ __forceinline__ float rope_elem(const float *v, uint32_t d, const flo
 }
 
 // KV group kvh, position split `split` of the step at position pos; scr:
-// attn_step_floats(HD, G) floats of shared memory.
-template <int HD, int G>
+// attn_step_floats(HD, G) floats of shared memory.  TC: the tensor-core walk
+// (about 250 registers per thread), else the FMA walk (fits the persistent
+// kernel's 128).
+template <int HD, int G, bool TC = false>
 __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t kvh, uint32_t split, uint32_t pos,
                                                float *scr) {
     constexpr int E = 8, LPP = HD / E;
@@ -350,6 +548,24 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
                 vh[(size_t)pos * HD + d] = __float2half_rn(vin[d]);
             }
         }
+        if constexpr (TC) {
+            // the G rotated query heads in shared memory, after the store scratch
+            // (the direct result later takes the same place, after the store's barrier)
+            float *qs = scr + attn_store_floats(HD, G);
+            for (uint32_t i = threadIdx.x; i < (uint32_t)(G * HD); i += blockDim.x)
+                qs[i] = rope_elem<HD>(p.qkv + (size_t)(kvh * G) * HD + (i / HD) * HD, i % HD, csr, p.adjacent);
+            __syncthreads();  // qs, and the K/V row written above, are read below
+            float m, l, o[HD / 8][4];
+            attn_walk_tc<HD, G>(qs, kh, vh, r.p0, r.p1, warp, m, l, o);
+            if (direct) {
+                float *res = scr + attn_store_floats(HD, G);
+                attn_store_split_tc<HD, G>(m, l, o, warp, p.part, split, p.nsplit, p.heads, kvh, scr, res);
+                __syncthreads();
+                attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
+                return;
+            }
+            attn_store_split_tc<HD, G>(m, l, o, warp, p.part, split, p.nsplit, p.heads, kvh, scr);
+        } else {
         float qr[G][E];
 #pragma unroll
         for (int g = 0; g < G; g++) {
@@ -375,6 +591,7 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
             return;
         }
         attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh, scr);
+        }
     }
     // the last CTA of this KV group (active or not) merges the group's heads
     __shared__ int is_last;
@@ -385,7 +602,7 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
     if (!is_last) return;
     __threadfence();
     float *res = scr + attn_merge_floats(G);
-    attn_merge<HD, G>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res, scr);
+    attn_merge<HD, G, TC ? 24 : 8>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res, scr);
     attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
     if (threadIdx.x == 0) p.tickets[kvh] = 0u;
 }

@@ -146,7 +146,7 @@ __global__ void __launch_bounds__(128) attn_step_kernel(const AttnStepArgs p) {
     griddep_wait();
     griddep_launch();
     __shared__ __align__(16) float scr[attn_step_floats(HD, G)];
-    attn_step_body<HD, G>(p, blockIdx.x, blockIdx.y, (uint32_t)p.state->pos, scr);
+    attn_step_body<HD, G, true>(p, blockIdx.x, blockIdx.y, (uint32_t)p.state->pos, scr);
 }
 
 // ------------------------------------------------------ prefill helpers --
@@ -270,7 +270,10 @@ int launch_rope_cache(const float *qkv, uint32_t qkv_stride, float *q_out, __hal
 }
 
 int attn_pick_nsplit(uint32_t kv_heads, uint32_t max_seq, int sm_count) {
-    int want = (2 * sm_count + (int)kv_heads - 1) / (int)kv_heads;
+    // CTAs per SM the splits aim at (128 threads, 168 registers: at most 3 fit)
+    int per_sm = 2;
+    if (const char *e = getenv("CUQ_ATTN_CTAS_PER_SM")) per_sm = atoi(e) > 0 ? atoi(e) : 2;
+    int want = (per_sm * sm_count + (int)kv_heads - 1) / (int)kv_heads;
     int maxs = (int)((max_seq + ATT_MIN_CHUNK - 1) / ATT_MIN_CHUNK);
     if (want > maxs) want = maxs;
     if (want > ATT_MAX_SPLIT) want = ATT_MAX_SPLIT;
