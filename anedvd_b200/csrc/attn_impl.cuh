@@ -593,16 +593,20 @@ __device__ __forceinline__ void attn_step_body(const AttnStepArgs &p, uint32_t k
         attn_store_split<HD, G>(m, l, o, warp, lp, pg, p.part, split, p.nsplit, p.heads, kvh, scr);
         }
     }
-    // the last CTA of this KV group (active or not) merges the group's heads
+    // the last CTA of this KV group (active or not) merges the group's heads.
+    // The barrier orders every thread's partial stores before thread 0's fence
+    // (cumulative), which publishes them before the ticket counts this CTA.
     __shared__ int is_last;
-    __threadfence();
     __syncthreads();
-    if (threadIdx.x == 0) is_last = atomicAdd(&p.tickets[kvh], 1u) == (unsigned)p.nsplit - 1u;
+    if (threadIdx.x == 0) {
+        __threadfence();
+        is_last = atomicAdd(&p.tickets[kvh], 1u) == (unsigned)p.nsplit - 1u;
+    }
     __syncthreads();
     if (!is_last) return;
     __threadfence();
     float *res = scr + attn_merge_floats(G);
-    attn_merge<HD, G, TC ? 24 : 8>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res, scr);
+    attn_merge<HD, G, TC ? 40 : 8>(p.part, p.nsplit, r.nact, p.heads, kvh * G, res, scr);
     attn_emit(res, G * HD, kvh * G * HD, nullptr, p.xq, xq_pad(qd));
     if (threadIdx.x == 0) p.tickets[kvh] = 0u;
 }

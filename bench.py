@@ -315,11 +315,19 @@ def gemv_roofline(ttype, raw, rows, cols, stream_ptr, pk, label, reps=64):
 
 
 # the kernel behind each node of the per-op decode step
-NODE_KERNEL = {"embed": "embed_norm_kernel", "qkv": "gemv_tma_kernel, q||k||v (+ v when its type differs)",
-               "attention": "attn_step_kernel", "o": "gemv_tma_kernel + residual",
-               "gate_up": "gemv_tma_kernel, gate|up + SiLU*mul",
-               "down": "gemv_tma_kernel + residual", "lm_head": "gemv_tma_kernel + argmax",
+NODE_KERNEL = {"embed": "embed_norm_kernel", "qkv": "%s, q||k||v (+ v when its type differs)",
+               "attention": "attn_step_kernel", "o": "%s + residual",
+               "gate_up": "%s, gate|up + SiLU*mul",
+               "down": "%s + residual", "lm_head": "gemv_kernel + argmax",
                "norm": "rmsnorm_xq_kernel"}
+
+
+def node_kernel(node, weight_bytes):
+    """The kernel behind a decode node: the layer GEMVs are TMA-fed when a rank
+    streams at least 2 GiB of weights per token, else register-prefetch; the
+    lm_head always runs the register-prefetch kernel."""
+    k = NODE_KERNEL.get(node, node)
+    return k % ("gemv_tma_kernel" if weight_bytes >= (2 << 30) else "gemv_kernel") if "%s" in k else k
 
 
 def tp_check(world, rank, local, exchange):
@@ -459,7 +467,8 @@ def run_ours(args, world, rank, local):
         traffic = prof.get("%s %s" % (name, dom), {}).get("dram_bytes_per_launch")
     except (OSError, ValueError):
         pass
-    roof = {"kernel": "%s node of the %s decode step (%s)" % (dom, name, NODE_KERNEL.get(dom, dom)), "bound": "hbm",
+    wlocal = sum(v["bytes"] for k, v in kernels.items() if k != "attention") / n_prof
+    roof = {"kernel": "%s node of the %s decode step (%s)" % (dom, name, node_kernel(dom, wlocal)), "bound": "hbm",
             "achieved": achieved, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": achieved / pk["hbm_gbs"],
             "traffic": traffic, "algorithmic_bytes": per_launch_bytes, "launch_us": dk_["us_per_launch"],
             "timing": "in-step, %d decode steps at positions %d..%d, CUDA events after every launch on the "
@@ -467,7 +476,6 @@ def run_ours(args, world, rank, local):
                                                                                  n_prompt + n_prof - 1),
             "share_of_step": dk_["ms"] / sum(v["ms"] for v in kernels.values())}
     # whole step: this rank's weights once + the K/V rows over the decode window, per token
-    wlocal = sum(v["bytes"] for k, v in kernels.items() if k != "attention") / n_prof
     cfg = model.cfg
     kvd_local = cfg.kv_heads * cfg.head_dim // (world if tp else 1)
     kv_avg = 2 * 2 * kvd_local * cfg.layers * (n_prompt + (n_decode + 1) / 2.0)
