@@ -50,7 +50,8 @@ __global__ void dequant_planes_f16_kernel(PlanesView p, __half *__restrict__ out
 // token_embd of loadRuntime (load_gguf.zig:578-647) read by Engine.forward
 // (engine.zig:561-564).  One CTA.
 __global__ void embed_row_kernel(PlanesView p, const int *__restrict__ token_ptr, float *__restrict__ x, int epb) {
-    embed_row_block(p, (uint32_t)*token_ptr, x, epb);
+    extern __shared__ __align__(16) uint8_t stage[];
+    embed_row_staged(p, (uint32_t)*token_ptr, x, epb, stage);
 }
 
 // Decode-step start: the embedding row of state->token (as embed_row_kernel)
@@ -60,7 +61,8 @@ __global__ void embed_norm_kernel(PlanesView p, const StepState *__restrict__ st
                                   int epb) {
     griddep_wait();
     griddep_launch();
-    embed_row_block(p, (uint32_t)st->token, x, epb);
+    extern __shared__ __align__(16) uint8_t stage[];
+    embed_row_staged(p, (uint32_t)st->token, x, epb, stage);
     __threadfence();
     __syncthreads();
     rmsnorm_xq_block(x, nw, n, eps, xq, xq_pad(n), nullptr);
@@ -171,10 +173,28 @@ int launch_unpack(const Planes &p, uint8_t *raw, cudaStream_t s) {
     return CUQ_OK;
 }
 
+// Shared memory of the single-CTA embedding kernels: the row's raw blocks.
+static int embed_stage_bytes(const Planes &p, size_t &bytes) {
+    bytes = (size_t)(p.cols / block_elems(p.type)) * block_bytes(p.type);
+    if (bytes > 200 * 1024) {
+        set_error("embedding row of %u columns does not fit shared memory", p.cols);
+        return CUQ_EUNSUPPORTED;
+    }
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(embed_norm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(embed_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    return CUQ_OK;
+}
+
 int launch_embed_norm(const Planes &p, const StepState *state, float *x, const float *norm_w, uint32_t n, float eps,
                       __half *xq, bool pdl, cudaStream_t s) {
-    cudaError_t e = launch_maybe_pdl(embed_norm_kernel, dim3(1), dim3(256), 0, s, pdl, view(p), state, x, norm_w, n,
-                                     eps, xq, block_elems(p.type));
+    size_t smem;
+    if (int rc = embed_stage_bytes(p, smem)) return rc;
+    cudaError_t e = launch_maybe_pdl(embed_norm_kernel, dim3(1), dim3(256), smem, s, pdl, view(p), state, x, norm_w,
+                                     n, eps, xq, block_elems(p.type));
     if (e != cudaSuccess) {
         set_error("embed launch: %s", cudaGetErrorString(e));
         return CUQ_ECUDA;
@@ -190,7 +210,9 @@ int launch_embed_rows(const Planes &p, const uint32_t *ids, uint32_t n, float *x
 }
 
 int launch_embed_row(const Planes &p, const int *token_ptr, float *x, cudaStream_t s) {
-    embed_row_kernel<<<1, 256, 0, s>>>(view(p), token_ptr, x, block_elems(p.type));
+    size_t smem;
+    if (int rc = embed_stage_bytes(p, smem)) return rc;
+    embed_row_kernel<<<1, 256, smem, s>>>(view(p), token_ptr, x, block_elems(p.type));
     CUQ_CUDA_TRY(cudaGetLastError());
     return CUQ_OK;
 }

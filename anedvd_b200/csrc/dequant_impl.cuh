@@ -211,6 +211,21 @@ __device__ __forceinline__ void embed_row_block(const PlanesView &p, uint32_t r,
     }
 }
 
+// The same row by one CTA with its raw blocks staged in shared memory (`stage`:
+// cols / epb * block_bytes bytes): one thread rebuilds each block once, then
+// every thread decodes elements out of shared memory.  For the decode step's
+// single-CTA embedding, where one thread per block share would rebuild every
+// block several times in local memory.
+__device__ __forceinline__ void embed_row_staged(const PlanesView &p, uint32_t r, float *x, int epb, uint8_t *stage) {
+    if (r >= p.rows) return;  // r is the same for the whole CTA
+    const int bpb = block_bytes(p.type);
+    const uint32_t nb = p.cols / epb;
+    for (uint32_t b = threadIdx.x; b < nb; b += blockDim.x) block_move(p, stage + (size_t)b * bpb, r, b, 1);
+    __syncthreads();
+    for (uint32_t i = threadIdx.x; i < p.cols; i += blockDim.x)
+        x[i] = __half2float(__float2half_rn(dq_elem(p.type, stage + (size_t)(i / epb) * bpb, (int)(i % epb))));
+}
+
 }  // namespace
 
 }  // namespace cuq
