@@ -134,6 +134,23 @@ __device__ float dq_elem(int type, const uint8_t *blk, int j) {
 
 // Copy one block between its raw form and the planes. dir = 0: raw -> planes.
 __device__ __forceinline__ void mv(uint8_t *planes_p, uint8_t *raw_p, int n, int dir) {
+    if (dir == 1 && (n & 15) == 0 && (reinterpret_cast<uintptr_t>(planes_p) & 15) == 0) {
+        // an aligned plane segment: four 16-byte loads in flight, then the byte stores
+        for (int i = 0; i < n; i += 64) {
+            uint4 v[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                v[k] = i + 16 * k < n ? *reinterpret_cast<const uint4 *>(planes_p + i + 16 * k) : make_uint4(0, 0, 0, 0);
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                if (i + 16 * k >= n) break;
+                const uint32_t w[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+                for (int j = 0; j < 16; j++) raw_p[i + 16 * k + j] = (uint8_t)(w[j >> 2] >> (8 * (j & 3)));
+            }
+        }
+        return;
+    }
     if (dir == 0)
         for (int i = 0; i < n; i++) planes_p[i] = raw_p[i];
     else
